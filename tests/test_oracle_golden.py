@@ -1,0 +1,174 @@
+"""Pin the CPU oracle against golden vectors produced by the reference's own kernels.
+
+The fixtures in tests/golden were produced by ``gen_golden.py`` running the reference
+Triton kernels under TRITON_INTERPRET=1. Selection / packing / decode-cache state must
+match bit for bit; attention outputs within the tolerances below.
+"""
+import numpy as np
+import pytest
+import torch
+
+import _inputs as I
+from oracle import delta_oracle as O
+
+
+def test_interpreter_bf16_arithmetic_is_bitwise(golden):
+    g = golden("bf16_interp_probe")
+    # the interpreter subtracts raw bit patterns: not the bf16 difference
+    assert not np.array_equal(g["interp"], g["true"])
+
+
+@pytest.mark.parametrize("dt_name,dt", [("bf16", torch.bfloat16), ("fp32", torch.float32)])
+def test_rope_matches_reference_eager(golden, dt_name, dt):
+    g = golden(f"rope_{dt_name}")
+    x = torch.from_numpy(I.ar1_keys(1, 2, 300, 128, seed=11, offset=True)).to(dt)
+    assert float(x.double().sum()) == pytest.approx(float(g["in_sum"]), rel=0, abs=1e-6)
+    cos, sin = O.rope_cos_sin(300, 128, 500000.0, dt)
+    np.testing.assert_array_equal(cos.float().numpy(), g["cos"])
+    out = O.apply_rope(x, cos, sin)
+    np.testing.assert_array_equal(out.float().numpy(), g["out"])
+
+
+SEL = [
+    ("keep_euclid_fp32", torch.float32, 1, 2, 1000, 64, 256, False, 1e4, 1),
+    ("keep_euclid_fp16", torch.float16, 1, 2, 1000, 128, 300, False, 5e5, 2),
+    ("keep_cosine_fp32", torch.float32, 1, 2, 1000, 64, 256, True, 1e4, 3),
+    ("keep_cosine_bf16", torch.bfloat16, 1, 2, 1000, 128, 300, True, 5e5, 4),
+    ("keep_cosine_fp16", torch.float16, 1, 2, 700, 96, 512, True, 5e5, 5),
+]
+
+
+@pytest.mark.parametrize("case", SEL, ids=[c[0] for c in SEL])
+def test_delta_keep_mask_bit_exact(golden, case):
+    name, dt, B, H, N, D, chunk, use_cos, theta, seed = case
+    g = golden(name)
+    k = I.post_rope_keys(B, H, N, D, theta, dt, seed=seed)
+    assert float(k.double().sum()) == pytest.approx(float(g["in_sum"]), rel=1e-12)
+    keep, cc = O.delta_keep_mask(k, float(g["threshold"]), use_cos, chunk, -(-N // chunk))
+    np.testing.assert_array_equal(keep.numpy(), g["keep"])
+    np.testing.assert_array_equal(cc.numpy(), g["chunk_counts"])
+    frac = g["keep"].mean()
+    assert 0.2 < frac < 0.9, frac   # the threshold exercises both branches
+
+
+def test_delta_keep_mask_strided_input(golden):
+    g = golden("keep_euclid_fp32_bshd")
+    k = I.post_rope_keys(1, 2, 1000, 64, 1e4, torch.float32, seed=1)
+    kb = k.transpose(1, 2).contiguous().transpose(1, 2)
+    keep, cc = O.delta_keep_mask(kb, float(g["threshold"]), False, 256, 4)
+    np.testing.assert_array_equal(keep.numpy(), g["keep"])
+
+
+def test_pack_bit_exact(golden):
+    g = golden("pack_fp32")
+    k = I.post_rope_keys(1, 2, 1000, 64, 1e4, torch.float32, seed=1)
+    v = torch.from_numpy(I.normal((1, 2, 1000, 64), seed=101)).float()
+    assert float(v.double().sum()) == pytest.approx(float(g["v_sum"]), rel=1e-12)
+    keep = torch.from_numpy(g["keep"])
+    im, kp, vp, ts, counts = O.pack_from_keep(k, v, keep)
+    np.testing.assert_array_equal(im.numpy(), g["index_map"])
+    np.testing.assert_array_equal(kp.numpy(), g["k_packed"])
+    np.testing.assert_array_equal(vp.numpy(), g["v_packed"])
+    np.testing.assert_array_equal(ts.numpy(), g["timestamps"])
+    np.testing.assert_array_equal(counts.numpy(), g["counts"])
+
+
+ATTN = [
+    ("attn_fp32_periodic", torch.float32, 2, 600, 64, "periodic", 21),
+    ("attn_fp32_delta", torch.float32, 2, 600, 64, "delta", 22),
+    ("attn_fp32_w0", torch.float32, 2, 600, 64, "periodic", 23),
+    ("attn_fp16_periodic", torch.float16, 2, 600, 128, "periodic", 24),
+    ("attn_fp16_delta", torch.float16, 2, 520, 128, "delta", 25),
+    ("attn_fp32_quirk", torch.float32, 2, 600, 64, "quirk", 26),
+]
+TOL = {torch.float32: (2e-5, 2e-6), torch.float16: (4e-3, 2e-4)}
+
+
+def attn_case(golden, case):
+    name, dt, H, N, D, packing, seed = case
+    g = golden(name)
+    q, k, v = I.attn_inputs(1, H, N, D, dt, seed)
+    assert float(q.double().sum()) == pytest.approx(float(g["q_sum"]), rel=1e-12)
+    keep = torch.from_numpy(g["keep"])
+    _, kp, vp, ts, counts = O.pack_from_keep(k, v, keep)
+    return g, q, k, v, kp, vp, ts, counts, int(g["W"])
+
+
+@pytest.mark.parametrize("case", ATTN, ids=[c[0] for c in ATTN])
+@pytest.mark.parametrize("variant", ["hybrid", "sanity", "pure_phase1"])
+def test_hybrid_attention_matches_reference(golden, case, variant):
+    g, q, k, v, kp, vp, ts, counts, W = attn_case(golden, case)
+    out = O.hybrid_attention(q, k, v, kp, vp, ts, counts.float(), q.shape[-1] ** -0.5, W, variant)
+    ref = torch.from_numpy(g[variant])
+    err = (out.float() - ref).abs()
+    mx, mean = TOL[q.dtype]
+    assert torch.isfinite(ref).all()
+    assert err.max() <= mx and err.mean() <= mean, (err.max(), err.mean())
+
+
+@pytest.mark.parametrize("case", ATTN[:1] + ATTN[3:4], ids=[ATTN[0][0], ATTN[3][0]])
+@pytest.mark.parametrize("causal", [True, False])
+def test_flash_matches_reference(golden, case, causal):
+    g, q, k, v, *_ = attn_case(golden, case)
+    out = O.flash_attention(q, k, v, causal=causal)
+    ref = torch.from_numpy(g["flash_causal" if causal else "flash_noncausal"])
+    mx, mean = TOL[q.dtype]
+    err = (out.float() - ref).abs()
+    assert err.max() <= mx and err.mean() <= mean, (err.max(), err.mean())
+
+
+def test_delta_padding_block_restarts_dense_window(golden):
+    """Reference quirk: a head with fewer anchors than M sees count-0 padding blocks
+    whose max timestamp is 0, so last_safe drops to 0 and phase 2 restarts at key 0."""
+    g, q, k, v, kp, vp, ts, counts, W = attn_case(golden, ATTN[5])
+    M = kp.shape[2]
+    n_h1 = int(counts[0, 1].gt(0).sum())
+    assert n_h1 + 128 <= M          # head 1 has at least one all-padding block
+    n1, ds, hi = O.hybrid_schedule(ts[0, 1].numpy(), M, 600, 512, W)
+    assert ds == 0 and n1 == 4
+    # head 0 (no padding) resumes dense attention near the diagonal
+    n1, ds, hi = O.hybrid_schedule(ts[0, 0].numpy(), M, 600, 512, W)
+    assert ds > 0
+
+
+@pytest.mark.parametrize("name,dt,use_cos", [("decode_fp32_euclid", torch.float32, False),
+                                             ("decode_fp16_cosine", torch.float16, True)])
+def test_decode_replay_matches_reference(golden, name, dt, use_cos):
+    g = golden(name)
+    st = I.decode_setup(dt, seed=31)
+    B, Hkv, Hq, D, W = st["B"], st["Hkv"], st["Hq"], st["D"], st["W"]
+    thr = float(g["threshold"])
+    kp, vp, cnt, tss, lens = st["kp"], st["vp"], st["counts"], st["ts"], st["lengths"]
+    ke, ve = st["ke"], st["ve"]
+    exact_len, total = st["exact_len"], st["total"]
+    outs = []
+    for step in range(st["steps"]):
+        O.decode_update(st["new_k"][step], st["new_v"][step], ke, ve, kp, vp, cnt, tss, lens,
+                        exact_len, total, thr, W, use_cos)
+        exact_len += 1
+        total += 1
+        np.testing.assert_array_equal(lens.numpy(), g["lengths"][step])
+        o = O.decode_attention(st["q"][step], kp, vp, cnt, lens.view(B, Hkv), ke, ve,
+                               D ** -0.5, min(exact_len, W), Hq // Hkv)
+        outs.append(o.float())
+    np.testing.assert_array_equal(cnt.numpy(), g["counts"])
+    np.testing.assert_array_equal(tss.numpy(), g["timestamps"])
+    np.testing.assert_array_equal(kp.float().numpy(), g["k_packed"])
+    np.testing.assert_array_equal(ke.float().numpy(), g["k_exact"])
+    out = torch.stack(outs)
+    ref = torch.from_numpy(g["outputs"])
+    mx, mean = TOL[dt]
+    err = (out - ref).abs()
+    assert err.max() <= mx and err.mean() <= mean, (err.max(), err.mean())
+    # the replay exercised both merges and appends
+    grew = g["lengths"][-1] - st["lengths"].numpy()
+    assert (grew > 0).any() and (grew < st["steps"]).any()
+
+
+def test_tile_counts_match_survey_table():
+    # tiles per head under the reference schedule, periodic packing, W=128
+    assert O.tile_count(2048, 4) == 84
+    assert O.tile_count(8192, 1) == 2080
+    assert O.tile_count(8192, 4) == 744
+    assert O.tile_count(32768, 4) == 9144
+    assert O.tile_count(32768, 1) == 32896
