@@ -1,0 +1,343 @@
+"""Benchmark: delta-attention prefill tokens/s for BASELINE config 2 (one GPU per rank).
+
+A step is one pass of the hot path over one layer of synthetic input: RoPE on q and k,
+periodic r=4 packing (timestamps / counts; packed K/V are strided views) and the two-phase
+count-weighted tcgen05 attention for B=1, Hq=32, Hkv=8, N=32768, d=128, bf16. Each rank
+processes its own sequence (weak scaling, no collective on the data path). Inputs (q 256
+MiB + k, v 64 MiB each) exceed the 126 MB L2, so no explicit flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line (rank 0). ``--impl reference`` times the CPU restatement of the
+reference's path (the oracle port) on this host's cores on a bounded sample of the same
+workload (the reference's own code is Triton and cannot run on a host without the
+interpreter and its source tree).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "delta-attn prefill tokens/s @N=32k, r=4 (one Llama-3.1-8B attention layer-op)"
+UNIT = "tokens/s"
+CFG = dict(B=1, Hq=32, Hkv=8, N=32768, D=128, r=4, W=128, theta=5e5)
+
+
+def workload_config(n_gpus):
+    return {"workload": "cfg2: RoPE(q,k) + periodic r=4 packing + two-phase delta attention, one layer",
+            "B_per_gpu": CFG["B"], "Hq": CFG["Hq"], "Hkv": CFG["Hkv"], "N": CFG["N"], "d": CFG["D"],
+            "r": CFG["r"], "dense_window": CFG["W"], "global_batch": CFG["B"] * n_gpus,
+            "parallelism": f"dp{n_gpus} (one sequence per GPU, no data-path collective)",
+            "l2": "inputs (384 MiB per step) larger than L2; no flush"}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured"
+    except Exception:
+        return 1590.0, 1400.0, "fallback"
+
+
+def traffic_per_launch():
+    """DRAM bytes per attention launch from the committed ncu summary, if present."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "attn_tc_cfg2_traffic.json")) as f:
+            return json.load(f).get("bytes_per_launch")
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = set(gpus)
+        self.proc = None
+        self.path = os.path.join("/tmp", f"dab_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], [], set()
+        try:
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9 or not f[0].isdigit() or int(f[0]) not in self.gpus:
+                    continue
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+                for name, val in zip(["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"],
+                                     f[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(name)
+        except Exception:
+            pass
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------ CPU side
+def cpu_sample(heads=(0,), N=CFG["N"]):
+    """Oracle (CPU restatement of the reference path) on q-heads `heads` of one cfg2 layer.
+
+    Returns (seconds, tokens-equivalent): the sample's share of one layer's N tokens."""
+    from deltaattention_b200 import synth
+    from oracle import delta_oracle as O
+    q, k, v = synth.layer_inputs(1, CFG["Hq"], CFG["Hkv"], N, CFG["D"], torch.bfloat16, seed=0, device="cpu")
+    cos, sin = synth.rope_tables(N, CFG["D"], CFG["theta"], torch.bfloat16)
+    kv_heads = sorted({h // (CFG["Hq"] // CFG["Hkv"]) for h in heads})
+    t0 = time.perf_counter()
+    q_ref = O.apply_rope(q[:, list(heads)].contiguous(), cos, sin)
+    k_ref = O.apply_rope(k[:, kv_heads].contiguous(), cos, sin)
+    vv = v[:, kv_heads].contiguous()
+    keep = O.periodic_keep_mask(1, len(kv_heads), N, 1.0 / CFG["r"])
+    _, kp, vp, ts, counts = O.pack_from_keep(k_ref, vv, keep)
+    n_rep = len(heads) if len(kv_heads) == 1 else 1
+    O.hybrid_attention(q_ref, k_ref, vv, kp, vp, ts, counts.float(), CFG["D"] ** -0.5, CFG["W"], n_rep=n_rep)
+    dt = time.perf_counter() - t0
+    return dt, N * len(heads) / CFG["Hq"]
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    heads = (0,)
+    for _ in range(args.warmup):
+        cpu_sample(heads)
+    secs, toks = 0.0, 0.0
+    for _ in range(args.steps):
+        dt, tk = cpu_sample(heads)
+        secs += dt
+        toks += tk
+    value = toks / secs
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * secs / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, BASELINE cfg2)",
+            "config": workload_config(world), "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"1 of 32 q-heads (its kv-head's RoPE, packing and attention) of one "
+                                       f"N={CFG['N']} layer per step; tokens scaled by 1/32"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------ GPU side
+def run_ours(args, world, rank, local):
+    from deltaattention_b200 import _lib as L
+    from deltaattention_b200 import ops, synth
+    dev = torch.device("cuda", local)
+    B, Hq, Hkv, N, D, r, W = CFG["B"], CFG["Hq"], CFG["Hkv"], CFG["N"], CFG["D"], CFG["r"], CFG["W"]
+    q, k, v = synth.layer_inputs(B, Hq, Hkv, N, D, torch.bfloat16, seed=1000 + rank, device=dev)
+    cos, sin = synth.rope_tables(N, D, CFG["theta"], torch.bfloat16, device=dev)
+    period = r
+    stream = torch.cuda.current_stream(dev)
+    attn_events = []
+    launches_per_step = 5  # rope(q), rope(k), periodic_meta, schedule, attention
+
+    def step(record=False):
+        q_rot = ops.rope(q, cos, sin)
+        k_rot = ops.rope(k, cos, sin)
+        packed = ops.pack_periodic(k_rot, v, period)
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        o = ops.attention(q_rot, k_rot, v, packed, dense_window=W)
+        if record:
+            e1.record(stream)
+            attn_events.append((e0, e1))
+        return o
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    with ClockSampler(range(world)) as clk:
+        torch.cuda.synchronize()
+        barrier(world)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step(record=True)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        clocks = clk.summary()
+    ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world)
+    attn_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in attn_events) / len(attn_events), world)
+    codes = L.workspace_errors()
+    if any(codes):
+        raise RuntimeError(f"bounded device wait timed out during the bench: {codes}")
+    tokens = B * N * world
+    value = tokens / (ms / 1000.0)
+
+    # dense (r = 1) comparator through the same kernel family: causal flash with GQA by index
+    q_rot, k_rot = ops.rope(q, cos, sin), ops.rope(k, cos, sin)
+    for _ in range(2):
+        ops.flash(q_rot, k_rot, v)
+    torch.cuda.synchronize()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    nd = max(3, args.steps // 4)
+    d0.record(stream)
+    for _ in range(nd):
+        ops.flash(q_rot, k_rot, v)
+    d1.record(stream)
+    torch.cuda.synchronize()
+    dense_ms = max_over_ranks(d0.elapsed_time(d1) / nd, world)
+    del q_rot, k_rot
+
+    # end to end through the public API: pinned host inputs -> device -> host output
+    hq = q.transpose(1, 2).contiguous().cpu().pin_memory()
+    hk = k.transpose(1, 2).contiguous().cpu().pin_memory()
+    hv = v.transpose(1, 2).contiguous().cpu().pin_memory()
+    ho = torch.empty((B, Hq, N, D), dtype=torch.bfloat16).pin_memory()
+    dq, dk, dv = torch.empty_like(hq, device=dev), torch.empty_like(hk, device=dev), torch.empty_like(hv, device=dev)
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        o = ops.delta_prefill(dq.transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2), cos, sin,
+                              keep_rate=1.0 / r, dense_window=W)
+        ho.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    ne = max(3, args.steps // 2)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(ne):
+        e2e_step()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(s0.elapsed_time(s1) / ne, world)
+
+    burst, sustained, src = peaks()
+    tiles = ops.tile_count_periodic(N, r, W)
+    flops = B * Hq * tiles * 4 * 128 * 128 * D
+    achieved = flops / (attn_ms / 1000.0) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded AR(1) keys + offsets, 0.5*N(0,1) q/v: BASELINE cfg2 distributions)",
+        "config": workload_config(world),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": burst, "unit": "TFLOP/s",
+                     "frac": achieved / burst, "traffic": traffic_per_launch(),
+                     "kernel": "attn_tc_kernel<128,bf16>", "attn_ms_per_launch": attn_ms,
+                     "flops_per_launch": flops, "tiles_per_head": tiles,
+                     "peak_kind": f"{src} bf16 burst (sustained {sustained})",
+                     "frac_of_sustained": achieved / sustained},
+        "e2e": {"value": B * N * world / (e2e_ms / 1000.0), "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": (hq.numel() + hk.numel() + hv.numel()) * 2,
+                "d2h_bytes_per_step": ho.numel() * 2},
+        "dense_r1": {"ms_per_step": dense_ms, "speedup_of_delta_attention": dense_ms / attn_ms},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        dt, tk = cpu_sample((0,))
+        line["cpu_baseline"] = {"value": tk / dt, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                                "sample": f"1 of 32 q-heads of one N={N} layer (RoPE, packing, two-phase "
+                                          f"attention), {dt:.1f} s; tokens scaled by 1/32"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup()
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,740 @@
+// tcgen05 / TMEM attention for the reference's prefill kernels on B200 (sm_100a).
+//
+// One kernel serves the four reference kernels (deltaFlashAttention.py:9-357 and
+// flashAttention.py:5-91) for bf16/fp16 inputs with head_dim 64 or 128 and the
+// reference's 128x128 logical blocks. The logical schedule (phase-1 stop rule, dense
+// restart block, causal limit) comes from a small pre-pass (`schedule_kernel`), so the
+// per-(query block, head) tile list is exactly the reference's.
+//
+// Structure (persistent, one CTA per SM, 384 threads):
+//   warp 0      TMA producer: Q tiles, K/V tiles into a ring of shared-memory slots, and
+//               the packed tile's counts (and timestamps) next to its V tile
+//   warp 1      MMA issuer (one thread): S = Q K^T into TMEM, O += P V with P read from TMEM
+//   warp 2      TMEM allocator
+//   warps 4-7   softmax + epilogue for query tile 0 (TMEM lanes 0..127, one row per thread)
+//   warps 8-11  softmax + epilogue for query tile 1
+// A work unit is two 128-row query tiles that share every K/V tile: two q-heads of one
+// GQA group at the same query block (kv_group even) or two consecutive query blocks of
+// one head. Units run heaviest first (latest query blocks first) in a serpentine static
+// order across CTAs. Softmax keeps a stale running max unless it grows by more than 2^8,
+// so the O correction pass is rare; O and l share the same reference so O / l is exact.
+#include <type_traits>
+
+#include "params.cuh"
+
+namespace dab {
+
+enum TcVariant : int { TC_HYBRID = 0, TC_SANITY = 1, TC_PURE = 2, TC_DENSE = 3 };
+
+constexpr int TC_THREADS = 384;
+constexpr int TC_BM = 128;
+constexpr int TC_BN = 128;
+
+template <int D> struct TcCfg {
+  static constexpr int QBYTES = TC_BM * D * 2;
+  static constexpr int KVBYTES = TC_BN * D * 2;
+  static constexpr int NSLOT = (D == 128) ? 4 : 8;
+  static constexpr int OFF_Q0 = 0;
+  static constexpr int OFF_Q1 = QBYTES;
+  static constexpr int OFF_SLOT = 2 * QBYTES;
+  static constexpr int OFF_AUXC = OFF_SLOT + NSLOT * KVBYTES;
+  static constexpr int OFF_AUXT = OFF_AUXC + NSLOT * TC_BN * 4;
+  static constexpr int OFF_BAR = OFF_AUXT + NSLOT * TC_BN * 4;
+  static constexpr int NBAR = 2 + 2 * NSLOT + 2 * 4 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM = OFF_MISC + 64 + 1024;  // + alignment slack
+};
+
+// ----------------------------------------------------------------------------- schedule
+// Per (batch, ts-head): packed-block max timestamps T_j (masked lanes read seq_k + 1), then
+// for every query block mb: n1 = first j with T_j >= 128*mb - window, last_safe = T_{n1-1}
+// (or -1), dense start block = (last_safe + 1) // 128. Also the smallest valid timestamp of
+// every packed block for the pure-phase-1 variant (count > 0 and index < num_packed).
+__global__ void __launch_bounds__(256) schedule_kernel(const int32_t* __restrict__ ts, int64_t tsb, int64_t tsh,
+                                                       int64_t tsn, const void* counts, int64_t cb, int64_t ch,
+                                                       int64_t cn, int counts_is_int, int Hts, int num_packed,
+                                                       int seq_k, int window, int nmb, int nblk, int2* sched,
+                                                       int32_t* blkmin, int want_blkmin) {
+  extern __shared__ int32_t sT[];  // nblk block maxima
+  const int bh = blockIdx.x;
+  const int b = bh / Hts, h = bh % Hts;
+  const int32_t* tsr = ts + b * tsb + h * tsh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int j = warp; j < nblk; j += blockDim.x >> 5) {
+    int tmax = INT32_MIN, tmin = INT32_MAX;
+    for (int e = lane; e < TC_BN; e += 32) {
+      const int key = j * TC_BN + e;
+      int t;
+      if (key < num_packed) {
+        t = tsr[static_cast<int64_t>(key) * tsn];
+        if (want_blkmin) {
+          const int64_t off = b * cb + h * ch + static_cast<int64_t>(key) * cn;
+          const float c = counts_is_int ? static_cast<float>(static_cast<const int32_t*>(counts)[off])
+                                        : static_cast<const float*>(counts)[off];
+          if (c > 0.f) tmin = min(tmin, t);
+        }
+      } else {
+        t = seq_k + 1;
+      }
+      tmax = max(tmax, t);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      tmax = max(tmax, __shfl_xor_sync(0xFFFFFFFFu, tmax, o));
+      tmin = min(tmin, __shfl_xor_sync(0xFFFFFFFFu, tmin, o));
+    }
+    if (lane == 0) {
+      sT[j] = tmax;
+      if (want_blkmin) blkmin[static_cast<int64_t>(bh) * nblk + j] = tmin;
+    }
+  }
+  __syncthreads();
+  for (int mb = threadIdx.x; mb < nmb; mb += blockDim.x) {
+    const int thr = mb * TC_BM - window;
+    int n1 = 0;
+    while (n1 < nblk && sT[n1] < thr) ++n1;
+    const int last_safe = n1 ? sT[n1 - 1] : -1;
+    const int ds = max(0, (last_safe + 1) / TC_BN);
+    sched[static_cast<int64_t>(bh) * nmb + mb] = make_int2(n1, ds);
+  }
+}
+
+// ----------------------------------------------------------------------------- units
+struct Unit {
+  int b, hq[2], hts[2], mb[2];
+  bool valid[2];
+};
+
+__device__ __forceinline__ Unit decode_unit(const TcParams& p, int u) {
+  Unit U;
+  if (p.pair_heads) {
+    const int Hkv = p.Hq / p.kv_group;
+    const int npair = p.kv_group / 2;
+    const int per_mb = p.B * Hkv * npair;
+    const int mb = p.nmb - 1 - u / per_mb;
+    const int r = u % per_mb;
+    const int bk = r / npair, pr = r % npair;
+    U.b = bk / Hkv;
+    const int hk = bk % Hkv;
+    U.hq[0] = hk * p.kv_group + 2 * pr;
+    U.hq[1] = U.hq[0] + 1;
+    U.mb[0] = U.mb[1] = mb;
+    U.valid[0] = U.valid[1] = true;
+  } else {
+    const int nmp = (p.nmb + 1) / 2;
+    const int per = p.B * p.Hq;
+    const int mp = nmp - 1 - u / per;
+    const int bh = u % per;
+    U.b = bh / p.Hq;
+    U.hq[0] = U.hq[1] = bh % p.Hq;
+    U.mb[0] = 2 * mp;
+    U.mb[1] = 2 * mp + 1;
+    U.valid[0] = true;
+    U.valid[1] = U.mb[1] < p.nmb;
+  }
+  U.hts[0] = U.hq[0] / p.kv_group;
+  U.hts[1] = U.hq[1] / p.kv_group;
+  return U;
+}
+
+// Serpentine static assignment: round r covers units [r*G, (r+1)*G); odd rounds reverse.
+__device__ __forceinline__ int unit_of(int iter, int cta, int G) {
+  const int base = iter * G;
+  return (iter & 1) ? base + (G - 1 - cta) : base + cta;
+}
+
+struct TileInfo {
+  int packed;   // 1: packed block, 0: dense block
+  int idx;      // block index (in 128-key blocks)
+  int use;      // bit x set: query tile x attends this block
+  int needs_v;  // the block's V is loaded and a PV product issued
+};
+
+// Enumerates the union of both query tiles' block lists in reference order (all packed
+// blocks first, then dense blocks ascending). Every role walks the same sequence.
+struct TileSeq {
+  int n1[2], ds[2], de[2];
+  int pmax, dlo, dhi;
+  int state, cur;  // state 0: packed, 1: dense, 2: done
+  int mb_lo[2];
+
+  __device__ __forceinline__ void init(const TcParams& p, const Unit& U) {
+    for (int x = 0; x < 2; ++x) {
+      n1[x] = 0; ds[x] = 0; de[x] = 0;
+      mb_lo[x] = U.mb[x] * TC_BM;
+      if (!U.valid[x]) continue;
+      const int m0 = U.mb[x] * TC_BM;
+      const int hi = min(p.seq_k, m0 + TC_BM);
+      if (p.variant == TC_HYBRID || p.variant == TC_SANITY) {
+        const int2 s = p.sched[(static_cast<int64_t>(U.b) * p.Hts + U.hts[x]) * p.nmb + U.mb[x]];
+        n1[x] = s.x;
+        ds[x] = s.y;
+        de[x] = (hi + TC_BN - 1) / TC_BN;
+      } else if (p.variant == TC_PURE) {
+        n1[x] = p.nblk;
+      } else {
+        ds[x] = 0;
+        de[x] = p.causal ? (hi + TC_BN - 1) / TC_BN : (p.seq_k + TC_BN - 1) / TC_BN;
+      }
+    }
+    const bool v0 = U.valid[0], v1 = U.valid[1];
+    pmax = max(v0 ? n1[0] : 0, v1 ? n1[1] : 0);
+    dlo = INT32_MAX; dhi = 0;
+    for (int x = 0; x < 2; ++x)
+      if (U.valid[x] && de[x] > ds[x]) { dlo = min(dlo, ds[x]); dhi = max(dhi, de[x]); }
+    if (dlo == INT32_MAX) { dlo = 0; dhi = 0; }
+    state = 0;
+    cur = 0;
+  }
+
+  __device__ __forceinline__ bool next(const TcParams& p, const Unit& U, TileInfo& t) {
+    while (state == 0) {
+      if (cur >= pmax) { state = 1; cur = dlo; break; }
+      const int j = cur++;
+      int use = 0;
+      for (int x = 0; x < 2; ++x) {
+        if (!U.valid[x] || j >= n1[x]) continue;
+        if (p.variant == TC_PURE) {
+          const int tmin = p.blkmin[(static_cast<int64_t>(U.b) * p.Hts + U.hts[x]) * p.nblk + j];
+          if (tmin > mb_lo[x] + TC_BM - 1) continue;  // block masked for every row: no-op
+        }
+        use |= 1 << x;
+      }
+      if (!use) continue;
+      t.packed = 1; t.idx = j; t.use = use; t.needs_v = (p.variant != TC_SANITY);
+      return true;
+    }
+    if (state == 1) {
+      while (cur < dhi) {
+        const int tb = cur++;
+        int use = 0;
+        for (int x = 0; x < 2; ++x)
+          if (U.valid[x] && tb >= ds[x] && tb < de[x]) use |= 1 << x;
+        if (!use) continue;
+        t.packed = 0; t.idx = tb; t.use = use; t.needs_v = 1;
+        return true;
+      }
+      state = 2;
+    }
+    return false;
+  }
+};
+
+// every lane of the warp waits; the outcome is made warp-uniform so warp-collective
+// tcgen05 instructions that follow stay converged
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t par, const Abort& ab, int code) {
+  const bool ok = mbar_wait(bar, par, ab, code);
+  return __all_sync(0xFFFFFFFFu, ok);
+}
+
+// ring of K/V slots: the k-th use maps to slot k % NS in round k / NS
+struct Ring {
+  int k;
+  __device__ __forceinline__ void take(int NS, int& slot, uint32_t& full_par, uint32_t& empty_par) {
+    slot = k % NS;
+    const int round = k / NS;
+    full_par = round & 1;
+    empty_par = (round & 1) ^ 1;
+    ++k;
+  }
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_constant__ TcParams p) {
+  using C = TcCfg<D>;
+  constexpr int NS = C::NSLOT;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* slot_full = bars + 2;
+  uint64_t* slot_empty = bars + 2 + NS;
+  uint64_t* s_full = bars + 2 + 2 * NS;       // [2]
+  uint64_t* p_full = s_full + 2;              // [2]
+  uint64_t* o_full = p_full + 2;              // [2]
+  uint64_t* tile_free = o_full + 2;           // [2]
+  uint64_t* mma_done = tile_free + 2;
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
+  float* auxc = reinterpret_cast<float*>(smem + C::OFF_AUXC);
+  int32_t* auxt = reinterpret_cast<int32_t*>(smem + C::OFF_AUXT);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(slot_full + s, 1);
+      mbar_init(slot_empty + s, 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(s_full + x, 1);
+      mbar_init(p_full + x, 4);
+      mbar_init(o_full + x, 1);
+      mbar_init(tile_free + x, 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tm_q);
+    tma_prefetch_desc(&p.tm_kd);
+    tma_prefetch_desc(&p.tm_vd);
+    tma_prefetch_desc(&p.tm_kp);
+    tma_prefetch_desc(&p.tm_vp);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_base_smem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_smem;
+  const Abort ab{abort_flag, p.err};
+  const int G = gridDim.x;
+  const int n_iter = (p.num_units + G - 1) / G;
+
+  if (warp == 0) {
+    // ================================================================ producer
+    Ring ring{0};
+    uint32_t q_par = 1;
+    int armed[NS];
+    for (int s = 0; s < NS; ++s) armed[s] = -1;
+    int q_issued = 0;
+    const uint32_t kv_bytes = C::KVBYTES;
+    for (int it = 0; it < n_iter; ++it) {
+      const int u = unit_of(it, blockIdx.x, G);
+      if (u >= p.num_units) continue;
+      const Unit U = decode_unit(p, u);
+      if (!warp_wait(q_empty, q_par, ab, ERR_TIMEOUT_PRODUCER)) goto producer_done;
+      q_par ^= 1;
+      if (lane == 0) {
+        const uint32_t qb = (U.valid[0] ? C::QBYTES : 0) + (U.valid[1] ? C::QBYTES : 0);
+        mbar_arrive_expect_tx(q_full, qb);
+        for (int x = 0; x < 2; ++x) {
+          if (!U.valid[x]) continue;
+          uint8_t* dst = smem + (x ? C::OFF_Q1 : C::OFF_Q0);
+          for (int bx = 0; bx < D / 64; ++bx)
+            tma_load_4d(dst + bx * (TC_BM * 128), &p.tm_q, q_full, bx * 64, U.mb[x] * TC_BM, U.hq[x], U.b);
+        }
+      }
+      ++q_issued;
+      TileSeq seq;
+      seq.init(p, U);
+      TileInfo t;
+      while (seq.next(p, U, t)) {
+        const int hk = U.hts[0];  // both tiles of a unit share the K/V head
+        const CUtensorMap* tk = t.packed ? &p.tm_kp : &p.tm_kd;
+        const CUtensorMap* tv = t.packed ? &p.tm_vp : &p.tm_vd;
+        int slot;
+        uint32_t fpar, epar;
+        ring.take(NS, slot, fpar, epar);
+        if (!warp_wait(slot_empty + slot, epar, ab, ERR_TIMEOUT_PRODUCER)) goto producer_done;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(slot_full + slot, kv_bytes);
+          uint8_t* dst = smem + C::OFF_SLOT + slot * C::KVBYTES;
+          for (int bx = 0; bx < D / 64; ++bx)
+            tma_load_4d(dst + bx * (TC_BN * 128), tk, slot_full + slot, bx * 64, t.idx * TC_BN, hk, U.b);
+          armed[slot] = ring.k - 1;
+        }
+        if (!t.needs_v) continue;
+        ring.take(NS, slot, fpar, epar);
+        if (!warp_wait(slot_empty + slot, epar, ab, ERR_TIMEOUT_PRODUCER)) goto producer_done;
+        if (t.packed) {
+          // counts (and timestamps) of this packed block ride with its V tile
+          float* c = auxc + slot * TC_BN;
+          int32_t* tt = auxt + slot * TC_BN;
+          for (int e = lane; e < TC_BN; e += 32) {
+            const int key = t.idx * TC_BN + e;
+            float cv = 0.f;
+            int32_t tv2 = 0;
+            if (key < p.num_packed) {
+              const int64_t off = U.b * p.cs_b + static_cast<int64_t>(hk) * p.cs_h + static_cast<int64_t>(key) * p.cs_n;
+              cv = p.counts_is_int ? static_cast<float>(static_cast<const int32_t*>(p.counts)[off])
+                                   : static_cast<const float*>(p.counts)[off];
+              if (p.variant == TC_PURE)
+                tv2 = p.ts[U.b * p.ts_b + static_cast<int64_t>(hk) * p.ts_h + static_cast<int64_t>(key) * p.ts_n];
+            }
+            c[e] = cv;
+            tt[e] = tv2;
+          }
+          __syncwarp();
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(slot_full + slot, kv_bytes);
+          uint8_t* dst = smem + C::OFF_SLOT + slot * C::KVBYTES;
+          for (int bx = 0; bx < D / 64; ++bx)
+            tma_load_4d(dst + bx * (TC_BN * 128), tv, slot_full + slot, bx * 64, t.idx * TC_BN, hk, U.b);
+          armed[slot] = ring.k - 1;
+        }
+      }
+    }
+  producer_done:
+    // drain: every copy this warp issued must land before the CTA exits
+    if (lane == 0) {
+      for (int s = 0; s < NS; ++s) {
+        if (armed[s] < 0) continue;
+        const uint32_t par = (armed[s] / NS) & 1;
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(slot_full + s, par) && globaltimer() - t0 < 50000000ull) {}
+      }
+      if (q_issued > 0) {
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(q_full, (q_issued - 1) & 1) && globaltimer() - t0 < 50000000ull) {}
+      }
+    }
+  } else if (warp == 1) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = umma_idesc_f16(TC_BM, TC_BN, BF16, false);
+      constexpr uint32_t IDESC_PV = umma_idesc_f16(TC_BM, D, BF16, true);
+      const uint32_t q_addr[2] = {smem_u32(smem + C::OFF_Q0), smem_u32(smem + C::OFF_Q1)};
+      const uint32_t slot_addr0 = smem_u32(smem + C::OFF_SLOT);
+      const uint32_t tS[2] = {tmem + 0, tmem + 128};
+      const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
+      Ring ring{0};
+      uint32_t q_par = 0;
+      uint32_t free_par[2] = {1, 1};
+      uint32_t p_par[2] = {0, 0};
+      bool aborted = false;
+      for (int it = 0; it < n_iter && !aborted; ++it) {
+        const int u = unit_of(it, blockIdx.x, G);
+        if (u >= p.num_units) continue;
+        const Unit U = decode_unit(p, u);
+        if (!mbar_wait(q_full, q_par, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+        q_par ^= 1;
+        tc_fence_after();
+        bool freed[2] = {false, false};
+        bool o_init[2] = {false, false};
+        auto ensure_free = [&](int x) -> bool {
+          if (freed[x]) return true;
+          if (!mbar_wait(tile_free + x, free_par[x], ab, ERR_TIMEOUT_MMA)) return false;
+          free_par[x] ^= 1;
+          tc_fence_after();
+          freed[x] = true;
+          return true;
+        };
+        auto issue_S = [&](int x, int kslot) {
+          const uint32_t kbase = slot_addr0 + kslot * C::KVBYTES;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (TC_BM * 128) + (kk & 3) * 32;
+            const uint64_t ad = umma_desc_sw128(q_addr[x] + off, 16, 1024);
+            const uint64_t bd = umma_desc_sw128(kbase + off, 16, 1024);
+            umma_ss(tS[x], ad, bd, IDESC_S, kk > 0);
+          }
+        };
+        auto issue_PV = [&](int x, int vslot) {
+          const uint32_t vbase = slot_addr0 + vslot * C::KVBYTES;
+#pragma unroll
+          for (int kk = 0; kk < TC_BN / 16; ++kk) {
+            const uint64_t bd = umma_desc_sw128(vbase + kk * 2048, TC_BN * 128, 1024);
+            umma_ts(tO[x], tS[x] + kk * 8, bd, IDESC_PV, (o_init[x] || kk > 0) ? 1u : 0u);
+          }
+          o_init[x] = true;
+        };
+
+        TileSeq seq;
+        seq.init(p, U);
+        TileInfo cur, nxt;
+        bool have_cur = seq.next(p, U, cur);
+        int cur_k, cur_v = -1;
+        uint32_t fp, ep;
+        const bool sanity = p.variant == TC_SANITY;
+        if (have_cur) {
+          ring.take(NS, cur_k, fp, ep);
+          if (!mbar_wait(slot_full + cur_k, fp, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+          tc_fence_after();
+          for (int x = 0; x < 2; ++x) {
+            if (!(cur.use >> x & 1)) continue;
+            if (!ensure_free(x)) { aborted = true; break; }
+            issue_S(x, cur_k);
+            if (!(sanity && cur.packed)) umma_commit(s_full + x);
+          }
+          if (aborted) break;
+          umma_commit(slot_empty + cur_k);
+        }
+        while (have_cur) {
+          if (cur.needs_v) {
+            ring.take(NS, cur_v, fp, ep);
+            if (!mbar_wait(slot_full + cur_v, fp, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+            tc_fence_after();
+          }
+          const bool have_nxt = seq.next(p, U, nxt);
+          int nk = -1;
+          bool nk_ready = false;
+          for (int x = 0; x < 2; ++x) {
+            if (cur.needs_v && (cur.use >> x & 1)) {
+              if (!mbar_wait(p_full + x, p_par[x], ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+              p_par[x] ^= 1;
+              tc_fence_after();
+              issue_PV(x, cur_v);
+            }
+            if (have_nxt && (nxt.use >> x & 1)) {
+              if (!nk_ready) {
+                ring.take(NS, nk, fp, ep);
+                if (!mbar_wait(slot_full + nk, fp, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+                tc_fence_after();
+                nk_ready = true;
+              }
+              if (!ensure_free(x)) { aborted = true; break; }
+              issue_S(x, nk);
+              if (!(sanity && nxt.packed)) umma_commit(s_full + x);
+            }
+          }
+          if (aborted) break;
+          if (cur.needs_v) umma_commit(slot_empty + cur_v);
+          if (nk_ready) umma_commit(slot_empty + nk);
+          if (!have_nxt) break;
+          cur = nxt;
+          cur_k = nk;
+        }
+        if (aborted) break;
+        // tile_free is consumed exactly once per unit and query tile
+        for (int x = 0; x < 2 && !aborted; ++x)
+          if (!ensure_free(x)) aborted = true;
+        if (aborted) break;
+        // all S of this unit issued: the Q buffers may be refilled once they complete
+        umma_commit(q_empty);
+        for (int x = 0; x < 2; ++x)
+          if (o_init[x]) umma_commit(o_full + x);
+      }
+      // wait for every MMA this thread issued before TMEM can be released
+      umma_commit(mma_done);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(mma_done, 0) && globaltimer() - t0 < 50000000ull) {}
+    }
+  } else if (warp >= 4) {
+    // ================================================================ softmax + epilogue
+    const int x = (warp - 4) >> 2;          // query tile
+    const int wq = warp & 3;                // TMEM lane quarter
+    const int r = wq * 32 + lane;           // row within the tile
+    const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_base + 128 * x;
+    const uint32_t tO = tmem + lane_base + 256 + D * x;
+    const float sl2 = p.scale_log2;
+    Ring ring{0};
+    uint32_t s_par = 0, o_par = 0;
+    for (int it = 0; it < n_iter; ++it) {
+      const int u = unit_of(it, blockIdx.x, G);
+      if (u >= p.num_units) continue;
+      const Unit U = decode_unit(p, u);
+      const int row = U.mb[x] * TC_BM + r;
+      float m_used = -INFINITY, l = 0.f;
+      bool o_has = false;
+      TileSeq seq;
+      seq.init(p, U);
+      TileInfo t;
+      bool ok = true;
+      while (seq.next(p, U, t)) {
+        int ks, vs = -1;
+        uint32_t fp, ep, vfp = 0;
+        ring.take(NS, ks, fp, ep);
+        if (t.needs_v) ring.take(NS, vs, vfp, ep);
+        if (!U.valid[x] || !(t.use >> x & 1) || !t.needs_v) continue;
+        if (!warp_wait(s_full + x, s_par, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
+        s_par ^= 1;
+        tc_fence_after();
+        const float* cnt = auxc + vs * TC_BN;
+        const int32_t* tsv = auxt + vs * TC_BN;
+        if (t.packed) {
+          // the packed block's counts arrive with its V tile
+          if (!warp_wait(slot_full + vs, vfp, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
+        }
+        const int n0 = t.idx * TC_BN;
+        const uint32_t NEG_INF = 0xFF800000u;
+        // pure-phase-1 validity (count > 0, index < num_packed, timestamp <= row) as a
+        // 128-bit mask, built before S is live to keep register pressure down
+        uint32_t vm[4] = {~0u, ~0u, ~0u, ~0u};
+        if (p.variant == TC_PURE) {
+#pragma unroll 1
+          for (int w = 0; w < 4; ++w) {
+            uint32_t bits = 0;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int j = w * 32 + e;
+              const bool v = (n0 + j < p.num_packed) && cnt[j] > 0.f && tsv[j] <= row;
+              bits |= (v ? 1u : 0u) << e;
+            }
+            if (w == 0) vm[0] = bits; else if (w == 1) vm[1] = bits; else if (w == 2) vm[2] = bits; else vm[3] = bits;
+          }
+        }
+        uint32_t sr[TC_BN];  // raw S bits; later reused in place for the packed P
+#pragma unroll
+        for (int c = 0; c < TC_BN / 32; ++c) tmem_ld32(tS + c * 32, sr + c * 32);
+        if (p.variant == TC_PURE) {
+#pragma unroll
+          for (int j = 0; j < TC_BN; ++j) sr[j] = ((vm[j >> 5] >> (j & 31)) & 1u) ? sr[j] : NEG_INF;
+        } else {
+          int lim = TC_BN;
+          if (t.packed) {
+            lim = p.num_packed - n0;
+          } else {
+            lim = p.seq_k - n0;
+            if (p.variant != TC_DENSE || p.causal) lim = min(lim, row - n0 + 1);
+          }
+          if (lim < TC_BN) {
+#pragma unroll
+            for (int j = 0; j < TC_BN; ++j) sr[j] = (j < lim) ? sr[j] : NEG_INF;
+          }
+        }
+        float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
+        float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
+#pragma unroll
+        for (int j = 4; j < TC_BN; j += 4) {
+          mx0 = fmaxf(mx0, __uint_as_float(sr[j]));
+          mx1 = fmaxf(mx1, __uint_as_float(sr[j + 1]));
+          mx2 = fmaxf(mx2, __uint_as_float(sr[j + 2]));
+          mx3 = fmaxf(mx3, __uint_as_float(sr[j + 3]));
+        }
+        const float mt = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+        // bf16 keeps a stale max until it grows by 2^8; fp16 tracks the exact max because
+        // probabilities times counts must stay inside fp16 range
+        const bool need = mt > m_used + (BF16 ? 8.f : 0.f);
+        if (__any_sync(0xFFFFFFFFu, need)) {
+          const float m_new = need ? mt : m_used;
+          const float f = need ? ex2(m_used - m_new) : 1.f;
+          l *= f;
+          if (o_has) {
+#pragma unroll 1
+            for (int c = 0; c < D / 16; ++c) {
+              uint32_t o[16];
+              tmem_ld16(tO + c * 16, o);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f);
+              tmem_st16(tO + c * 16, o);
+            }
+          }
+          m_used = m_new;
+        }
+        const float msub = (m_used == -INFINITY) ? 0.f : m_used;
+        float l0 = 0.f, l1 = 0.f;
+        // pair (2c, 2c+1) is packed in place into sr[c] as bf16x2 / f16x2
+        if (t.packed) {
+#pragma unroll
+          for (int j = 0; j < TC_BN; j += 2) {
+            // keep count loads next to their use (16 keys at a time)
+            if ((j & 15) == 0) asm volatile("" ::: "memory");
+            const float2 cc = *reinterpret_cast<const float2*>(cnt + j);
+            const float a = ex2(fmaf(__uint_as_float(sr[j]), sl2, -msub)) * cc.x;
+            const float bq = ex2(fmaf(__uint_as_float(sr[j + 1]), sl2, -msub)) * cc.y;
+            l0 += a;
+            l1 += bq;
+            sr[j / 2] = pack2(a, bq, BF16);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < TC_BN; j += 2) {
+            const float a = ex2(fmaf(__uint_as_float(sr[j]), sl2, -msub));
+            const float bq = ex2(fmaf(__uint_as_float(sr[j + 1]), sl2, -msub));
+            l0 += a;
+            l1 += bq;
+            sr[j / 2] = pack2(a, bq, BF16);
+          }
+        }
+        l += l0 + l1;
+        tmem_st32(tS, sr);
+        tmem_st32(tS + 32, sr + 32);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full + x);
+        o_has = true;
+      }
+      if (!ok) break;
+      if (!U.valid[x]) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tile_free + x);
+        continue;
+      }
+      // ---------------- epilogue: O / l -> out
+      float lf = l;
+      if (p.variant == TC_PURE && !(lf > 0.f)) lf = 1.f;
+      const float inv = 1.f / lf;
+      const bool row_ok = row < p.seq_q;
+      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      T* orow = static_cast<T*>(p.out) + U.b * p.os_b + static_cast<int64_t>(U.hq[x]) * p.os_h +
+                static_cast<int64_t>(row) * p.os_m;
+      if (o_has) {
+        if (!warp_wait(o_full + x, o_par, ab, ERR_TIMEOUT_EPILOGUE)) break;
+        o_par ^= 1;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t ob[32];
+          tmem_ld32(tO + c * 32, ob);
+          float o[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = __uint_as_float(ob[j]);
+          if (row_ok) {
+            if (p.out_vec_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 w;
+                w.x = pack2(o[j] * inv, o[j + 1] * inv, BF16);
+                w.y = pack2(o[j + 2] * inv, o[j + 3] * inv, BF16);
+                w.z = pack2(o[j + 4] * inv, o[j + 5] * inv, BF16);
+                w.w = pack2(o[j + 6] * inv, o[j + 7] * inv, BF16);
+                *reinterpret_cast<uint4*>(orow + c * 32 + j) = w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) orow[c * 32 + j] = from_f32<T>(o[j] * inv);
+            }
+          }
+        }
+      } else if (row_ok) {
+        // no block attended: the reference divides a zero accumulator by l
+        const float v = 0.f * inv;
+        for (int j = 0; j < D; ++j) orow[j] = from_f32<T>(v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tile_free + x);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem, 512);
+}
+
+template <int D, bool BF16>
+static cudaError_t launch_tc_t(const TcParams& p, int num_sms, cudaStream_t st) {
+  using C = TcCfg<D>;
+  auto kfn = attn_tc_kernel<D, BF16>;
+  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  const int grid = p.num_units < num_sms ? p.num_units : num_sms;
+  if (grid <= 0) return cudaSuccess;
+  kfn<<<grid, TC_THREADS, C::SMEM, st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attn_tc(int head_dim, bool bf16, const TcParams& p, int num_sms, cudaStream_t st) {
+  if (head_dim == 128) return bf16 ? launch_tc_t<128, true>(p, num_sms, st) : launch_tc_t<128, false>(p, num_sms, st);
+  if (head_dim == 64) return bf16 ? launch_tc_t<64, true>(p, num_sms, st) : launch_tc_t<64, false>(p, num_sms, st);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_schedule(const int32_t* ts, const int64_t* tss, const void* counts, const int64_t* cs,
+                            int counts_is_int, int B, int Hts, int num_packed, int seq_k, int window, int nmb,
+                            int nblk, int2* sched, int32_t* blkmin, int want_blkmin, cudaStream_t st) {
+  if (B * Hts == 0) return cudaSuccess;
+  const size_t sm = static_cast<size_t>(nblk > 0 ? nblk : 1) * sizeof(int32_t);
+  if (sm > 200 * 1024) return cudaErrorInvalidValue;
+  if (sm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(schedule_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(sm));
+    if (e != cudaSuccess) return e;
+  }
+  schedule_kernel<<<B * Hts, 256, sm, st>>>(ts, tss[0], tss[1], tss[2], counts, cs[0], cs[1], cs[2], counts_is_int,
+                                            Hts, num_packed, seq_k, window, nmb, nblk, sched, blkmin, want_blkmin);
+  return cudaGetLastError();
+}
+
+}  // namespace dab

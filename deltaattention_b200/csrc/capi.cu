@@ -1,0 +1,424 @@
+// C ABI of the B200 delta-attention library (declared in include/deltaattn_b200.h).
+//
+// Every entry point takes plain device pointers, element strides, scalars and a CUDA
+// stream, launches asynchronously on that stream and returns 0 or a nonzero status whose
+// message `dab_last_error()` returns. No entry point allocates device memory: scratch is
+// passed in by the caller (sizes from the *_workspace_size functions).
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "params.cuh"
+#include "../../include/deltaattn_b200.h"
+
+namespace dab {
+cudaError_t launch_chunked_eval(int, int, bool, const void*, const int64_t*, int32_t*, const int64_t*, int32_t*,
+                                const int64_t*, float, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                                cudaStream_t);
+cudaError_t launch_scatter_pack(int, const void*, const void*, void*, void*, int32_t*, const int32_t*,
+                                const int32_t*, const int64_t*, const int64_t*, const int64_t*, const int64_t*,
+                                const int64_t*, const int64_t*, const int64_t*, int64_t, int64_t, int64_t, int64_t,
+                                int64_t, int64_t, cudaStream_t);
+cudaError_t launch_rope(int, const void*, const int64_t*, void*, const int64_t*, const void*, const void*,
+                        const int64_t*, int64_t, int64_t, int64_t, int64_t, cudaStream_t);
+cudaError_t launch_periodic_meta(int32_t*, int32_t*, int64_t, int64_t, int64_t, int64_t, cudaStream_t);
+cudaError_t launch_pack_from_keep(int, const int32_t*, const int64_t*, const void*, const int64_t*, const void*,
+                                  const int64_t*, void*, void*, const int64_t*, int32_t*, int32_t*, const int64_t*,
+                                  int32_t*, int64_t, int64_t, int64_t, int64_t, int64_t, int32_t*, int32_t*,
+                                  int32_t*, cudaStream_t);
+cudaError_t launch_attn_simt(int, const SimtParams&, cudaStream_t);
+cudaError_t launch_attn_tc(int, bool, const TcParams&, int, cudaStream_t);
+cudaError_t launch_schedule(const int32_t*, const int64_t*, const void*, const int64_t*, int, int, int, int, int,
+                            int, int, int, int2*, int32_t*, int, cudaStream_t);
+cudaError_t launch_decode_update(int, int, bool, const void*, const void*, void*, void*, void*, void*, int32_t*,
+                                 int32_t*, int32_t*, int64_t, int64_t, float, int64_t, const int64_t*,
+                                 const int64_t*, const int64_t*, const int64_t*, int64_t, int64_t, int64_t, int64_t,
+                                 int*, cudaStream_t);
+cudaError_t launch_decode_attn(int, const void*, const int64_t*, const void*, const int64_t*, const void*,
+                               const int64_t*, const int32_t*, const int64_t*, const int32_t*, const int64_t*,
+                               const void*, const int64_t*, const void*, const int64_t*, void*, const int64_t*,
+                               float, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float*, cudaStream_t);
+size_t decode_attn_workspace(int64_t, int64_t, int64_t, int64_t, int64_t);
+cudaError_t launch_nm_select(int, const void*, const int64_t*, int32_t*, const int64_t*, int64_t, int64_t, int64_t,
+                             int64_t, int, int, int64_t, cudaStream_t);
+}  // namespace dab
+
+using namespace dab;
+
+namespace {
+thread_local std::string g_err;
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return 0;
+  return fail(2, std::string("CUDA error in ") + what + ": " + cudaGetErrorString(e));
+}
+int elem_size(int dtype) { return dtype == F32 ? 4 : 2; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int num_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// 4-D map over (d, rows, heads, batch) with a 64 x 128 box and 128-byte swizzle.
+bool encode_rows(CUtensorMap* m, const void* base, int dtype, int64_t d, int64_t rows, int64_t heads,
+                 int64_t batch, int64_t s_row, int64_t s_head, int64_t s_batch) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return false;
+  const int es = elem_size(dtype);
+  if (rows < 1 || heads < 1 || batch < 1) return false;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(batch)};
+  // extents of 1 never move: give them a harmless legal stride
+  int64_t sr = s_row, sh = s_head, sb = s_batch;
+  if (rows == 1) sr = d;
+  if (heads == 1) sh = sr * rows;
+  if (batch == 1) sb = sh * heads;
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(sr * es), static_cast<cuuint64_t>(sh * es),
+                           static_cast<cuuint64_t>(sb * es)};
+  for (auto s : strides)
+    if (s % 16 != 0 || s == 0 || s >= (1ull << 40)) return false;
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt = dtype == BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+constexpr size_t WS_HEADER = 256;  // device error word + padding
+size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+}  // namespace
+
+extern "C" {
+
+const char* dab_last_error(void) { return g_err.c_str(); }
+
+int dab_abi_version(void) { return 1; }
+
+int dab_set_device(int device) { return cuda_status(cudaSetDevice(device), "dab_set_device"); }
+
+int dab_workspace_error(void* workspace, int* code, void* stream) {
+  if (!workspace || !code) return fail(1, "dab_workspace_error: null argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(workspace, 0, sizeof(int), st);
+  if (e != cudaSuccess) return cuda_status(e, "dab_workspace_error");
+  *code = v;
+  return 0;
+}
+
+// ------------------------------------------------------------------------- selection
+int dab_chunked_eval(const void* in, int dtype, const int64_t* in_strides, int32_t* keep_mask,
+                     const int64_t* km_strides, int32_t* chunk_counts, const int64_t* cc_strides, float threshold,
+                     int64_t seq_len, int64_t head_dim, int64_t chunk_size, int64_t num_heads, int64_t grid_bh,
+                     int64_t grid_chunks, int64_t block_d, int use_cosine, void* stream) {
+  if (!in || !keep_mask || !chunk_counts) return fail(1, "dab_chunked_eval: null pointer");
+  if (block_d < head_dim || block_d > 256 || (block_d & (block_d - 1)))
+    return fail(1, "dab_chunked_eval: BLOCK_D must be a power of two in [head_dim, 256]");
+  if (chunk_size <= 0 || num_heads <= 0) return fail(1, "dab_chunked_eval: bad chunk_size / num_heads");
+  const int bd = block_d < 16 ? 16 : static_cast<int>(block_d);
+  return cuda_status(launch_chunked_eval(dtype, bd, use_cosine != 0, in, in_strides, keep_mask, km_strides,
+                                         chunk_counts, cc_strides, threshold, seq_len, head_dim, chunk_size,
+                                         num_heads, grid_bh, grid_chunks, static_cast<cudaStream_t>(stream)),
+                     "chunked_eval");
+}
+
+int dab_parallel_scatter_pack_kv(const void* k_in, const void* v_in, void* k_packed, void* v_packed,
+                                 int32_t* packed_ts, const int32_t* keep_mask, const int32_t* index_map, int dtype,
+                                 const int64_t* k_strides, const int64_t* v_strides, const int64_t* kp_strides,
+                                 const int64_t* vp_strides, const int64_t* ts_strides, const int64_t* km_strides,
+                                 const int64_t* im_strides, int64_t seq_len, int64_t head_dim, int64_t num_heads,
+                                 int64_t num_packed, int64_t grid_bh, int64_t grid_s, int64_t block_s,
+                                 void* stream) {
+  if (!k_in || !v_in || !keep_mask || !index_map) return fail(1, "dab_parallel_scatter_pack_kv: null pointer");
+  if (num_packed > 0 && (!k_packed || !v_packed || !packed_ts))
+    return fail(1, "dab_parallel_scatter_pack_kv: null packed buffer");
+  if (num_heads <= 0) return fail(1, "dab_parallel_scatter_pack_kv: num_heads must be positive");
+  return cuda_status(launch_scatter_pack(dtype, k_in, v_in, k_packed, v_packed, packed_ts, keep_mask, index_map,
+                                         k_strides, v_strides, kp_strides, vp_strides, ts_strides, km_strides,
+                                         im_strides, seq_len, head_dim, num_heads, grid_bh, grid_s * block_s,
+                                         num_packed, static_cast<cudaStream_t>(stream)),
+                     "parallel_scatter_pack_kv");
+}
+
+// ------------------------------------------------------------------------- attention
+size_t dab_hybrid_flash_workspace_size(int64_t batch, int64_t ts_heads, int64_t seq_len_q, int64_t num_packed) {
+  const int64_t nmb = (seq_len_q + 127) / 128;
+  const int64_t nblk = (num_packed + 127) / 128;
+  return WS_HEADER + round256(static_cast<size_t>(batch * ts_heads * nmb) * 8) +
+         round256(static_cast<size_t>(batch * ts_heads * (nblk > 0 ? nblk : 1)) * 4);
+}
+
+static int run_attention(int variant, int causal, const void* q, const void* kd, const void* vd, const void* kp,
+                         const void* vp, const int32_t* ts, const void* counts, int counts_is_int, void* out,
+                         int dtype, const int64_t* qs, const int64_t* kds, const int64_t* vds, const int64_t* kps,
+                         const int64_t* vps, const int64_t* tss, const int64_t* cs, const int64_t* os,
+                         float sm_scale, int64_t seq_q, int64_t seq_k, int64_t num_packed, int64_t head_dim,
+                         int64_t num_heads, int64_t window, int64_t grid_m, int64_t grid_bh, int64_t block_m,
+                         int64_t block_n, int64_t block_d, int64_t kv_group, void* workspace,
+                         size_t workspace_bytes, int force_simt, cudaStream_t st, const char* name) {
+  if (!q || !kd || !vd || !out) return fail(1, std::string(name) + ": null pointer");
+  if (num_heads <= 0 || kv_group <= 0 || num_heads % kv_group) return fail(1, std::string(name) + ": bad heads");
+  if (grid_bh % num_heads) return fail(1, std::string(name) + ": grid must cover whole batches of heads");
+  if (block_d < head_dim) return fail(1, std::string(name) + ": BLOCK_D < head_dim");
+  const int64_t B = grid_bh / num_heads;
+  const int64_t Hts = num_heads / kv_group;
+  const bool needs_packed = (variant != 3);
+  if (needs_packed && num_packed > 0 && (!kp || !vp || !ts || !counts))
+    return fail(1, std::string(name) + ": null packed tensor");
+  const int64_t nmb = (seq_q + 127) / 128;
+  const int64_t nblk = (num_packed + 127) / 128;
+
+  // ---- tcgen05 path eligibility
+  bool tc = !force_simt && (dtype == BF16 || dtype == F16) && (head_dim == 64 || head_dim == 128) &&
+            block_d == head_dim && block_m == 128 && block_n == 128 && grid_m == nmb && sm_scale > 0.f &&
+            seq_q > 0 && seq_k > 0 && seq_q < (1ll << 31) && seq_k < (1ll << 31) && num_packed < (1ll << 31);
+  tc = tc && qs[3] == 1 && kds[3] == 1 && vds[3] == 1 && os[3] == 1 && aligned16(q) && aligned16(kd) &&
+       aligned16(vd);
+  if (needs_packed && num_packed > 0) tc = tc && kps[3] == 1 && vps[3] == 1 && aligned16(kp) && aligned16(vp);
+  const size_t need_ws = dab_hybrid_flash_workspace_size(B, Hts, seq_q, num_packed);
+  if (tc && (!workspace || workspace_bytes < need_ws)) tc = false;
+  if (tc) {
+    TcParams p;
+    std::memset(&p, 0, sizeof(p));
+    bool ok = encode_rows(&p.tm_q, q, dtype, head_dim, seq_q, num_heads, B, qs[2], qs[1], qs[0]);
+    ok = ok && encode_rows(&p.tm_kd, kd, dtype, head_dim, seq_k, Hts, B, kds[2], kds[1], kds[0]);
+    ok = ok && encode_rows(&p.tm_vd, vd, dtype, head_dim, seq_k, Hts, B, vds[2], vds[1], vds[0]);
+    if (needs_packed && num_packed > 0) {
+      ok = ok && encode_rows(&p.tm_kp, kp, dtype, head_dim, num_packed, Hts, B, kps[2], kps[1], kps[0]);
+      ok = ok && encode_rows(&p.tm_vp, vp, dtype, head_dim, num_packed, Hts, B, vps[2], vps[1], vps[0]);
+    } else {
+      p.tm_kp = p.tm_kd;
+      p.tm_vp = p.tm_vd;
+    }
+    if (ok) {
+      uint8_t* ws = static_cast<uint8_t*>(workspace);
+      p.err = reinterpret_cast<int*>(ws);
+      p.sched = reinterpret_cast<const int2*>(ws + WS_HEADER);
+      p.blkmin = reinterpret_cast<const int32_t*>(ws + WS_HEADER + round256(static_cast<size_t>(B * Hts * nmb) * 8));
+      p.out = out;
+      p.os_b = os[0]; p.os_h = os[1]; p.os_m = os[2];
+      p.ts = ts; p.ts_b = tss ? tss[0] : 0; p.ts_h = tss ? tss[1] : 0; p.ts_n = tss ? tss[2] : 0;
+      p.counts = counts; p.cs_b = cs ? cs[0] : 0; p.cs_h = cs ? cs[1] : 0; p.cs_n = cs ? cs[2] : 0;
+      p.counts_is_int = counts_is_int;
+      p.scale_log2 = sm_scale * 1.4426950408889634f;
+      p.seq_q = static_cast<int>(seq_q); p.seq_k = static_cast<int>(seq_k);
+      p.num_packed = static_cast<int>(needs_packed ? num_packed : 0);
+      p.B = static_cast<int>(B); p.Hq = static_cast<int>(num_heads); p.kv_group = static_cast<int>(kv_group);
+      p.Hts = static_cast<int>(Hts);
+      p.nmb = static_cast<int>(nmb); p.nblk = static_cast<int>(needs_packed ? nblk : 0);
+      p.variant = variant; p.causal = causal;
+      p.pair_heads = (kv_group % 2 == 0) ? 1 : 0;
+      p.num_units = static_cast<int>(p.pair_heads ? nmb * B * Hts * (kv_group / 2) : ((nmb + 1) / 2) * B * num_heads);
+      p.out_vec_ok = aligned16(out) && (os[0] * 2) % 16 == 0 && (os[1] * 2) % 16 == 0 && (os[2] * 2) % 16 == 0;
+      if (variant != 3 && num_packed > 0) {
+        cudaError_t e = launch_schedule(ts, tss, counts, cs, counts_is_int, static_cast<int>(B),
+                                        static_cast<int>(Hts), static_cast<int>(num_packed), static_cast<int>(seq_k),
+                                        static_cast<int>(window), static_cast<int>(nmb), static_cast<int>(nblk),
+                                        reinterpret_cast<int2*>(ws + WS_HEADER),
+                                        reinterpret_cast<int32_t*>(const_cast<int32_t*>(p.blkmin)), variant == 2, st);
+        if (e != cudaSuccess) return cuda_status(e, "schedule");
+      } else if (variant != 3) {
+        // no packed keys: phase 1 is empty and phase 2 starts at key 0
+        cudaError_t e = cudaMemsetAsync(ws + WS_HEADER, 0, static_cast<size_t>(B * Hts * nmb) * 8, st);
+        if (e != cudaSuccess) return cuda_status(e, "schedule");
+      }
+      return cuda_status(launch_attn_tc(static_cast<int>(head_dim), dtype == BF16, p, num_sms(), st), name);
+    }
+    // tensor maps not encodable (strides / alignment): fall through to the CUDA-core path
+  }
+  SimtParams sp;
+  std::memset(&sp, 0, sizeof(sp));
+  sp.q = q; sp.kd = kd; sp.vd = vd; sp.kp = kp; sp.vp = vp; sp.ts = ts; sp.counts = counts; sp.out = out;
+  for (int i = 0; i < 4; ++i) {
+    sp.qs[i] = qs[i]; sp.kds[i] = kds[i]; sp.vds[i] = vds[i]; sp.os[i] = os[i];
+    sp.kps[i] = kps ? kps[i] : 0; sp.vps[i] = vps ? vps[i] : 0;
+  }
+  for (int i = 0; i < 3; ++i) { sp.tss[i] = tss ? tss[i] : 0; sp.cs[i] = cs ? cs[i] : 0; }
+  sp.sm_scale = sm_scale;
+  sp.seq_q = seq_q; sp.seq_k = seq_k; sp.num_packed = needs_packed ? num_packed : 0; sp.head_dim = head_dim;
+  sp.num_heads = num_heads; sp.dense_window = window; sp.grid_m = grid_m; sp.grid_bh = grid_bh;
+  sp.block_m = block_m; sp.block_n = block_n; sp.kv_group = kv_group; sp.counts_is_int = counts_is_int;
+  sp.causal = causal; sp.variant = variant;
+  if (head_dim > 128) return fail(1, std::string(name) + ": head_dim > 128 is not supported");
+  if (block_m % 32) return fail(1, std::string(name) + ": BLOCK_M must be a multiple of 32");
+  return cuda_status(launch_attn_simt(dtype, sp, st), name);
+}
+
+int dab_hybrid_flash(int variant, const void* q, const void* k_dense, const void* v_dense, const void* k_packed,
+                     const void* v_packed, const int32_t* packed_ts, const void* packed_counts, int counts_is_int,
+                     void* out, int dtype, const int64_t* strides, float sm_scale, int64_t seq_len_q,
+                     int64_t seq_len_k, int64_t num_packed, int64_t head_dim, int64_t num_heads,
+                     int64_t dense_window, int64_t grid_m, int64_t grid_bh, int64_t block_m, int64_t block_n,
+                     int64_t block_d, int64_t kv_group, void* workspace, size_t workspace_bytes, int force_simt,
+                     void* stream) {
+  if (variant < 0 || variant > 2) return fail(1, "dab_hybrid_flash: variant must be 0, 1 or 2");
+  if (!strides) return fail(1, "dab_hybrid_flash: null strides");
+  const int64_t* s = strides;
+  return run_attention(variant, 1, q, k_dense, v_dense, k_packed, v_packed, packed_ts, packed_counts,
+                       counts_is_int, out, dtype, s + 0, s + 4, s + 8, s + 12, s + 16, s + 20, s + 23, s + 26,
+                       sm_scale, seq_len_q, seq_len_k, num_packed, head_dim, num_heads, dense_window, grid_m,
+                       grid_bh, block_m, block_n, block_d, kv_group, workspace, workspace_bytes, force_simt,
+                       static_cast<cudaStream_t>(stream), "hybrid_flash");
+}
+
+int dab_attn_fwd_flat(const void* q, const void* k, const void* v, float sm_scale, void* out, int dtype,
+                      const int64_t* strides, int64_t Z, int64_t H, int64_t n_ctx, int64_t head_dim,
+                      int64_t block_m, int64_t block_n, int is_causal, int64_t grid_m, int64_t grid_zh,
+                      int64_t kv_group, void* workspace, size_t workspace_bytes, int force_simt, void* stream) {
+  if (!strides) return fail(1, "dab_attn_fwd_flat: null strides");
+  (void)Z;
+  const int64_t* s = strides;
+  int bd = 16;
+  while (bd < head_dim) bd <<= 1;
+  return run_attention(3, is_causal, q, k, v, nullptr, nullptr, nullptr, nullptr, 0, out, dtype, s + 0, s + 4,
+                       s + 8, nullptr, nullptr, nullptr, nullptr, s + 12, sm_scale, n_ctx, n_ctx, 0, head_dim, H, 0,
+                       grid_m, grid_zh, block_m, block_n, bd, kv_group, workspace, workspace_bytes, force_simt,
+                       static_cast<cudaStream_t>(stream), "attn_fwd_flat");
+}
+
+// ------------------------------------------------------------------------- decoding
+int dab_decode_update(const void* new_k, const void* new_v, void* k_exact, void* v_exact, void* k_packed,
+                      void* v_packed, int32_t* packed_counts, int32_t* packed_ts, int32_t* packed_lengths,
+                      int64_t exact_seq_len, int64_t total_seq_len, float threshold, int64_t exact_window,
+                      int dtype, const int64_t* new_strides, const int64_t* exact_strides,
+                      const int64_t* pack_strides, const int64_t* pc_strides, int64_t num_heads, int64_t head_dim,
+                      int64_t block_d, int use_cosine, int64_t programs, int64_t capacity, int* err_word,
+                      void* stream) {
+  if (!new_k || !new_v || !k_exact || !v_exact || !k_packed || !v_packed || !packed_counts || !packed_ts ||
+      !packed_lengths)
+    return fail(1, "dab_decode_update: null pointer");
+  if (block_d < head_dim || block_d > 256 || (block_d & (block_d - 1)))
+    return fail(1, "dab_decode_update: BLOCK_D must be a power of two in [head_dim, 256]");
+  const int bd = block_d < 16 ? 16 : static_cast<int>(block_d);
+  return cuda_status(launch_decode_update(dtype, bd, use_cosine != 0, new_k, new_v, k_exact, v_exact, k_packed,
+                                          v_packed, packed_counts, packed_ts, packed_lengths, exact_seq_len,
+                                          total_seq_len, threshold, exact_window, new_strides, exact_strides,
+                                          pack_strides, pc_strides, num_heads, head_dim, programs, capacity,
+                                          err_word, static_cast<cudaStream_t>(stream)),
+                     "decode_update");
+}
+
+size_t dab_decode_attention_workspace_size(int64_t batch, int64_t num_q_heads, int64_t capacity,
+                                           int64_t exact_len, int64_t head_dim) {
+  return decode_attn_workspace(batch, num_q_heads, capacity, exact_len, head_dim);
+}
+
+int dab_decode_attention(const void* q, const void* k_packed, const void* v_packed, const int32_t* packed_counts,
+                         const int32_t* packed_lengths, const void* k_exact, const void* v_exact, void* out,
+                         int dtype, const int64_t* strides, float sm_scale, int64_t exact_len,
+                         int64_t num_kv_groups, int64_t batch, int64_t num_q_heads, int64_t head_dim,
+                         int64_t capacity, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !k_packed || !v_packed || !packed_counts || !packed_lengths || !k_exact || !v_exact || !out)
+    return fail(1, "dab_decode_attention: null pointer");
+  if (!strides) return fail(1, "dab_decode_attention: null strides");
+  if (num_kv_groups <= 0 || num_q_heads % num_kv_groups) return fail(1, "dab_decode_attention: bad kv groups");
+  if (num_kv_groups > 8) return fail(1, "dab_decode_attention: more than 8 q-heads per kv-head");
+  if (head_dim > 256) return fail(1, "dab_decode_attention: head_dim > 256");
+  const size_t need = decode_attn_workspace(batch, num_q_heads, capacity, exact_len, head_dim);
+  if (!workspace || workspace_bytes < need) return fail(1, "dab_decode_attention: workspace too small");
+  // strides: q(3) kp(4) vp(4) counts(3) lengths(2) ke(4) ve(4) out(3) = 27 (deltaDecoding.py:244-251)
+  const int64_t* s = strides;
+  return cuda_status(launch_decode_attn(dtype, q, s + 0, k_packed, s + 3, v_packed, s + 7, packed_counts, s + 11,
+                                        packed_lengths, s + 14, k_exact, s + 16, v_exact, s + 20, out, s + 24,
+                                        sm_scale, exact_len, num_kv_groups, batch, num_q_heads / num_kv_groups,
+                                        head_dim, capacity, static_cast<float*>(workspace),
+                                        static_cast<cudaStream_t>(stream)),
+                     "decode_attention");
+}
+
+// ------------------------------------------------------------------------- native pieces
+int dab_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* y_strides, const void* cos_t,
+             const void* sin_t, const int64_t* cs_strides, int dtype, int64_t batch, int64_t heads, int64_t seq_len,
+             int64_t head_dim, void* stream) {
+  if (!x || !y || !cos_t || !sin_t) return fail(1, "dab_rope: null pointer");
+  return cuda_status(launch_rope(dtype, x, x_strides, y, y_strides, cos_t, sin_t, cs_strides, batch, heads, seq_len,
+                                 head_dim, static_cast<cudaStream_t>(stream)),
+                     "rope");
+}
+
+int dab_periodic_meta(int32_t* packed_ts, int32_t* packed_counts, int64_t batch_heads, int64_t num_packed,
+                      int64_t seq_len, int64_t period, void* stream) {
+  if (!packed_ts || !packed_counts) return fail(1, "dab_periodic_meta: null pointer");
+  if (period < 1) return fail(1, "dab_periodic_meta: period must be >= 1");
+  if (num_packed != (seq_len + period - 1) / period) return fail(1, "dab_periodic_meta: num_packed != ceil(N/period)");
+  return cuda_status(launch_periodic_meta(packed_ts, packed_counts, batch_heads, num_packed, seq_len, period,
+                                          static_cast<cudaStream_t>(stream)),
+                     "periodic_meta");
+}
+
+size_t dab_pack_from_keep_workspace_size(int64_t batch, int64_t heads, int64_t seq_len) {
+  const int64_t ntile = (seq_len + 1023) / 1024;
+  return static_cast<size_t>(4 * batch * heads * (ntile > 0 ? ntile : 1)) * sizeof(int32_t);
+}
+
+int dab_pack_from_keep(const int32_t* keep_mask, const int64_t* km_strides, const void* k, const int64_t* k_strides,
+                       const void* v, const int64_t* v_strides, void* k_packed, void* v_packed,
+                       const int64_t* pack_strides, int32_t* packed_ts, int32_t* packed_counts,
+                       const int64_t* meta_strides, int32_t* index_map, int dtype, int64_t batch, int64_t heads,
+                       int64_t seq_len, int64_t head_dim, int64_t capacity, int32_t* anchors_per_head,
+                       int32_t* max_anchors, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!keep_mask || !k || !v || !k_packed || !v_packed || !packed_ts || !packed_counts || !anchors_per_head ||
+      !max_anchors)
+    return fail(1, "dab_pack_from_keep: null pointer");
+  if (workspace_bytes < dab_pack_from_keep_workspace_size(batch, heads, seq_len) || !workspace)
+    return fail(1, "dab_pack_from_keep: workspace too small");
+  if (k_strides[3] != 1 || v_strides[3] != 1 || pack_strides[3] != 1 || meta_strides[2] != 1)
+    return fail(1, "dab_pack_from_keep: innermost strides must be 1");
+  return cuda_status(launch_pack_from_keep(dtype, keep_mask, km_strides, k, k_strides, v, v_strides, k_packed,
+                                           v_packed, pack_strides, packed_ts, packed_counts, meta_strides, index_map,
+                                           batch, heads, seq_len, head_dim, capacity,
+                                           static_cast<int32_t*>(workspace), anchors_per_head, max_anchors,
+                                           static_cast<cudaStream_t>(stream)),
+                     "pack_from_keep");
+}
+
+int64_t dab_nm_num_packed(int64_t seq_len, int64_t n_keep, int64_t m_group, int64_t stride) {
+  if (seq_len <= 0 || n_keep <= 0 || m_group <= 0 || stride <= 0) return 0;
+  const int64_t G = (seq_len + stride - 1) / stride;
+  const int64_t full = G / m_group, rem = G % m_group;
+  return full * (n_keep < m_group ? n_keep : m_group) + (rem < n_keep ? rem : n_keep);
+}
+
+int dab_nm_select(const void* k, const int64_t* k_strides, int32_t* keep_mask, const int64_t* km_strides, int dtype,
+                  int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t n_keep, int64_t m_group,
+                  int64_t stride, void* stream) {
+  if (!k || !keep_mask) return fail(1, "dab_nm_select: null pointer");
+  if (m_group < 1 || m_group > 16 || n_keep < 1 || stride < 1)
+    return fail(1, "dab_nm_select: need 1 <= n, 1 <= m <= 16, stride >= 1");
+  if (head_dim > 256) return fail(1, "dab_nm_select: head_dim > 256");
+  return cuda_status(launch_nm_select(dtype, k, k_strides, keep_mask, km_strides, batch, heads, seq_len, head_dim,
+                                      static_cast<int>(n_keep), static_cast<int>(m_group), stride,
+                                      static_cast<cudaStream_t>(stream)),
+                     "nm_select");
+}
+
+}  // extern "C"

@@ -1,0 +1,347 @@
+// Delta decoding on B200: cache update and single-token attention (HBM bound).
+//
+//  * decode_update: fused_hybrid_decode_update_kernel (deltaDecoding.py:9-104). One warp
+//    per (batch, kv-head). When the exact ring is full, the token it evicts is compared
+//    with the last packed key (fp32, reduced in the reference's order so merge / append
+//    decisions are bit-exact) and either merged into that anchor's count or appended.
+//  * decode_attn: fused_hybrid_decode_kernel (deltaDecoding.py:236-362) as split-K
+//    flash-decoding. A CTA owns 128 keys of one (batch, kv-head) for ALL q-heads of the
+//    group, so the packed cache is read from HBM once per kv-head (the reference reads it
+//    once per q-head). Each lane scores one key for every head; chunk max / sum use warp
+//    shuffles; partials (m, l, acc) are merged by decode_combine.
+#include "common.cuh"
+
+namespace dab {
+
+template <typename T, int BD, bool COS>
+__global__ void __launch_bounds__(128) decode_update_kernel(
+    const T* __restrict__ nk, const T* __restrict__ nv, T* __restrict__ ke, T* __restrict__ ve,
+    T* __restrict__ kp, T* __restrict__ vp, int32_t* __restrict__ counts, int32_t* __restrict__ ts,
+    int32_t* __restrict__ lengths, int64_t exact_seq_len, int64_t total_seq_len, float thr, int64_t W,
+    int64_t ns_b, int64_t ns_h, int64_t ns_s, int64_t ns_d, int64_t es_b, int64_t es_h, int64_t es_s, int64_t es_d,
+    int64_t ps_b, int64_t ps_h, int64_t ps_s, int64_t ps_d, int64_t cs_b, int64_t cs_h, int64_t cs_s,
+    int64_t num_heads, int64_t head_dim, int64_t programs, int64_t capacity, int* err) {
+  constexpr int NH = BD > 128 ? 2 : 1;
+  constexpr int PER = BD / 8 / NH;
+  const int lane = threadIdx.x & 31;
+  const int g = lane & 7;
+  const int64_t pid = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (pid >= programs) return;
+  const int64_t b = pid / num_heads, h = pid % num_heads;
+  const int64_t w = exact_seq_len % W;
+  T* ek = ke + b * es_b + h * es_h + w * es_s;
+  T* ev = ve + b * es_b + h * es_h + w * es_s;
+  T* pk = kp + b * ps_b + h * ps_h;
+  T* pv = vp + b * ps_b + h * ps_h;
+  int32_t* cb = counts + b * cs_b + h * cs_h;
+  int32_t* tb = ts + b * cs_b + h * cs_h;
+  const int32_t plen = lengths[pid];
+  if (exact_seq_len >= W) {
+    bool merge = false;
+    if (plen > 0) {
+      const T* lk = pk + static_cast<int64_t>(plen - 1) * ps_s;
+      float ea[NH][PER], la[NH][PER];
+#pragma unroll
+      for (int hh = 0; hh < NH; ++hh)
+#pragma unroll
+        for (int m = 0; m < PER; ++m) {
+          const int e = hh * 128 + g + 8 * m;
+          ea[hh][m] = e < head_dim ? to_f32(ek[e * es_d]) : 0.f;
+          la[hh][m] = e < head_dim ? to_f32(lk[e * ps_d]) : 0.f;
+        }
+      auto tree = [&](float v) {
+        v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+        v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
+        v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));
+        return v;
+      };
+      if constexpr (COS) {
+        float dot = 0.f, n1 = 0.f, n2 = 0.f;
+#pragma unroll
+        for (int hh = 0; hh < NH; ++hh) {
+          float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+#pragma unroll
+          for (int m = 0; m < PER; ++m) {
+            const float p0 = __fmul_rn(ea[hh][m], la[hh][m]);
+            const float p1 = __fmul_rn(ea[hh][m], ea[hh][m]);
+            const float p2 = __fmul_rn(la[hh][m], la[hh][m]);
+            a0 = m ? __fadd_rn(a0, p0) : p0;
+            a1 = m ? __fadd_rn(a1, p1) : p1;
+            a2 = m ? __fadd_rn(a2, p2) : p2;
+          }
+          a0 = tree(a0); a1 = tree(a1); a2 = tree(a2);
+          dot = hh ? __fadd_rn(dot, a0) : a0;
+          n1 = hh ? __fadd_rn(n1, a1) : a1;
+          n2 = hh ? __fadd_rn(n2, a2) : a2;
+        }
+        const float ne = __fsqrt_rn(__fadd_rn(n1, 1e-8f));
+        const float nl = __fsqrt_rn(__fadd_rn(n2, 1e-8f));
+        merge = __fdiv_rn(dot, __fmul_rn(ne, nl)) >= thr;
+      } else {
+        float tot = 0.f;
+#pragma unroll
+        for (int hh = 0; hh < NH; ++hh) {
+          float acc = 0.f;
+#pragma unroll
+          for (int m = 0; m < PER; ++m) {
+            const float d = __fsub_rn(ea[hh][m], la[hh][m]);
+            const float sq = __fmul_rn(d, d);
+            acc = m ? __fadd_rn(acc, sq) : sq;
+          }
+          acc = tree(acc);
+          tot = hh ? __fadd_rn(tot, acc) : acc;
+        }
+        merge = tot <= thr;
+      }
+    }
+    if (merge) {
+      if (lane == 0) cb[static_cast<int64_t>(plen - 1) * cs_s] += 1;
+    } else if (plen < capacity) {
+      T* dk = pk + static_cast<int64_t>(plen) * ps_s;
+      T* dv = pv + static_cast<int64_t>(plen) * ps_s;
+      for (int64_t d = lane; d < head_dim; d += 32) {
+        dk[d * ps_d] = ek[d * es_d];
+        dv[d * ps_d] = ev[d * es_d];
+      }
+      if (lane == 0) {
+        cb[static_cast<int64_t>(plen) * cs_s] = 1;
+        tb[static_cast<int64_t>(plen) * cs_s] = static_cast<int32_t>(total_seq_len - W);
+        lengths[pid] = plen + 1;
+      }
+    } else if (lane == 0 && err) {
+      atomicCAS(err, 0, 0x201);  // packed cache full: the caller must grow it first
+    }
+  }
+  __syncwarp();
+  const T* sk = nk + b * ns_b + h * ns_h;
+  const T* sv = nv + b * ns_b + h * ns_h;
+  for (int64_t d = lane; d < head_dim; d += 32) {
+    ek[d * es_d] = sk[d * ns_d];
+    ev[d * es_d] = sv[d * ns_d];
+  }
+}
+
+cudaError_t launch_decode_update(int dtype, int bd, bool cosine, const void* nk, const void* nv, void* ke,
+                                 void* ve, void* kp, void* vp, int32_t* counts, int32_t* ts, int32_t* lengths,
+                                 int64_t exact_seq_len, int64_t total_seq_len, float thr, int64_t W,
+                                 const int64_t* ns, const int64_t* es, const int64_t* ps, const int64_t* cs,
+                                 int64_t num_heads, int64_t head_dim, int64_t programs, int64_t capacity, int* err,
+                                 cudaStream_t st) {
+  if (programs <= 0) return cudaSuccess;
+  if (W <= 0) return cudaErrorInvalidValue;
+  const unsigned blocks = static_cast<unsigned>((programs + 3) / 4);
+#define DAB_UPD(TY, N, C)                                                                                     \
+  decode_update_kernel<TY, N, C><<<blocks, 128, 0, st>>>(                                                     \
+      static_cast<const TY*>(nk), static_cast<const TY*>(nv), static_cast<TY*>(ke), static_cast<TY*>(ve),      \
+      static_cast<TY*>(kp), static_cast<TY*>(vp), counts, ts, lengths, exact_seq_len, total_seq_len, thr, W,   \
+      ns[0], ns[1], ns[2], ns[3], es[0], es[1], es[2], es[3], ps[0], ps[1], ps[2], ps[3], cs[0], cs[1], cs[2], \
+      num_heads, head_dim, programs, capacity, err);                                                          \
+  return cudaGetLastError();
+#define DAB_UPD_BD(TY, C)            \
+  switch (bd) {                      \
+    case 16: DAB_UPD(TY, 16, C)      \
+    case 32: DAB_UPD(TY, 32, C)      \
+    case 64: DAB_UPD(TY, 64, C)      \
+    case 128: DAB_UPD(TY, 128, C)    \
+    case 256: DAB_UPD(TY, 256, C)    \
+    default: return cudaErrorInvalidValue; \
+  }
+#define DAB_UPD_DT(TY) \
+  if (cosine) { DAB_UPD_BD(TY, true) } else { DAB_UPD_BD(TY, false) }
+  switch (dtype) {
+    case F32: DAB_UPD_DT(float)
+    case F16: DAB_UPD_DT(__half)
+    case BF16: DAB_UPD_DT(__nv_bfloat16)
+    default: return cudaErrorInvalidValue;
+  }
+#undef DAB_UPD
+#undef DAB_UPD_BD
+#undef DAB_UPD_DT
+}
+
+// ----------------------------------------------------------------------------- attention
+constexpr int DEC_KC = 128;   // keys per CTA
+constexpr int DEC_GMAX = 8;   // q-heads per kv-head handled by one CTA
+
+template <typename T, int BD>
+__global__ void __launch_bounds__(128) decode_attn_kernel(
+    const T* __restrict__ q, int64_t qs_b, int64_t qs_h, int64_t qs_d, const T* __restrict__ kp, int64_t kps_b,
+    int64_t kps_h, int64_t kps_n, int64_t kps_d, const T* __restrict__ vp, int64_t vps_b, int64_t vps_h,
+    int64_t vps_n, int64_t vps_d, const int32_t* __restrict__ counts, int64_t cs_b, int64_t cs_h, int64_t cs_n,
+    const int32_t* __restrict__ lengths, int64_t ls_b, int64_t ls_h, const T* __restrict__ ke, int64_t kes_b,
+    int64_t kes_h, int64_t kes_n, int64_t kes_d, const T* __restrict__ ve, int64_t ves_b, int64_t ves_h,
+    int64_t ves_n, int64_t ves_d, float sm_scale, int64_t exact_len, int64_t G, int64_t Hkv, int64_t head_dim,
+    int64_t nchunk, float* __restrict__ part) {
+  __shared__ float sq[DEC_GMAX][BD];
+  __shared__ float sp[DEC_GMAX][DEC_KC];
+  __shared__ float swm[4][DEC_GMAX];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t chunk = blockIdx.x;
+  const int64_t bk = blockIdx.y;
+  const int64_t b = bk / Hkv, hk = bk % Hkv;
+  const int64_t plen = lengths[b * ls_b + hk * ls_h];
+  const int64_t total = plen + exact_len;
+  const int64_t k0 = chunk * DEC_KC;
+  float* pout = part + ((bk * nchunk + chunk) * G) * (BD + 2);
+  if (k0 >= total) {
+    // empty partial: m = -inf, l = 0
+    for (int g = 0; g < G; ++g)
+      if (tid == 0) { pout[g * (BD + 2)] = -INFINITY; pout[g * (BD + 2) + 1] = 0.f; }
+    return;
+  }
+  for (int i = tid; i < G * BD; i += 128) {
+    const int g = i / BD, d = i % BD;
+    sq[g][d] = d < head_dim ? to_f32(q[b * qs_b + (hk * G + g) * qs_h + d * qs_d]) : 0.f;
+  }
+  __syncthreads();
+  // score: lane owns key k0 + warp*32 + lane
+  const int64_t key = k0 + warp * 32 + lane;
+  const bool valid = key < total;
+  const bool packed = key < plen;
+  float s[DEC_GMAX];
+#pragma unroll
+  for (int g = 0; g < DEC_GMAX; ++g) s[g] = 0.f;
+  if (valid) {
+    const T* kr = packed ? kp + b * kps_b + hk * kps_h + key * kps_n
+                         : ke + b * kes_b + hk * kes_h + (key - plen) * kes_n;
+    const int64_t sd = packed ? kps_d : kes_d;
+    for (int d = 0; d < head_dim; ++d) {
+      const float kv = to_f32(kr[d * sd]);
+#pragma unroll
+      for (int g = 0; g < DEC_GMAX; ++g)
+        if (g < G) s[g] = fmaf(sq[g][d], kv, s[g]);
+    }
+  }
+  float bias = 0.f;
+  if (valid && packed) bias = logf(static_cast<float>(counts[b * cs_b + hk * cs_h + key * cs_n]));
+  float mloc[DEC_GMAX];
+#pragma unroll
+  for (int g = 0; g < DEC_GMAX; ++g) {
+    s[g] = valid ? s[g] * sm_scale + bias : -INFINITY;
+    float m = s[g];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    mloc[g] = m;
+  }
+  if (lane == 0)
+    for (int g = 0; g < G; ++g) swm[warp][g] = mloc[g];
+  __syncthreads();
+  float m_c[DEC_GMAX];
+#pragma unroll
+  for (int g = 0; g < DEC_GMAX; ++g)
+    m_c[g] = (g < G) ? fmaxf(fmaxf(swm[0][g], swm[1][g]), fmaxf(swm[2][g], swm[3][g])) : 0.f;
+  __syncthreads();
+  float lsum[DEC_GMAX];
+#pragma unroll
+  for (int g = 0; g < DEC_GMAX; ++g) {
+    if (g >= G) continue;
+    const float ref = (m_c[g] == -INFINITY) ? 0.f : m_c[g];
+    const float pv = valid ? expf(s[g] - ref) : 0.f;
+    sp[g][warp * 32 + lane] = round_as<T>(pv);  // P is cast to V's dtype before the PV product
+    float l = pv;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+    lsum[g] = l;
+  }
+  if (lane == 0)
+    for (int g = 0; g < G; ++g) swm[warp][g] = lsum[g];
+  __syncthreads();
+  // PV: thread owns head-dim column d = tid (and tid + 128 when BD = 256)
+  const int64_t kend = (total - k0 < DEC_KC) ? (total - k0) : DEC_KC;
+  for (int d = tid; d < BD; d += 128) {
+    float acc[DEC_GMAX];
+#pragma unroll
+    for (int g = 0; g < DEC_GMAX; ++g) acc[g] = 0.f;
+    if (d < head_dim) {
+      for (int64_t j = 0; j < kend; ++j) {
+        const int64_t kk = k0 + j;
+        const float v = (kk < plen) ? to_f32(vp[b * vps_b + hk * vps_h + kk * vps_n + d * vps_d])
+                                    : to_f32(ve[b * ves_b + hk * ves_h + (kk - plen) * ves_n + d * ves_d]);
+#pragma unroll
+        for (int g = 0; g < DEC_GMAX; ++g)
+          if (g < G) acc[g] = fmaf(sp[g][j], v, acc[g]);
+      }
+    }
+    for (int g = 0; g < G; ++g) pout[g * (BD + 2) + 2 + d] = acc[g];
+  }
+  if (tid < G) {
+    pout[tid * (BD + 2)] = m_c[tid];
+    pout[tid * (BD + 2) + 1] = swm[0][tid] + swm[1][tid] + swm[2][tid] + swm[3][tid];
+  }
+}
+
+template <typename T, int BD>
+__global__ void __launch_bounds__(128) decode_combine_kernel(const float* __restrict__ part, T* __restrict__ out,
+                                                             int64_t os_b, int64_t os_h, int64_t os_d, int64_t G,
+                                                             int64_t Hkv, int64_t nchunk, int64_t head_dim) {
+  const int64_t bh = blockIdx.x;  // (b, q-head)
+  const int64_t Hq = Hkv * G;
+  const int64_t b = bh / Hq, h = bh % Hq;
+  const int64_t hk = h / G, g = h % G;
+  const int64_t bk = b * Hkv + hk;
+  float m = -INFINITY;
+  for (int64_t c = 0; c < nchunk; ++c) m = fmaxf(m, part[((bk * nchunk + c) * G + g) * (BD + 2)]);
+  const float ref = (m == -INFINITY) ? 0.f : m;
+  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+    float l = 0.f, acc = 0.f;
+    for (int64_t c = 0; c < nchunk; ++c) {
+      const float* pc = part + ((bk * nchunk + c) * G + g) * (BD + 2);
+      const float mc = pc[0];
+      if (mc == -INFINITY) continue;
+      const float f = expf(mc - ref);
+      l += pc[1] * f;
+      acc += pc[2 + d] * f;
+    }
+    out[b * os_b + h * os_h + d * os_d] = from_f32<T>(acc / l);
+  }
+}
+
+size_t decode_attn_workspace(int64_t B, int64_t Hq, int64_t capacity, int64_t exact_len, int64_t head_dim) {
+  int bd = 16;
+  while (bd < head_dim) bd <<= 1;
+  const int64_t nchunk = (capacity + exact_len + DEC_KC - 1) / DEC_KC;
+  return static_cast<size_t>(B * Hq * (nchunk > 0 ? nchunk : 1) * (bd + 2)) * sizeof(float);
+}
+
+cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, const void* kp, const int64_t* kps,
+                               const void* vp, const int64_t* vps, const int32_t* counts, const int64_t* cs,
+                               const int32_t* lengths, const int64_t* ls, const void* ke, const int64_t* kes,
+                               const void* ve, const int64_t* ves, void* out, const int64_t* os, float sm_scale,
+                               int64_t exact_len, int64_t G, int64_t B, int64_t Hkv, int64_t head_dim,
+                               int64_t capacity, float* part, cudaStream_t st) {
+  if (B * Hkv == 0) return cudaSuccess;
+  if (G < 1 || G > DEC_GMAX) return cudaErrorInvalidValue;
+  int bd = 16;
+  while (bd < head_dim) bd <<= 1;
+  if (bd > 256) return cudaErrorInvalidValue;
+  int64_t nchunk = (capacity + exact_len + DEC_KC - 1) / DEC_KC;
+  if (nchunk < 1) nchunk = 1;
+  dim3 grid(static_cast<unsigned>(nchunk), static_cast<unsigned>(B * Hkv));
+#define DAB_DEC(TY, N)                                                                                          \
+  decode_attn_kernel<TY, N><<<grid, 128, 0, st>>>(                                                              \
+      static_cast<const TY*>(q), qs[0], qs[1], qs[2], static_cast<const TY*>(kp), kps[0], kps[1], kps[2], kps[3], \
+      static_cast<const TY*>(vp), vps[0], vps[1], vps[2], vps[3], counts, cs[0], cs[1], cs[2], lengths, ls[0],  \
+      ls[1], static_cast<const TY*>(ke), kes[0], kes[1], kes[2], kes[3], static_cast<const TY*>(ve), ves[0],    \
+      ves[1], ves[2], ves[3], sm_scale, exact_len, G, Hkv, head_dim, nchunk, part);                             \
+  decode_combine_kernel<TY, N><<<static_cast<unsigned>(B * Hkv * G), 128, 0, st>>>(                             \
+      part, static_cast<TY*>(out), os[0], os[1], os[2], G, Hkv, nchunk, head_dim);                              \
+  return cudaGetLastError();
+#define DAB_DEC_BD(TY)           \
+  switch (bd) {                  \
+    case 16: DAB_DEC(TY, 16)     \
+    case 32: DAB_DEC(TY, 32)     \
+    case 64: DAB_DEC(TY, 64)     \
+    case 128: DAB_DEC(TY, 128)   \
+    default: DAB_DEC(TY, 256)    \
+  }
+  switch (dtype) {
+    case F32: DAB_DEC_BD(float)
+    case F16: DAB_DEC_BD(__half)
+    case BF16: DAB_DEC_BD(__nv_bfloat16)
+    default: return cudaErrorInvalidValue;
+  }
+#undef DAB_DEC
+#undef DAB_DEC_BD
+}
+
+}  // namespace dab

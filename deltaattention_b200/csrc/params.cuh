@@ -1,0 +1,44 @@
+// Launch-parameter structs shared by the kernels and the C ABI layer.
+#pragma once
+#include "common.cuh"
+
+namespace dab {
+
+enum Variant : int { HYBRID = 0, SANITY = 1, PURE = 2, DENSE = 3 };
+
+// CUDA-core attention (any dtype / strides / block sizes, head_dim <= 128)
+struct SimtParams {
+  const void* q; const void* kd; const void* vd; const void* kp; const void* vp;
+  const int32_t* ts; const void* counts; void* out;
+  int64_t qs[4], kds[4], vds[4], kps[4], vps[4], tss[3], cs[3], os[4];
+  float sm_scale;
+  int64_t seq_q, seq_k, num_packed, head_dim, num_heads, dense_window;
+  int64_t grid_m, grid_bh, block_m, block_n;
+  int64_t kv_group;      // q-head h reads K/V/ts/counts of head h / kv_group
+  int counts_is_int;     // counts given as int32 (else fp32)
+  int causal;            // DENSE only
+  int variant;
+};
+
+// tcgen05 attention (bf16 / fp16, head_dim 64 or 128, 128x128 logical blocks)
+struct TcParams {
+  CUtensorMap tm_q, tm_kd, tm_vd, tm_kp, tm_vp;
+  void* out;
+  int64_t os_b, os_h, os_m;
+  const int32_t* ts;
+  int64_t ts_b, ts_h, ts_n;
+  const void* counts;
+  int64_t cs_b, cs_h, cs_n;
+  const int2* sched;       // [B*Hts][nmb] = (phase-1 blocks, dense start block)
+  const int32_t* blkmin;   // [B*Hts][nblk] smallest valid timestamp of each packed block
+  int* err;
+  float scale_log2;        // sm_scale * log2(e)
+  int seq_q, seq_k, num_packed;
+  int B, Hq, kv_group, Hts;
+  int nmb, nblk;
+  int variant, causal, counts_is_int, pair_heads;
+  int num_units;
+  int out_vec_ok;          // output rows are 16-byte aligned with unit d-stride
+};
+
+}  // namespace dab

@@ -1,0 +1,547 @@
+// Anchor selection, packing and RoPE kernels (HBM / latency bound integer+byte work).
+//
+//  * chunked_eval: the delta scan of tritonModules.py:7-69. One 8-lane group owns one
+//    chunk and walks it token by token; the squared distance / cosine is reduced in
+//    the reference's order (eight strided fp32 accumulators, then a pairwise tree,
+//    identical to numpy's summation that the Triton interpreter uses), so keep
+//    decisions are bit-exact with the reference.
+//  * scatter_pack: parallel_scatter_pack_kv_kernel (tritonModules.py:72-132).
+//  * rope: apply_rotary_pos_emb (modeling_llama.py:200-204) with eager rounding.
+//  * periodic_meta / keep-mask packing for the native path (modeling_llama.py:626-685
+//    without the host sync and without repeat_kv).
+#include "common.cuh"
+
+namespace dab {
+
+// ---------------------------------------------------------------------------------------
+// delta scan
+// ---------------------------------------------------------------------------------------
+template <typename T, int BD, bool COS>
+__global__ void __launch_bounds__(256) chunked_eval_kernel(
+    const T* __restrict__ x, int64_t xs_b, int64_t xs_h, int64_t xs_s, int64_t xs_d,
+    int32_t* __restrict__ keep, int64_t km_b, int64_t km_h, int64_t km_s,
+    int32_t* __restrict__ ccount, int64_t cc_b, int64_t cc_h, int64_t cc_c,
+    float thr, int64_t seq_len, int64_t head_dim, int64_t chunk_size, int64_t num_heads,
+    int64_t grid_bh, int64_t grid_chunks) {
+  constexpr int NH = BD > 128 ? 2 : 1;      // numpy splits n > 128 into two halves
+  constexpr int PER = BD / 8 / NH;          // elements per lane per half
+  const int lane = threadIdx.x & 31;
+  const int g = lane & 7;                   // lane within the 8-lane group
+  const unsigned gmask = 0xFFu << (lane & 24);
+  const int64_t chunk = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 3) + (threadIdx.x >> 3);
+  const int64_t bh = blockIdx.y;
+  if (chunk >= grid_chunks || bh >= grid_bh) return;
+  const int64_t b = bh / num_heads, h = bh % num_heads;
+  const int64_t start = chunk * chunk_size;
+  if (start >= seq_len) return;
+  const int64_t end = min(start + chunk_size, seq_len);
+  const T* row0 = x + b * xs_b + h * xs_h;
+  int32_t* krow = keep + b * km_b + h * km_h;
+
+  float ref[NH][PER], cur[NH][PER], nxt[NH][PER];
+  auto load = [&](int64_t pos, float (&dst)[NH][PER]) {
+    const T* r = row0 + pos * xs_s;
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh)
+#pragma unroll
+      for (int m = 0; m < PER; ++m) {
+        const int e = hh * 128 + g + 8 * m;
+        dst[hh][m] = (e < head_dim) ? to_f32(r[e * xs_d]) : 0.f;
+      }
+  };
+  auto tree = [&](float v) {
+    v = __fadd_rn(v, __shfl_xor_sync(gmask, v, 1));
+    v = __fadd_rn(v, __shfl_xor_sync(gmask, v, 2));
+    v = __fadd_rn(v, __shfl_xor_sync(gmask, v, 4));
+    return v;
+  };
+
+  load(start, ref);
+  if (g == 0) krow[start * km_s] = 1;
+  int local = 1;
+  if (start + 1 < end) load(start + 1, cur);
+  for (int64_t i = start + 1; i < end; ++i) {
+    if (i + 1 < end) load(i + 1, nxt);
+    bool kp;
+    if constexpr (COS) {
+      float dot = 0.f, cc = 0.f, rr = 0.f;
+#pragma unroll
+      for (int hh = 0; hh < NH; ++hh) {
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+#pragma unroll
+        for (int m = 0; m < PER; ++m) {
+          const float p0 = __fmul_rn(cur[hh][m], ref[hh][m]);
+          const float p1 = __fmul_rn(cur[hh][m], cur[hh][m]);
+          const float p2 = __fmul_rn(ref[hh][m], ref[hh][m]);
+          a0 = m ? __fadd_rn(a0, p0) : p0;
+          a1 = m ? __fadd_rn(a1, p1) : p1;
+          a2 = m ? __fadd_rn(a2, p2) : p2;
+        }
+        a0 = tree(a0);
+        a1 = tree(a1);
+        a2 = tree(a2);
+        dot = hh ? __fadd_rn(dot, a0) : a0;
+        cc = hh ? __fadd_rn(cc, a1) : a1;
+        rr = hh ? __fadd_rn(rr, a2) : a2;
+      }
+      const float nc = __fsqrt_rn(__fadd_rn(cc, 1e-8f));
+      const float nr = __fsqrt_rn(__fadd_rn(rr, 1e-8f));
+      const float cs = __fdiv_rn(dot, __fmul_rn(nc, nr));
+      kp = cs < thr;
+    } else {
+      float tot = 0.f;
+#pragma unroll
+      for (int hh = 0; hh < NH; ++hh) {
+        float acc = 0.f;
+#pragma unroll
+        for (int m = 0; m < PER; ++m) {
+          // elementwise ops round to the input dtype (fp32 math, then RNE)
+          const float d = round_as<T>(__fsub_rn(cur[hh][m], ref[hh][m]));
+          const float sq = round_as<T>(__fmul_rn(d, d));
+          acc = m ? __fadd_rn(acc, sq) : sq;
+        }
+        acc = tree(acc);
+        tot = hh ? __fadd_rn(tot, acc) : acc;
+      }
+      tot = round_as<T>(tot);
+      kp = tot > thr;
+    }
+    if (g == 0) krow[i * km_s] = kp ? 1 : 0;
+    if (kp) {
+#pragma unroll
+      for (int hh = 0; hh < NH; ++hh)
+#pragma unroll
+        for (int m = 0; m < PER; ++m) ref[hh][m] = cur[hh][m];
+      ++local;
+    }
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh)
+#pragma unroll
+      for (int m = 0; m < PER; ++m) cur[hh][m] = nxt[hh][m];
+  }
+  if (g == 0) ccount[b * cc_b + h * cc_h + chunk * cc_c] = local;
+}
+
+template <typename T, int BD, bool COS>
+static cudaError_t launch_chunked_eval_t(const void* x, const int64_t* xs, int32_t* keep, const int64_t* km,
+                                         int32_t* cc, const int64_t* ccs, float thr, int64_t seq_len,
+                                         int64_t head_dim, int64_t chunk_size, int64_t num_heads,
+                                         int64_t grid_bh, int64_t grid_chunks, cudaStream_t st) {
+  const int groups_per_block = 8;  // 64 threads
+  dim3 grid(static_cast<unsigned>((grid_chunks + groups_per_block - 1) / groups_per_block),
+            static_cast<unsigned>(grid_bh));
+  chunked_eval_kernel<T, BD, COS><<<grid, groups_per_block * 8, 0, st>>>(
+      static_cast<const T*>(x), xs[0], xs[1], xs[2], xs[3], keep, km[0], km[1], km[2], cc, ccs[0], ccs[1],
+      ccs[2], thr, seq_len, head_dim, chunk_size, num_heads, grid_bh, grid_chunks);
+  return cudaGetLastError();
+}
+
+template <typename T, bool COS>
+static cudaError_t launch_chunked_eval_bd(int bd, const void* x, const int64_t* xs, int32_t* keep,
+                                          const int64_t* km, int32_t* cc, const int64_t* ccs, float thr,
+                                          int64_t seq_len, int64_t head_dim, int64_t chunk_size,
+                                          int64_t num_heads, int64_t grid_bh, int64_t grid_chunks,
+                                          cudaStream_t st) {
+#define DAB_BD_CASE(N)                                                                                     \
+  case N:                                                                                                  \
+    return launch_chunked_eval_t<T, N, COS>(x, xs, keep, km, cc, ccs, thr, seq_len, head_dim, chunk_size, \
+                                            num_heads, grid_bh, grid_chunks, st);
+  switch (bd) {
+    DAB_BD_CASE(16)
+    DAB_BD_CASE(32)
+    DAB_BD_CASE(64)
+    DAB_BD_CASE(128)
+    DAB_BD_CASE(256)
+    default:
+      return cudaErrorInvalidValue;
+  }
+#undef DAB_BD_CASE
+}
+
+cudaError_t launch_chunked_eval(int dtype, int bd, bool cosine, const void* x, const int64_t* xs, int32_t* keep,
+                                const int64_t* km, int32_t* cc, const int64_t* ccs, float thr, int64_t seq_len,
+                                int64_t head_dim, int64_t chunk_size, int64_t num_heads, int64_t grid_bh,
+                                int64_t grid_chunks, cudaStream_t st) {
+  if (grid_bh <= 0 || grid_chunks <= 0) return cudaSuccess;
+  if (grid_bh > 65535) return cudaErrorInvalidValue;
+#define DAB_DT(TY)                                                                                           \
+  return cosine ? launch_chunked_eval_bd<TY, true>(bd, x, xs, keep, km, cc, ccs, thr, seq_len, head_dim,   \
+                                                   chunk_size, num_heads, grid_bh, grid_chunks, st)          \
+                : launch_chunked_eval_bd<TY, false>(bd, x, xs, keep, km, cc, ccs, thr, seq_len, head_dim,  \
+                                                    chunk_size, num_heads, grid_bh, grid_chunks, st);
+  switch (dtype) {
+    case F32: DAB_DT(float)
+    case F16: DAB_DT(__half)
+    case BF16: DAB_DT(__nv_bfloat16)
+    default: return cudaErrorInvalidValue;
+  }
+#undef DAB_DT
+}
+
+// ---------------------------------------------------------------------------------------
+// scatter pack (drop-in): for kept s, Kp[idx[s]] = K[s], Vp[idx[s]] = V[s], ts[idx[s]] = s
+// ---------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) scatter_pack_kernel(
+    const T* __restrict__ k, const int64_t* __restrict__ unused, const T* __restrict__ v, T* __restrict__ kp,
+    T* __restrict__ vp, int32_t* __restrict__ ts, const int32_t* __restrict__ km,
+    const int32_t* __restrict__ im, int64_t ks_b, int64_t ks_h, int64_t ks_s, int64_t ks_d, int64_t vs_b,
+    int64_t vs_h, int64_t vs_s, int64_t vs_d, int64_t kps_b, int64_t kps_h, int64_t kps_a, int64_t kps_d,
+    int64_t vps_b, int64_t vps_h, int64_t vps_a, int64_t vps_d, int64_t tss_b, int64_t tss_h, int64_t tss_a,
+    int64_t kms_b, int64_t kms_h, int64_t kms_s, int64_t ims_b, int64_t ims_h, int64_t ims_s, int64_t seq_len,
+    int64_t head_dim, int64_t num_heads, int64_t rows_covered, int64_t num_packed) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t s = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
+  const int64_t bh = blockIdx.y;
+  if (s >= seq_len || s >= rows_covered) return;
+  const int64_t b = bh / num_heads, h = bh % num_heads;
+  if (km[b * kms_b + h * kms_h + s * kms_s] != 1) return;
+  const int64_t dst = im[b * ims_b + h * ims_h + s * ims_s];
+  if (dst < 0 || dst >= num_packed) return;  // out-of-range destinations are dropped, not written
+  const T* krow = k + b * ks_b + h * ks_h + s * ks_s;
+  const T* vrow = v + b * vs_b + h * vs_h + s * vs_s;
+  T* kdst = kp + b * kps_b + h * kps_h + dst * kps_a;
+  T* vdst = vp + b * vps_b + h * vps_h + dst * vps_a;
+  for (int64_t d = lane; d < head_dim; d += 32) {
+    kdst[d * kps_d] = krow[d * ks_d];
+    vdst[d * vps_d] = vrow[d * vs_d];
+  }
+  if (lane == 0) ts[b * tss_b + h * tss_h + dst * tss_a] = static_cast<int32_t>(s);
+}
+
+cudaError_t launch_scatter_pack(int dtype, const void* k, const void* v, void* kp, void* vp, int32_t* ts,
+                                const int32_t* km, const int32_t* im, const int64_t* ks, const int64_t* vs,
+                                const int64_t* kps, const int64_t* vps, const int64_t* tss, const int64_t* kms,
+                                const int64_t* ims, int64_t seq_len, int64_t head_dim, int64_t num_heads,
+                                int64_t grid_bh, int64_t rows_covered, int64_t num_packed, cudaStream_t st) {
+  if (grid_bh <= 0 || rows_covered <= 0 || seq_len <= 0) return cudaSuccess;
+  const int64_t rows = rows_covered < seq_len ? rows_covered : seq_len;
+  dim3 grid(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(grid_bh));
+#define DAB_SP(TY)                                                                                           \
+  scatter_pack_kernel<TY><<<grid, 256, 0, st>>>(                                                             \
+      static_cast<const TY*>(k), nullptr, static_cast<const TY*>(v), static_cast<TY*>(kp),                   \
+      static_cast<TY*>(vp), ts, km, im, ks[0], ks[1], ks[2], ks[3], vs[0], vs[1], vs[2], vs[3], kps[0],      \
+      kps[1], kps[2], kps[3], vps[0], vps[1], vps[2], vps[3], tss[0], tss[1], tss[2], kms[0], kms[1], kms[2], \
+      ims[0], ims[1], ims[2], seq_len, head_dim, num_heads, rows_covered, num_packed);                       \
+  return cudaGetLastError();
+  switch (dtype) {
+    case F32: DAB_SP(float)
+    case F16: DAB_SP(__half)
+    case BF16: DAB_SP(__nv_bfloat16)
+    default: return cudaErrorInvalidValue;
+  }
+#undef DAB_SP
+}
+
+// ---------------------------------------------------------------------------------------
+// RoPE: out = round(round(x*cos) + round(rotate_half(x)*sin)), eager-torch rounding
+// ---------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) rope_kernel(const T* __restrict__ x, int64_t xb, int64_t xh, int64_t xs,
+                                                   int64_t xd, T* __restrict__ y, int64_t yb, int64_t yh,
+                                                   int64_t ys, int64_t yd, const T* __restrict__ cs,
+                                                   const T* __restrict__ sn, int64_t cb, int64_t cs_s,
+                                                   int64_t cd, int64_t H, int64_t N, int64_t D,
+                                                   int64_t total_rows) {
+  // one thread = one (row, i) pair with i < D/2: produces outputs i and i + D/2
+  const int64_t half = D / 2;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= total_rows * half) return;
+  const int64_t row = idx / half, i = idx % half;
+  const int64_t b = row / (H * N), rem = row % (H * N), h = rem / N, s = rem % N;
+  const T* xr = x + b * xb + h * xh + s * xs;
+  T* yr = y + b * yb + h * yh + s * ys;
+  const int64_t c0 = b * cb + s * cs_s;
+  const float x1 = to_f32(xr[i * xd]), x2 = to_f32(xr[(i + half) * xd]);
+  const float c1 = to_f32(cs[c0 + i * cd]), c2 = to_f32(cs[c0 + (i + half) * cd]);
+  const float s1 = to_f32(sn[c0 + i * cd]), s2 = to_f32(sn[c0 + (i + half) * cd]);
+  // rotate_half: [-x2, x1]
+  const float o1 = round_as<T>(__fadd_rn(round_as<T>(__fmul_rn(x1, c1)), round_as<T>(__fmul_rn(-x2, s1))));
+  const float o2 = round_as<T>(__fadd_rn(round_as<T>(__fmul_rn(x2, c2)), round_as<T>(__fmul_rn(x1, s2))));
+  yr[i * yd] = from_f32<T>(o1);
+  yr[(i + half) * yd] = from_f32<T>(o2);
+}
+
+cudaError_t launch_rope(int dtype, const void* x, const int64_t* xs, void* y, const int64_t* ys, const void* cs,
+                        const void* sn, const int64_t* css, int64_t B, int64_t H, int64_t N, int64_t D,
+                        cudaStream_t st) {
+  const int64_t rows = B * H * N;
+  if (rows == 0) return cudaSuccess;
+  if (D % 2) return cudaErrorInvalidValue;
+  const int64_t work = rows * (D / 2);
+  const unsigned blocks = static_cast<unsigned>((work + 255) / 256);
+#define DAB_RP(TY)                                                                                              \
+  rope_kernel<TY><<<blocks, 256, 0, st>>>(static_cast<const TY*>(x), xs[0], xs[1], xs[2], xs[3],               \
+                                          static_cast<TY*>(y), ys[0], ys[1], ys[2], ys[3],                     \
+                                          static_cast<const TY*>(cs), static_cast<const TY*>(sn), css[0],       \
+                                          css[1], css[2], H, N, D, rows);                                       \
+  return cudaGetLastError();
+  switch (dtype) {
+    case F32: DAB_RP(float)
+    case F16: DAB_RP(__half)
+    case BF16: DAB_RP(__nv_bfloat16)
+    default: return cudaErrorInvalidValue;
+  }
+#undef DAB_RP
+}
+
+// ---------------------------------------------------------------------------------------
+// periodic packing metadata: anchor j sits at j*period and covers min(period, N - j*period)
+// tokens (modeling_llama.py:626-632 + :655-685 for keep = t % period == 0)
+// ---------------------------------------------------------------------------------------
+__global__ void periodic_meta_kernel(int32_t* ts, int32_t* counts, int64_t BH, int64_t M, int64_t N,
+                                     int64_t period) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= BH * M) return;
+  const int64_t j = idx % M;
+  const int64_t p = j * period;
+  ts[idx] = static_cast<int32_t>(p);
+  counts[idx] = static_cast<int32_t>(min(period, N - p));
+}
+
+cudaError_t launch_periodic_meta(int32_t* ts, int32_t* counts, int64_t BH, int64_t M, int64_t N, int64_t period,
+                                 cudaStream_t st) {
+  if (BH * M == 0) return cudaSuccess;
+  periodic_meta_kernel<<<static_cast<unsigned>((BH * M + 255) / 256), 256, 0, st>>>(ts, counts, BH, M, N, period);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------
+// device-side packing from a keep mask (native path: no host sync, no repeat_kv)
+//   pass 1: per (head, 1024-token tile) kept counts
+//   pass 2: per head exclusive scan over tiles, anchors per head, first kept per tile
+//   pass 3: per tile local scan -> index map, scatter K/V/ts, run-length counts
+// ---------------------------------------------------------------------------------------
+constexpr int PACK_TILE = 1024;
+
+__global__ void __launch_bounds__(PACK_TILE) keep_tile_count_kernel(const int32_t* __restrict__ keep,
+                                                                    int64_t kb, int64_t kh, int64_t ks,
+                                                                    int64_t H, int64_t N, int32_t* tile_cnt,
+                                                                    int32_t* tile_first, int64_t ntile) {
+  const int64_t bh = blockIdx.y, t = blockIdx.x;
+  const int64_t b = bh / H, h = bh % H;
+  const int64_t s = t * PACK_TILE + threadIdx.x;
+  const int kv = (s < N) ? (keep[b * kb + h * kh + s * ks] == 1) : 0;
+  const int c = __syncthreads_count(kv);
+  __shared__ int first;
+  if (threadIdx.x == 0) first = INT32_MAX;
+  __syncthreads();
+  if (kv) atomicMin(&first, static_cast<int>(s));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    tile_cnt[bh * ntile + t] = c;
+    tile_first[bh * ntile + t] = first;
+  }
+}
+
+// one block per head: exclusive scan of tile counts; next_first[t] = first kept position
+// strictly after tile t (or N); anchors[bh] = total kept; atomicMax into *max_anchors
+__global__ void __launch_bounds__(1024) keep_tile_scan_kernel(int32_t* tile_cnt, int32_t* tile_first,
+                                                              int32_t* tile_off, int32_t* next_first,
+                                                              int32_t* anchors, int32_t* max_anchors,
+                                                              int64_t ntile, int64_t N) {
+  const int64_t bh = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int32_t run = 0;
+    for (int64_t t = 0; t < ntile; ++t) {
+      tile_off[bh * ntile + t] = run;
+      run += tile_cnt[bh * ntile + t];
+    }
+    int32_t nf = static_cast<int32_t>(N);
+    for (int64_t t = ntile - 1; t >= 0; --t) {
+      next_first[bh * ntile + t] = nf;
+      const int32_t f = tile_first[bh * ntile + t];
+      if (f != INT32_MAX) nf = f;
+    }
+    anchors[bh] = run;
+    atomicMax(max_anchors, run);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(PACK_TILE) keep_pack_kernel(
+    const int32_t* __restrict__ keep, int64_t kb, int64_t kh, int64_t ks, const T* __restrict__ k, int64_t xb,
+    int64_t xh, int64_t xs, const T* __restrict__ v, int64_t vb, int64_t vh, int64_t vs, T* __restrict__ kp,
+    T* __restrict__ vp, int64_t pb, int64_t ph, int64_t ps, int32_t* __restrict__ ts, int32_t* __restrict__ counts,
+    int64_t mb, int64_t mh, int32_t* __restrict__ index_map, const int32_t* tile_off, const int32_t* next_first,
+    int64_t H, int64_t N, int64_t D, int64_t ntile, int64_t capacity) {
+  __shared__ int32_t warp_off[PACK_TILE / 32];
+  __shared__ int32_t pos_of[PACK_TILE];
+  __shared__ int32_t total;
+  const int64_t bh = blockIdx.y, t = blockIdx.x;
+  const int64_t b = bh / H, h = bh % H;
+  const int64_t s = t * PACK_TILE + threadIdx.x;
+  const int kv = (s < N) ? (keep[b * kb + h * kh + s * ks] == 1) : 0;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned bal = __ballot_sync(0xFFFFFFFFu, kv);
+  const int in_warp = __popc(bal & ((1u << lane) - 1));
+  if (lane == 0) warp_off[warp] = __popc(bal);
+  __syncthreads();
+  if (warp == 0) {
+    const int v0 = warp_off[lane];
+    int incl = v0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    warp_off[lane] = incl - v0;
+    if (lane == 31) total = incl;
+  }
+  __syncthreads();
+  const int local = warp_off[warp] + in_warp;  // exclusive index of s among kept positions of the tile
+  const int32_t base = tile_off[bh * ntile + t];
+  const int32_t j = base + local;               // packed slot of s when kept
+  if (s < N && index_map) index_map[bh * N + s] = j + kv - 1;  // cumsum(keep) - 1
+  if (kv) pos_of[local] = static_cast<int32_t>(s);
+  __syncthreads();
+  if (kv && j < capacity) {
+    // run length: distance to the next anchor (or to N after the last one)
+    const int32_t nxt = (local + 1 < total) ? pos_of[local + 1] : next_first[bh * ntile + t];
+    ts[b * mb + h * mh + j] = static_cast<int32_t>(s);
+    counts[b * mb + h * mh + j] = nxt - static_cast<int32_t>(s);
+  }
+  // each warp copies the K/V rows of its kept lanes
+  for (unsigned m = bal; m; m &= m - 1) {
+    const int src = __ffs(m) - 1;
+    const int64_t ss = t * PACK_TILE + warp * 32 + src;
+    const int32_t jj = __shfl_sync(0xFFFFFFFFu, j, src);
+    if (jj >= capacity) continue;
+    const T* kr = k + b * xb + h * xh + ss * xs;
+    const T* vr = v + b * vb + h * vh + ss * vs;
+    T* kd = kp + b * pb + h * ph + static_cast<int64_t>(jj) * ps;
+    T* vd = vp + b * pb + h * ph + static_cast<int64_t>(jj) * ps;
+    for (int64_t d = lane; d < D; d += 32) {
+      kd[d] = kr[d];
+      vd[d] = vr[d];
+    }
+  }
+}
+
+cudaError_t launch_pack_from_keep(int dtype, const int32_t* keep, const int64_t* kms, const void* k,
+                                  const int64_t* xs, const void* v, const int64_t* vs, void* kp, void* vp,
+                                  const int64_t* ps, int32_t* ts, int32_t* counts, const int64_t* ms,
+                                  int32_t* index_map, int64_t B, int64_t H, int64_t N, int64_t D,
+                                  int64_t capacity, int32_t* ws, int32_t* anchors, int32_t* max_anchors,
+                                  cudaStream_t st) {
+  const int64_t ntile = (N + PACK_TILE - 1) / PACK_TILE;
+  const int64_t BH = B * H;
+  if (BH == 0 || N == 0) return cudaSuccess;
+  int32_t* tile_cnt = ws;
+  int32_t* tile_first = ws + BH * ntile;
+  int32_t* tile_off = ws + 2 * BH * ntile;
+  int32_t* next_first = ws + 3 * BH * ntile;
+  cudaMemsetAsync(max_anchors, 0, sizeof(int32_t), st);
+  keep_tile_count_kernel<<<dim3(static_cast<unsigned>(ntile), static_cast<unsigned>(BH)), PACK_TILE, 0, st>>>(
+      keep, kms[0], kms[1], kms[2], H, N, tile_cnt, tile_first, ntile);
+  keep_tile_scan_kernel<<<static_cast<unsigned>(BH), 32, 0, st>>>(tile_cnt, tile_first, tile_off, next_first,
+                                                                  anchors, max_anchors, ntile, N);
+#define DAB_KP(TY)                                                                                           \
+  keep_pack_kernel<TY><<<dim3(static_cast<unsigned>(ntile), static_cast<unsigned>(BH)), PACK_TILE, 0, st>>>( \
+      keep, kms[0], kms[1], kms[2], static_cast<const TY*>(k), xs[0], xs[1], xs[2],                         \
+      static_cast<const TY*>(v), vs[0], vs[1], vs[2], static_cast<TY*>(kp), static_cast<TY*>(vp), ps[0],     \
+      ps[1], ps[2], ts, counts, ms[0], ms[1], index_map, tile_off, next_first, H, N, D, ntile, capacity);    \
+  return cudaGetLastError();
+  switch (dtype) {
+    case F32: DAB_KP(float)
+    case F16: DAB_KP(__half)
+    case BF16: DAB_KP(__nv_bfloat16)
+    default: return cudaErrorInvalidValue;
+  }
+#undef DAB_KP
+}
+
+// ---------------------------------------------------------------------------------------
+// N:M structured selection (builder-specified: the reference ships no source for it).
+// Candidates are positions t = i*c; candidate i scores +inf (i == 0) or the fp32 squared
+// distance between K[t] and K[t-c] (numpy summation order). Each run of m consecutive
+// candidates keeps its min(n, size) best (ties to the earlier position). One thread owns
+// one group and writes the keep mask of every position the group spans.
+// ---------------------------------------------------------------------------------------
+template <typename T, int BD>
+__global__ void __launch_bounds__(128) nm_select_kernel(const T* __restrict__ x, int64_t xb, int64_t xh, int64_t xs,
+                                                        int64_t xd, int32_t* __restrict__ keep, int64_t kb,
+                                                        int64_t kh, int64_t ks, int64_t H, int64_t N, int64_t D,
+                                                        int n_keep, int m_group, int64_t c, int64_t groups) {
+  constexpr int NH = BD > 128 ? 2 : 1;
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t bh = blockIdx.y;
+  if (gid >= groups) return;
+  const int64_t b = bh / H, h = bh % H;
+  const T* base = x + b * xb + h * xh;
+  int32_t* kr = keep + b * kb + h * kh;
+  const int64_t G = (N + c - 1) / c;  // candidates
+  const int64_t i0 = gid * m_group;
+  const int64_t left = G - i0;
+  const int size = static_cast<int>(left < m_group ? left : m_group);
+  float sc[16];
+  for (int a = 0; a < size; ++a) {
+    const int64_t i = i0 + a;
+    if (i == 0) { sc[a] = INFINITY; continue; }
+    const T* r1 = base + i * c * xs;
+    const T* r0 = base + (i * c - c) * xs;
+    float tot = 0.f;
+    for (int hh = 0; hh < NH; ++hh) {
+      float r[8];
+      for (int k = 0; k < 8; ++k) {
+        float acc = 0.f;
+        for (int mm = 0; mm < BD / 8 / NH; ++mm) {
+          const int e = hh * 128 + k + 8 * mm;
+          const float d = (e < D) ? __fsub_rn(to_f32(r1[e * xd]), to_f32(r0[e * xd])) : 0.f;
+          const float sq = __fmul_rn(d, d);
+          acc = mm ? __fadd_rn(acc, sq) : sq;
+        }
+        r[k] = acc;
+      }
+      const float t = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
+                                __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
+      tot = hh ? __fadd_rn(tot, t) : t;
+    }
+    sc[a] = tot;
+  }
+  const int nk = min(n_keep, size);
+  const int64_t p0 = i0 * c;
+  const int64_t p1e = (i0 + size) * c;
+  const int64_t p1 = p1e < N ? p1e : N;
+  for (int64_t p = p0; p < p1; ++p) kr[p * ks] = 0;
+  for (int a = 0; a < size; ++a) {
+    int rank = 0;
+    for (int o = 0; o < size; ++o) rank += (sc[o] > sc[a]) || (sc[o] == sc[a] && o < a);
+    if (rank < nk) kr[(i0 + a) * c * ks] = 1;
+  }
+}
+
+cudaError_t launch_nm_select(int dtype, const void* x, const int64_t* xs, int32_t* keep, const int64_t* kms,
+                             int64_t B, int64_t H, int64_t N, int64_t D, int n_keep, int m_group, int64_t c,
+                             cudaStream_t st) {
+  if (B * H == 0 || N == 0) return cudaSuccess;
+  if (m_group < 1 || m_group > 16 || n_keep < 1 || c < 1) return cudaErrorInvalidValue;
+  int bd = 16;
+  while (bd < D) bd <<= 1;
+  if (bd > 256) return cudaErrorInvalidValue;
+  const int64_t G = (N + c - 1) / c;
+  const int64_t groups = (G + m_group - 1) / m_group;
+  dim3 grid(static_cast<unsigned>((groups + 127) / 128), static_cast<unsigned>(B * H));
+#define DAB_NM(TY, BDV)                                                                                      \
+  nm_select_kernel<TY, BDV><<<grid, 128, 0, st>>>(static_cast<const TY*>(x), xs[0], xs[1], xs[2], xs[3], keep, \
+                                                  kms[0], kms[1], kms[2], H, N, D, n_keep, m_group, c, groups); \
+  return cudaGetLastError();
+#define DAB_NM_BD(TY)                                                                                 \
+  switch (bd) {                                                                                       \
+    case 16: DAB_NM(TY, 16)                                                                           \
+    case 32: DAB_NM(TY, 32)                                                                           \
+    case 64: DAB_NM(TY, 64)                                                                           \
+    case 128: DAB_NM(TY, 128)                                                                         \
+    default: DAB_NM(TY, 256)                                                                          \
+  }
+  switch (dtype) {
+    case F32: DAB_NM_BD(float)
+    case F16: DAB_NM_BD(__half)
+    case BF16: DAB_NM_BD(__nv_bfloat16)
+    default: return cudaErrorInvalidValue;
+  }
+#undef DAB_NM
+#undef DAB_NM_BD
+}
+
+}  // namespace dab

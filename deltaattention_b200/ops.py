@@ -1,0 +1,226 @@
+"""Native B200 entry points for the delta-attention prefill path.
+
+``delta_prefill`` runs the whole hot path the reference spreads over
+modeling_llama.py:555 and :600-749 (RoPE, anchor selection, index map, packing, counts,
+GQA expansion, two-phase attention) with these B200-specific changes:
+
+* GQA is index arithmetic (q-head h reads kv-head h // n_rep): the six ``repeat_kv`` copies
+  of modeling_llama.py:700-708 are gone;
+* periodic packing is a strided view of the rotated keys / values (row stride x period), so
+  nothing is copied; timestamps and counts come from one tiny kernel;
+* delta / explicit keep masks pack on the device; the only host sync is the reference's
+  own read of the packed length (modeling_llama.py:656);
+* the output can be written straight into the ``[B, N, H, d]`` layout ``o_proj`` consumes.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+
+VARIANTS = {"hybrid": 0, "sanity": 1, "pure_phase1": 2}
+
+
+def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: Optional[torch.Tensor] = None):
+    """``apply_rotary_pos_emb`` for one [B, H, N, d] tensor (modeling_llama.py:180-204).
+
+    cos / sin are [B or 1, N, d] in x's dtype; rounding follows eager torch exactly.
+    """
+    L.require_cuda(x, cos, sin)
+    B, H, N, D = x.shape
+    if out is None:
+        out = torch.empty((B, H, N, D), dtype=x.dtype, device=x.device)
+    cb = cos.stride(0) if cos.shape[0] > 1 else 0
+    if cos.stride() != sin.stride():
+        sin = sin.contiguous()
+        cos = cos.contiguous()
+        cb = cos.stride(0) if cos.shape[0] > 1 else 0
+    st = L.stream_of(x)
+    L.check(L.load().dab_rope(L.ptr(x), L.strides(x.stride()), L.ptr(out), L.strides(out.stride()), L.ptr(cos),
+                              L.ptr(sin), L.strides([cb, cos.stride(1), cos.stride(2)]), L.dtype_code(x), B, H, N,
+                              D, st), "rope")
+    return out
+
+
+@dataclass
+class Packed:
+    """Packed history of one layer: K/V rows, anchor timestamps and run-length counts."""
+    k: torch.Tensor          # [B, Hkv, M, d] (possibly a strided view)
+    v: torch.Tensor
+    timestamps: torch.Tensor  # [B, Hkv, M] int32
+    counts: torch.Tensor      # [B, Hkv, M] int32
+    keep_mask: Optional[torch.Tensor] = None
+
+
+def pack_periodic(k_rot: torch.Tensor, v: torch.Tensor, period: int) -> Packed:
+    """Periodic packing (modeling_llama.py:626-632 + :655-685) without copies."""
+    B, H, N, D = k_rot.shape
+    M = -(-N // period)
+    ts = torch.empty((B, H, M), dtype=torch.int32, device=k_rot.device)
+    cnt = torch.empty_like(ts)
+    st = L.stream_of(k_rot)
+    L.check(L.load().dab_periodic_meta(L.ptr(ts), L.ptr(cnt), B * H, M, N, period, st), "periodic_meta")
+    return Packed(k_rot[:, :, ::period], v[:, :, ::period], ts, cnt)
+
+
+def delta_keep_mask(k_rot: torch.Tensor, threshold: float, similarity: str = "euclidean", chunk_size: int = 512):
+    """Delta selection (modeling_llama.py:634-653): keep mask and per-chunk anchor counts.
+
+    ``threshold`` is the raw threshold; like the reference, only ``similarity == 'cosine'``
+    selects cosine, every other value selects squared Euclidean with threshold**2.
+    """
+    from .launch import chunked_eval_kernel
+    B, H, N, D = k_rot.shape
+    cs = min(chunk_size, N) if chunk_size > 0 else N
+    nch = max(1, -(-N // cs))
+    use_cos = similarity == "cosine"
+    thr = threshold if use_cos else threshold ** 2
+    keep = torch.zeros((B, H, N), dtype=torch.int32, device=k_rot.device)
+    cc = torch.zeros((B, H, nch), dtype=torch.int32, device=k_rot.device)
+    bd = 1 << max(4, (D - 1).bit_length())
+    chunked_eval_kernel[(B * H, nch)](
+        k_rot, keep, cc, thr, *k_rot.stride(), *keep.stride(), *cc.stride(), N, D, cs, num_heads=H,
+        BLOCK_D=bd, USE_COSINE=use_cos)
+    return keep, cc
+
+
+def pack_from_keep(k_rot: torch.Tensor, v: torch.Tensor, keep: torch.Tensor, num_packed: Optional[int] = None,
+                   want_index_map: bool = False) -> Packed:
+    """Device-side index map + scatter + counts (modeling_llama.py:655-685)."""
+    B, H, N, D = k_rot.shape
+    if num_packed is None:
+        num_packed = int(keep.sum(-1).max().item())  # the reference's packed length (modeling_llama.py:656)
+    M = int(num_packed)
+    dev = k_rot.device
+    kp = torch.zeros((B, H, M, D), dtype=k_rot.dtype, device=dev)
+    vp = torch.zeros_like(kp)
+    ts = torch.zeros((B, H, M), dtype=torch.int32, device=dev)
+    cnt = torch.zeros_like(ts)
+    anchors = torch.zeros((B * H,), dtype=torch.int32, device=dev)
+    mx = torch.zeros((1,), dtype=torch.int32, device=dev)
+    im = torch.empty((B, H, N), dtype=torch.int32, device=dev) if want_index_map else None
+    lib = L.load()
+    st = L.stream_of(k_rot)
+    wsb = lib.dab_pack_from_keep_workspace_size(B, H, N)
+    ws = torch.empty(max(int(wsb), 16), dtype=torch.uint8, device=dev)
+    L.check(lib.dab_pack_from_keep(
+        L.ptr(keep), L.strides(keep.stride()), L.ptr(k_rot), L.strides(k_rot.stride()), L.ptr(v),
+        L.strides(v.stride()), L.ptr(kp), L.ptr(vp), L.strides(kp.stride()), L.ptr(ts), L.ptr(cnt),
+        L.strides(ts.stride()), L.ptr(im), L.dtype_code(k_rot), B, H, N, D, M, L.ptr(anchors), L.ptr(mx),
+        L.ptr(ws), ws.numel(), st), "pack_from_keep")
+    p = Packed(kp, vp, ts, cnt, keep)
+    p.index_map = im
+    return p
+
+
+def attention(q_rot, k_rot, v, packed: Optional[Packed], *, sm_scale=None, dense_window=128,
+              variant="hybrid", out=None, force_simt=False):
+    """Two-phase count-weighted attention (deltaFlashAttention.py:9-357) with GQA by index.
+
+    q_rot [B, Hq, N, d]; k_rot / v / packed tensors [B, Hkv, ...]; out any [B, Hq, N, d] view.
+    """
+    B, Hq, N, D = q_rot.shape
+    Hkv = k_rot.shape[1]
+    if Hq % Hkv:
+        raise ValueError("query heads must be a multiple of kv heads")
+    if sm_scale is None:
+        sm_scale = D ** -0.5
+    if out is None:
+        out = torch.empty((B, Hq, N, D), dtype=q_rot.dtype, device=q_rot.device)
+    M = packed.k.shape[2] if packed is not None else 0
+    kp = packed.k if packed is not None else k_rot
+    vp = packed.v if packed is not None else v
+    ts = packed.timestamps if packed is not None else torch.zeros((B, Hkv, 1), dtype=torch.int32,
+                                                                   device=q_rot.device)
+    cnt = packed.counts if packed is not None else ts
+    lib = L.load()
+    st = L.stream_of(q_rot)
+    wsb = lib.dab_hybrid_flash_workspace_size(B, Hkv, N, M)
+    ws = L.workspace(q_rot.device, st.value, wsb)
+    bd = 1 << max(4, (D - 1).bit_length())
+    strides = [*q_rot.stride(), *k_rot.stride(), *v.stride(), *kp.stride(), *vp.stride(), *ts.stride(),
+               *cnt.stride(), *out.stride()]
+    L.check(lib.dab_hybrid_flash(
+        VARIANTS[variant], L.ptr(q_rot), L.ptr(k_rot), L.ptr(v), L.ptr(kp), L.ptr(vp), L.ptr(ts), L.ptr(cnt),
+        1 if cnt.dtype == torch.int32 else 0, L.ptr(out), L.dtype_code(q_rot), L.strides(strides), float(sm_scale),
+        N, k_rot.shape[2], M, D, Hq, int(dense_window), -(-N // 128), B * Hq, 128, 128, bd, Hq // Hkv, L.ptr(ws),
+        ws.numel(), 1 if force_simt else 0, st), "attention")
+    return out
+
+
+def flash(q_rot, k_rot, v, *, causal=True, sm_scale=None, out=None, force_simt=False):
+    """Dense flash attention (flashAttention.py:5-91) with GQA by index: the r = 1 comparator."""
+    B, Hq, N, D = q_rot.shape
+    Hkv = k_rot.shape[1]
+    if sm_scale is None:
+        sm_scale = D ** -0.5
+    if out is None:
+        out = torch.empty((B, Hq, N, D), dtype=q_rot.dtype, device=q_rot.device)
+    lib = L.load()
+    st = L.stream_of(q_rot)
+    wsb = lib.dab_hybrid_flash_workspace_size(B, Hkv, N, 0)
+    ws = L.workspace(q_rot.device, st.value, wsb)
+    strides = [*q_rot.stride(), *k_rot.stride(), *v.stride(), *out.stride()]
+    L.check(lib.dab_attn_fwd_flat(
+        L.ptr(q_rot), L.ptr(k_rot), L.ptr(v), float(sm_scale), L.ptr(out), L.dtype_code(q_rot), L.strides(strides),
+        B, Hq, N, D, 128, 128, 1 if causal else 0, -(-N // 128), B * Hq, Hq // Hkv, L.ptr(ws), ws.numel(),
+        1 if force_simt else 0, st), "flash")
+    return out
+
+
+def delta_prefill(q, k, v, cos, sin, *, mode="periodic", keep_rate=0.25, threshold=None,
+                  similarity="euclidean", chunk_size=512, dense_window=128, variant="hybrid", sm_scale=None,
+                  out=None, keep_mask=None, return_packed=False):
+    """The whole delta-attention prefill layer-op on pre-RoPE q / k and v.
+
+    q [B, Hq, N, d], k / v [B, Hkv, N, d] (any strides, e.g. the [B, N, H, d] projection
+    layout viewed with transpose(1, 2)). mode: 'periodic' (keep t % round(1/keep_rate) == 0),
+    'delta' (threshold selection in chunks of ``chunk_size``) or 'mask' (``keep_mask``).
+    Returns the attention output [B, Hq, N, d] (and the packed history when requested).
+    """
+    q_rot = rope(q, cos, sin)
+    k_rot = rope(k, cos, sin)
+    if mode == "periodic":
+        period = max(1, round(1.0 / keep_rate))
+        packed = pack_periodic(k_rot, v, period)
+    elif mode == "delta":
+        if threshold is None:
+            raise ValueError("delta mode needs a threshold")
+        keep, _ = delta_keep_mask(k_rot, threshold, similarity, chunk_size)
+        packed = pack_from_keep(k_rot, v, keep)
+    elif mode == "mask":
+        packed = pack_from_keep(k_rot, v, keep_mask.to(torch.int32))
+    else:
+        raise ValueError(f"unknown mode {mode}")
+    o = attention(q_rot, k_rot, v, packed, sm_scale=sm_scale, dense_window=dense_window, variant=variant, out=out)
+    if return_packed:
+        return o, packed, k_rot
+    return o
+
+
+def tile_count_periodic(N: int, r: int, W: int = 128) -> int:
+    """128x128 tiles one head runs under the reference schedule with periodic-r packing."""
+    nb = -(-N // 128)
+    if r == 1:
+        return nb * (nb + 1) // 2
+    M = -(-N // r)
+    nblk = -(-M // 128)
+    T = [min(128 * j + 127, M - 1) * r if 128 * j + 127 < M else N + 1 for j in range(nblk)]
+    tot = 0
+    for mb in range(nb):
+        thr = 128 * mb - W
+        n1 = 0
+        while n1 < nblk and T[n1] < thr:
+            n1 += 1
+        last = T[n1 - 1] if n1 else -1
+        ds = max(0, (last + 1) // 128)
+        de = -(-min(N, 128 * mb + 128) // 128)
+        tot += n1 + max(0, de - ds)
+    return tot
+
+
+_ = math

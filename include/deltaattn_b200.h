@@ -1,0 +1,177 @@
+/* deltaattn_b200.h - C ABI of the B200 (sm_100a) DeltaAttention hot-path library.
+ *
+ * Conventions shared by every entry point:
+ *   - pointers are device pointers; strides are in ELEMENTS, one int64 per dimension, in
+ *     the same order as the reference kernel's stride arguments;
+ *   - `dtype` is DAB_F32, DAB_F16 or DAB_BF16 and applies to the float tensors;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); every call is
+ *     asynchronous on it and allocates no device memory;
+ *   - the return value is 0 on success; otherwise dab_last_error() describes the failure
+ *     (its text contains "CUDA" when a CUDA call failed, matching the reference's
+ *     classifier at eval_speedup.py:119-123).
+ * Reference citations are file:line in the DeltaAttention project.
+ */
+#ifndef DELTAATTN_B200_H
+#define DELTAATTN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DAB_F32 0
+#define DAB_F16 1
+#define DAB_BF16 2
+
+#define DAB_HYBRID 0      /* hybrid_compressed_flash_kernel         deltaFlashAttention.py:9-146   */
+#define DAB_SANITY 1      /* hybrid_compressed_flash_kernel_sanity  deltaFlashAttention.py:149-259 */
+#define DAB_PURE_PHASE1 2 /* pure_phase1_flash_kernel               deltaFlashAttention.py:262-357 */
+
+/* Message of the last failing call on this thread. */
+const char* dab_last_error(void);
+/* ABI revision of this header (1). */
+int dab_abi_version(void);
+
+/* Makes `device` current for this library's CUDA runtime on the calling thread (callers
+ * that switch devices with another runtime instance call this before launching). */
+int dab_set_device(int device);
+
+/* Reads and clears the device error word at the start of an attention workspace (a bounded
+ * in-kernel wait that timed out records a nonzero code there). Synchronises `stream`. */
+int dab_workspace_error(void* workspace, int* code, void* stream);
+
+/* chunked_eval_kernel[grid](in_ptr, keep_mask_ptr, chunk_counts_ptr, threshold_sq,
+ *   stride_in_*(4), stride_km_*(3), stride_cc_*(3), seq_len, head_dim, chunk_size,
+ *   num_heads, BLOCK_D, USE_COSINE) - tritonModules.py:7-69, launched at
+ * modeling_llama.py:643-652 with grid (grid_bh, grid_chunks). Keep decisions are bit-exact
+ * with the reference (same reduction order). */
+int dab_chunked_eval(const void* in, int dtype, const int64_t* in_strides, int32_t* keep_mask,
+                     const int64_t* km_strides, int32_t* chunk_counts, const int64_t* cc_strides,
+                     float threshold, int64_t seq_len, int64_t head_dim, int64_t chunk_size,
+                     int64_t num_heads, int64_t grid_bh, int64_t grid_chunks, int64_t block_d,
+                     int use_cosine, void* stream);
+
+/* parallel_scatter_pack_kv_kernel[grid](k_in, v_in, k_packed, v_packed, pt, keep_mask,
+ *   index_map, strides k(4) v(4) kp(4) vp(4) pt(3) km(3) im(3), seq_len, head_dim,
+ *   num_heads, BLOCK_S, BLOCK_D) - tritonModules.py:72-132, launched at
+ * modeling_llama.py:667-680 with grid (grid_bh, grid_s). `num_packed` is the packed row
+ * count (destinations outside [0, num_packed) are skipped instead of written). */
+int dab_parallel_scatter_pack_kv(const void* k_in, const void* v_in, void* k_packed, void* v_packed,
+                                 int32_t* packed_ts, const int32_t* keep_mask, const int32_t* index_map,
+                                 int dtype, const int64_t* k_strides, const int64_t* v_strides,
+                                 const int64_t* kp_strides, const int64_t* vp_strides,
+                                 const int64_t* ts_strides, const int64_t* km_strides,
+                                 const int64_t* im_strides, int64_t seq_len, int64_t head_dim,
+                                 int64_t num_heads, int64_t num_packed, int64_t grid_bh, int64_t grid_s,
+                                 int64_t block_s, void* stream);
+
+/* Scratch bytes dab_hybrid_flash / dab_attn_fwd_flat need (batch, heads of the timestamp
+ * tensor, query length, packed length). */
+size_t dab_hybrid_flash_workspace_size(int64_t batch, int64_t ts_heads, int64_t seq_len_q, int64_t num_packed);
+
+/* hybrid_compressed_flash_kernel / _sanity / pure_phase1_flash_kernel[grid](Q, K_dense,
+ *   V_dense, K_packed, V_packed, Packed_Timestamps, Packed_Counts, Out, 30 strides in the
+ *   reference order (q, kd, vd, kp, vp: 4 each; ts, counts: 3 each; out: 4), sm_scale,
+ *   seq_len_q, seq_len_k, num_packed_keys, head_dim, num_heads, denseWindowSize,
+ *   BLOCK_M, BLOCK_N, BLOCK_D) - deltaFlashAttention.py:9-357, wrappers at
+ * modeling_llama.py:306-451, grid (grid_m, grid_bh).
+ * Extensions: `counts_is_int` (counts given as int32 rather than the wrapper's fp32);
+ * `kv_group` (q-head h reads K/V/timestamps/counts of head h / kv_group, which replaces the
+ * repeat_kv copies of modeling_llama.py:700-708; 1 = the reference's expanded call);
+ * `force_simt` (use the CUDA-core kernel even when the tcgen05 kernel applies).
+ * bf16/fp16 with head_dim 64/128 and 128x128 blocks run on tcgen05; everything else on the
+ * CUDA-core kernel. */
+int dab_hybrid_flash(int variant, const void* q, const void* k_dense, const void* v_dense,
+                     const void* k_packed, const void* v_packed, const int32_t* packed_ts,
+                     const void* packed_counts, int counts_is_int, void* out, int dtype,
+                     const int64_t* strides, float sm_scale, int64_t seq_len_q, int64_t seq_len_k,
+                     int64_t num_packed, int64_t head_dim, int64_t num_heads, int64_t dense_window,
+                     int64_t grid_m, int64_t grid_bh, int64_t block_m, int64_t block_n, int64_t block_d,
+                     int64_t kv_group, void* workspace, size_t workspace_bytes, int force_simt, void* stream);
+
+/* _attn_fwd_flat[grid](Q, K, V, sm_scale, Out, 16 strides (q, k, v, out), Z, H, N_CTX,
+ *   HEAD_DIM, BLOCK_M, BLOCK_N, IS_CAUSAL) - flashAttention.py:5-91, wrapper
+ * triton_flash_attention flashAttention.py:94-130, grid (grid_m, grid_zh). */
+int dab_attn_fwd_flat(const void* q, const void* k, const void* v, float sm_scale, void* out, int dtype,
+                      const int64_t* strides, int64_t Z, int64_t H, int64_t n_ctx, int64_t head_dim,
+                      int64_t block_m, int64_t block_n, int is_causal, int64_t grid_m, int64_t grid_zh,
+                      int64_t kv_group, void* workspace, size_t workspace_bytes, int force_simt, void* stream);
+
+/* fused_hybrid_decode_update_kernel[(programs,)](new_k, new_v, k_exact, v_exact, k_packed,
+ *   v_packed, packed_counts, packed_timestamps, packed_lengths, exact_seq_len,
+ *   total_seq_len, threshold_sq, exact_window_size, strides new(4) exact(4) pack(4) pc(3),
+ *   num_heads, head_dim, BLOCK_D, USE_COSINE) - deltaDecoding.py:9-104, launched at
+ * deltaDecoding.py:197-211. `capacity` bounds appends; an append past it writes 0x201 into
+ * `err_word` (may be NULL) instead of memory. */
+int dab_decode_update(const void* new_k, const void* new_v, void* k_exact, void* v_exact, void* k_packed,
+                      void* v_packed, int32_t* packed_counts, int32_t* packed_ts, int32_t* packed_lengths,
+                      int64_t exact_seq_len, int64_t total_seq_len, float threshold, int64_t exact_window,
+                      int dtype, const int64_t* new_strides, const int64_t* exact_strides,
+                      const int64_t* pack_strides, const int64_t* pc_strides, int64_t num_heads,
+                      int64_t head_dim, int64_t block_d, int use_cosine, int64_t programs, int64_t capacity,
+                      int* err_word, void* stream);
+
+/* Scratch bytes dab_decode_attention needs. */
+size_t dab_decode_attention_workspace_size(int64_t batch, int64_t num_q_heads, int64_t capacity,
+                                           int64_t exact_len, int64_t head_dim);
+
+/* fused_hybrid_decode_kernel[(B, Hq)](Q, K_packed, V_packed, Packed_Counts, Packed_Lengths,
+ *   K_exact, V_exact, Out, 27 strides (q 3, kp 4, vp 4, counts 3, lengths 2, ke 4, ve 4,
+ *   out 3), sm_scale, exact_len, num_kv_groups, head_dim, BLOCK_M, BLOCK_N, BLOCK_D) -
+ * deltaDecoding.py:236-362, wrapper modeling_llama.py:453-518. `capacity` is the packed
+ * buffers' row capacity (bounds the split-K grid). */
+int dab_decode_attention(const void* q, const void* k_packed, const void* v_packed, const int32_t* packed_counts,
+                         const int32_t* packed_lengths, const void* k_exact, const void* v_exact, void* out,
+                         int dtype, const int64_t* strides, float sm_scale, int64_t exact_len,
+                         int64_t num_kv_groups, int64_t batch, int64_t num_q_heads, int64_t head_dim,
+                         int64_t capacity, void* workspace, size_t workspace_bytes, void* stream);
+
+/* apply_rotary_pos_emb for one tensor (modeling_llama.py:180-204): y = x*cos +
+ * rotate_half(x)*sin with eager rounding to the tensor dtype after each op. x/y strides
+ * (b, h, s, d); cos/sin strides (b, s, d) (b-stride 0 broadcasts). */
+int dab_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* y_strides, const void* cos_t,
+             const void* sin_t, const int64_t* cs_strides, int dtype, int64_t batch, int64_t heads,
+             int64_t seq_len, int64_t head_dim, void* stream);
+
+/* Packed timestamps / counts of periodic packing (modeling_llama.py:626-632 followed by
+ * :655-685): anchor j at j*period covering min(period, seq_len - j*period) tokens.
+ * Buffers are [batch_heads][num_packed] contiguous; num_packed must be ceil(seq_len/period).
+ * The packed K/V rows of periodic packing are a strided view of K/V (row stride x period),
+ * so no copy is made. */
+int dab_periodic_meta(int32_t* packed_ts, int32_t* packed_counts, int64_t batch_heads, int64_t num_packed,
+                      int64_t seq_len, int64_t period, void* stream);
+
+/* Scratch bytes dab_pack_from_keep needs. */
+size_t dab_pack_from_keep_workspace_size(int64_t batch, int64_t heads, int64_t seq_len);
+
+/* Device-side packing from a keep mask (modeling_llama.py:655-685 without the host sync at
+ * :656): index_map = cumsum(keep) - 1 (optional, [B][H][N] contiguous), packed K/V rows,
+ * timestamps and run-length counts into buffers of `capacity` rows (rows beyond a head's
+ * anchors are left untouched: zero-initialise them for the reference's padding
+ * semantics), anchors per head and their maximum (the reference's M). */
+int dab_pack_from_keep(const int32_t* keep_mask, const int64_t* km_strides, const void* k, const int64_t* k_strides,
+                       const void* v, const int64_t* v_strides, void* k_packed, void* v_packed,
+                       const int64_t* pack_strides, int32_t* packed_ts, int32_t* packed_counts,
+                       const int64_t* meta_strides, int32_t* index_map, int dtype, int64_t batch, int64_t heads,
+                       int64_t seq_len, int64_t head_dim, int64_t capacity, int32_t* anchors_per_head,
+                       int32_t* max_anchors, void* workspace, size_t workspace_bytes, void* stream);
+
+/* N:M structured anchor selection (nmDeltaFlashAttention; the reference ships only a
+ * compiled module for it, so the semantics are this library's own): candidates are the
+ * positions t % stride == 0; candidate t scores +inf at t == 0, else the fp32 squared
+ * distance between K[t] and K[t - stride]; every run of m_group consecutive candidates
+ * keeps its min(n_keep, size) highest scores (ties to the earlier position). Writes the
+ * whole keep mask (int32, 0/1). The packed length is dab_nm_num_packed(...) for every
+ * head, so the result packs without a host sync. */
+int dab_nm_select(const void* k, const int64_t* k_strides, int32_t* keep_mask, const int64_t* km_strides, int dtype,
+                  int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t n_keep, int64_t m_group,
+                  int64_t stride, void* stream);
+/* Anchors per head that dab_nm_select keeps. */
+int64_t dab_nm_num_packed(int64_t seq_len, int64_t n_keep, int64_t m_group, int64_t stride);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DELTAATTN_B200_H */

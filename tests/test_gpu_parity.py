@@ -1,0 +1,384 @@
+"""GPU parity: the CUDA kernels (through the reference-facing launch API and the C ABI)
+against the reference goldens and the CPU oracle.
+
+Selection, packing, N:M selection, RoPE and decode-cache state must match bit for bit.
+Attention outputs: fp32 within 1e-4 (max abs); bf16/fp16 within max-abs 2e-2 and
+mean-abs 2e-3 (the tolerances BASELINE.json's north star states).
+"""
+import numpy as np
+import pytest
+import torch
+
+import _inputs as I
+from oracle import delta_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: (1e-4, 1e-5), torch.float16: (2e-2, 2e-3), torch.bfloat16: (2e-2, 2e-3)}
+
+
+@pytest.fixture(scope="module", autouse=True)
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import deltaattention_b200 as d
+    d._lib.load()
+    from deltaattention_b200.dropin import install
+    install()
+    return d
+
+
+def _check_ws_clean():
+    from deltaattention_b200 import _lib as L
+    torch.cuda.synchronize()
+    codes = L.workspace_errors()
+    assert all(c == 0 for c in codes), f"a bounded device wait timed out: {[hex(c) for c in codes]}"
+
+
+def _cmp(out, ref, dtype, what=""):
+    out = out.float().cpu()
+    ref = ref.float().cpu()
+    assert torch.isfinite(out).all() == torch.isfinite(ref).all(), what
+    err = (out - ref).abs()
+    mx, mean = TOL[dtype]
+    assert err.max().item() <= mx and err.mean().item() <= mean, (what, err.max().item(), err.mean().item())
+
+
+# ------------------------------------------------------------------ selection / packing
+SEL = [
+    ("keep_euclid_fp32", torch.float32, 1, 2, 1000, 64, 256, False, 1e4, 1),
+    ("keep_euclid_fp16", torch.float16, 1, 2, 1000, 128, 300, False, 5e5, 2),
+    ("keep_cosine_fp32", torch.float32, 1, 2, 1000, 64, 256, True, 1e4, 3),
+    ("keep_cosine_bf16", torch.bfloat16, 1, 2, 1000, 128, 300, True, 5e5, 4),
+    ("keep_cosine_fp16", torch.float16, 1, 2, 700, 96, 512, True, 5e5, 5),
+]
+
+
+@pytest.mark.parametrize("case", SEL, ids=[c[0] for c in SEL])
+def test_chunked_eval_matches_reference_bit_exact(golden, case):
+    import tritonModules as tm
+    name, dt, B, H, N, D, chunk, use_cos, theta, seed = case
+    g = golden(name)
+    k = I.post_rope_keys(B, H, N, D, theta, dt, seed=seed).cuda()
+    nch = -(-N // chunk)
+    keep = torch.zeros((B, H, N), dtype=torch.int32, device="cuda")
+    cc = torch.zeros((B, H, nch), dtype=torch.int32, device="cuda")
+    bd = 1 << (D - 1).bit_length()
+    tm.chunked_eval_kernel[(B * H, nch)](
+        k, keep, cc, float(g["threshold"]), k.stride(0), k.stride(1), k.stride(2), k.stride(3),
+        keep.stride(0), keep.stride(1), keep.stride(2), cc.stride(0), cc.stride(1), cc.stride(2),
+        N, D, chunk, num_heads=H, BLOCK_D=bd, USE_COSINE=use_cos, num_warps=4)
+    np.testing.assert_array_equal(keep.cpu().numpy(), g["keep"])
+    np.testing.assert_array_equal(cc.cpu().numpy(), g["chunk_counts"])
+
+
+def test_chunked_eval_strided_bshd(golden):
+    import tritonModules as tm
+    g = golden("keep_euclid_fp32_bshd")
+    k = I.post_rope_keys(1, 2, 1000, 64, 1e4, torch.float32, seed=1)
+    kb = k.transpose(1, 2).contiguous().transpose(1, 2).cuda()
+    keep = torch.zeros((1, 2, 1000), dtype=torch.int32, device="cuda")
+    cc = torch.zeros((1, 2, 4), dtype=torch.int32, device="cuda")
+    tm.chunked_eval_kernel[(2, 4)](kb, keep, cc, float(g["threshold"]), *kb.stride(), *keep.stride(), *cc.stride(),
+                                   1000, 64, 256, num_heads=2, BLOCK_D=64, USE_COSINE=False)
+    np.testing.assert_array_equal(keep.cpu().numpy(), g["keep"])
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16, torch.float32])
+def test_chunked_eval_euclid_matches_oracle(dt):
+    """bf16 Euclid has no interpreter golden (bf16 arithmetic there is bitwise); the oracle
+    restates the reference's rounding and reduction order and the kernel must agree."""
+    import tritonModules as tm
+    B, H, N, D, chunk = 1, 4, 2048, 128, 512
+    k = I.post_rope_keys(B, H, N, D, 5e5, dt, seed=77, offset=True)
+    thr = I.median_threshold(k, False)
+    ref_keep, ref_cc = O.delta_keep_mask(k, thr, False, chunk, N // chunk)
+    kc = k.cuda()
+    keep = torch.zeros((B, H, N), dtype=torch.int32, device="cuda")
+    cc = torch.zeros((B, H, N // chunk), dtype=torch.int32, device="cuda")
+    tm.chunked_eval_kernel[(B * H, N // chunk)](kc, keep, cc, thr, *kc.stride(), *keep.stride(), *cc.stride(), N, D,
+                                                chunk, num_heads=H, BLOCK_D=128, USE_COSINE=False)
+    np.testing.assert_array_equal(keep.cpu().numpy(), ref_keep.numpy())
+    np.testing.assert_array_equal(cc.cpu().numpy(), ref_cc.numpy())
+
+
+def test_scatter_pack_matches_reference(golden):
+    import tritonModules as tm
+    g = golden("pack_fp32")
+    k = I.post_rope_keys(1, 2, 1000, 64, 1e4, torch.float32, seed=1).cuda()
+    v = torch.from_numpy(I.normal((1, 2, 1000, 64), seed=101)).cuda()
+    keep = torch.from_numpy(g["keep"]).cuda()
+    im = (torch.cumsum(keep, -1) - 1).to(torch.int32)
+    M = int(keep.sum(-1).max())
+    kp = torch.zeros((1, 2, M, 64), device="cuda")
+    vp = torch.zeros_like(kp)
+    ts = torch.zeros((1, 2, M), dtype=torch.int32, device="cuda")
+    tm.parallel_scatter_pack_kv_kernel[(2, -(-1000 // 64))](
+        k, v, kp, vp, ts, keep, im, *k.stride(), *v.stride(), *kp.stride(), *vp.stride(), *ts.stride(),
+        *keep.stride(), *im.stride(), 1000, 64, 2, BLOCK_S=64, BLOCK_D=64)
+    np.testing.assert_array_equal(kp.cpu().numpy(), g["k_packed"])
+    np.testing.assert_array_equal(vp.cpu().numpy(), g["v_packed"])
+    np.testing.assert_array_equal(ts.cpu().numpy(), g["timestamps"])
+
+
+def test_device_pack_from_keep_matches_reference(golden):
+    from deltaattention_b200 import ops
+    g = golden("pack_fp32")
+    k = I.post_rope_keys(1, 2, 1000, 64, 1e4, torch.float32, seed=1).cuda()
+    v = torch.from_numpy(I.normal((1, 2, 1000, 64), seed=101)).cuda()
+    keep = torch.from_numpy(g["keep"]).cuda()
+    p = ops.pack_from_keep(k, v, keep, want_index_map=True)
+    np.testing.assert_array_equal(p.index_map.cpu().numpy(), g["index_map"])
+    np.testing.assert_array_equal(p.k.cpu().numpy(), g["k_packed"])
+    np.testing.assert_array_equal(p.v.cpu().numpy(), g["v_packed"])
+    np.testing.assert_array_equal(p.timestamps.cpu().numpy(), g["timestamps"])
+    np.testing.assert_array_equal(p.counts.cpu().numpy(), g["counts"])
+
+
+@pytest.mark.parametrize("dt_name,dt", [("bf16", torch.bfloat16), ("fp32", torch.float32)])
+def test_rope_matches_reference(golden, dt_name, dt):
+    from deltaattention_b200 import ops
+    g = golden(f"rope_{dt_name}")
+    x = torch.from_numpy(I.ar1_keys(1, 2, 300, 128, seed=11, offset=True)).to(dt)
+    cos, sin = O.rope_cos_sin(300, 128, 500000.0, dt)
+    y = ops.rope(x.cuda(), cos.cuda(), sin.cuda())
+    np.testing.assert_array_equal(y.float().cpu().numpy(), g["out"])
+
+
+def test_nm_select_matches_oracle():
+    from deltaattention_b200.dropin import nmDeltaFlashAttention as nm
+    for (n, m, r, N) in [(2, 4, 4, 2000), (2, 4, 2, 777), (1, 4, 4, 1024), (3, 8, 8, 1500)]:
+        k = I.post_rope_keys(2, 2, N, 128, 5e5, torch.bfloat16, seed=N)
+        ref = O.nm_keep_mask(k, n, m, r)
+        got = nm.nm_keep_mask(k.cuda(), n, m, r)
+        np.testing.assert_array_equal(got.cpu().numpy(), ref.numpy())
+        assert int(got[0, 0].sum()) == nm.nm_num_packed(N, n, m, r)
+
+
+# ------------------------------------------------------------------ attention
+ATTN = [
+    ("attn_fp32_periodic", torch.float32, 2, 600, 64, "periodic", 21),
+    ("attn_fp32_delta", torch.float32, 2, 600, 64, "delta", 22),
+    ("attn_fp32_w0", torch.float32, 2, 600, 64, "periodic", 23),
+    ("attn_fp16_periodic", torch.float16, 2, 600, 128, "periodic", 24),
+    ("attn_fp16_delta", torch.float16, 2, 520, 128, "delta", 25),
+    ("attn_fp32_quirk", torch.float32, 2, 600, 64, "quirk", 26),
+]
+VARIANT_KERNEL = {"hybrid": "hybrid_compressed_flash_kernel", "sanity": "hybrid_compressed_flash_kernel_sanity",
+                  "pure_phase1": "pure_phase1_flash_kernel"}
+
+
+def _launch_variant(variant, q, kd, vd, kp, vp, ts, counts, W, force_simt=False):
+    """The launch modeling_llama.py:306-451 performs, through the drop-in kernel objects."""
+    import deltaFlashAttention as dfa
+    from deltaattention_b200 import launch
+    B, H, N, D = q.shape
+    out = torch.empty_like(q)
+    args = (q, kd, vd, kp, vp, ts, counts, out,
+            *q.stride(), *kd.stride(), *vd.stride(), *kp.stride(), *vp.stride(), *ts.stride(), *counts.stride(),
+            *out.stride(), D ** -0.5, N, kd.shape[2], kp.shape[2], D, H, W)
+    grid = (-(-N // 128), B * H, 1)
+    bd = 1 << (D - 1).bit_length()
+    if force_simt:
+        b = launch._bind(launch.HYBRID_PARAMS, args, dict(BLOCK_M=128, BLOCK_N=128, BLOCK_D=bd), "x")
+        launch.hybrid_call({"hybrid": 0, "sanity": 1, "pure_phase1": 2}[variant], launch._grid(grid, b), b,
+                           force_simt=True)
+    else:
+        getattr(dfa, VARIANT_KERNEL[variant])[grid](*args, BLOCK_M=128, BLOCK_N=128, BLOCK_D=bd, num_warps=8,
+                                                    num_stages=1)
+    return out
+
+
+@pytest.mark.parametrize("case", ATTN, ids=[c[0] for c in ATTN])
+@pytest.mark.parametrize("variant", ["hybrid", "sanity", "pure_phase1"])
+def test_hybrid_variants_match_reference(golden, case, variant):
+    name, dt, H, N, D, packing, seed = case
+    g = golden(name)
+    q, k, v = I.attn_inputs(1, H, N, D, dt, seed)
+    keep = torch.from_numpy(g["keep"])
+    _, kp, vp, ts, counts = O.pack_from_keep(k, v, keep)
+    c = lambda t: t.cuda().contiguous()  # noqa: E731
+    out = _launch_variant(variant, c(q), c(k), c(v), c(kp), c(vp), c(ts), c(counts.float()), int(g["W"]))
+    _cmp(out, torch.from_numpy(g[variant]), dt, f"{name}/{variant}")
+    _check_ws_clean()
+
+
+@pytest.mark.parametrize("case", [ATTN[0], ATTN[3]], ids=[ATTN[0][0], ATTN[3][0]])
+@pytest.mark.parametrize("causal", [True, False])
+def test_flash_matches_reference(golden, case, causal):
+    import flashAttention as fa
+    name, dt, H, N, D, packing, seed = case
+    g = golden(name)
+    q, k, v = I.attn_inputs(1, H, N, D, dt, seed)
+    out = fa.triton_flash_attention(q.cuda(), k.cuda(), v.cuda(), causal=causal)
+    _cmp(out, torch.from_numpy(g["flash_causal" if causal else "flash_noncausal"]), dt, name)
+    _check_ws_clean()
+
+
+@pytest.mark.parametrize("variant", ["hybrid", "sanity", "pure_phase1"])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [128, 64])
+def test_tcgen05_vs_simt_and_oracle(variant, dt, D):
+    """Expanded-head call (repeat_kv layout): tcgen05 path vs the oracle, ragged N."""
+    H, N = 3, 1000
+    q, k, v = I.attn_inputs(1, H, N, D, dt, 90 + D)
+    keep = O.periodic_keep_mask(1, H, N, 0.25)
+    _, kp, vp, ts, counts = O.pack_from_keep(k, v, keep)
+    ref = O.hybrid_attention(q, k, v, kp, vp, ts, counts.float(), D ** -0.5, 128, variant)
+    c = lambda t: t.cuda().contiguous()  # noqa: E731
+    out = _launch_variant(variant, c(q), c(k), c(v), c(kp), c(vp), c(ts), c(counts.float()), 128)
+    _cmp(out, ref, dt, f"tc/{variant}")
+    simt = _launch_variant(variant, c(q), c(k), c(v), c(kp), c(vp), c(ts), c(counts.float()), 128, force_simt=True)
+    _cmp(simt, ref, dt, f"simt/{variant}")
+    _check_ws_clean()
+
+
+@pytest.mark.parametrize("mode", ["periodic", "delta"])
+def test_native_gqa_prefill_matches_oracle(mode):
+    """ops.delta_prefill: RoPE + selection + device packing + GQA-by-index attention."""
+    from deltaattention_b200 import ops, synth
+    B, Hq, Hkv, N, D = 1, 8, 2, 2304, 128
+    q, k, v = synth.layer_inputs(B, Hq, Hkv, N, D, torch.bfloat16, seed=5, device="cpu")
+    cos, sin = synth.rope_tables(N, D, 5e5, torch.bfloat16)
+    kw = dict(mode=mode, keep_rate=0.25) if mode == "periodic" else dict(mode="delta", threshold=1.6,
+                                                                          chunk_size=512)
+    out, packed, k_rot = ops.delta_prefill(q.cuda(), k.cuda(), v.cuda(), cos.cuda(), sin.cuda(), return_packed=True,
+                                           **kw)
+    q_ref = O.apply_rope(q.contiguous(), cos, sin)
+    k_ref = O.apply_rope(k.contiguous(), cos, sin)
+    np.testing.assert_array_equal(k_rot.float().cpu().numpy(), k_ref.float().numpy())
+    if mode == "periodic":
+        keep = O.periodic_keep_mask(B, Hkv, N, 0.25)
+    else:
+        keep, _ = O.delta_keep_mask(k_ref, 1.6 ** 2, False, 512, N // 512 + 1)
+        np.testing.assert_array_equal(packed.keep_mask.cpu().numpy(), keep.numpy())
+    _, kp, vp, ts, counts = O.pack_from_keep(k_ref, v.contiguous(), keep)
+    np.testing.assert_array_equal(packed.timestamps.cpu().numpy(), ts.numpy())
+    np.testing.assert_array_equal(packed.counts.cpu().numpy(), counts.numpy())
+    ref = O.hybrid_attention(q_ref, k_ref, v.contiguous(), kp, vp, ts, counts.float(), D ** -0.5, 128, "hybrid",
+                             n_rep=Hq // Hkv)
+    _cmp(out, ref, torch.bfloat16, f"native/{mode}")
+    _check_ws_clean()
+
+
+def test_cfg1_fp32_full_size():
+    """BASELINE config 1 (fp32, B=1, H=8, N=2048, d=64, r=4) at 1e-4."""
+    from deltaattention_b200 import ops, synth
+    c = synth.CONFIGS["cfg1"]
+    q, k, v = synth.layer_inputs(1, 8, 8, 2048, 64, torch.float32, seed=0, device="cpu", qv_scale=1.0,
+                                 key_offset=False)
+    cos, sin = synth.rope_tables(2048, 64, c["theta"], torch.float32)
+    out = ops.delta_prefill(q.cuda(), k.cuda(), v.cuda(), cos.cuda(), sin.cuda(), keep_rate=0.25)
+    q_ref, k_ref = O.apply_rope(q.contiguous(), cos, sin), O.apply_rope(k.contiguous(), cos, sin)
+    keep = O.periodic_keep_mask(1, 8, 2048, 0.25)
+    _, kp, vp, ts, counts = O.pack_from_keep(k_ref, v.contiguous(), keep)
+    ref = O.hybrid_attention(q_ref, k_ref, v.contiguous(), kp, vp, ts, counts.float(), 64 ** -0.5, 128)
+    _cmp(out, ref, torch.float32, "cfg1")
+
+
+def test_cfg2_full_size_sampled_heads():
+    """BASELINE config 2 shape (bf16, Hq=32, Hkv=8, N=32768, d=128, r=4): all rows of two
+    q-heads against the oracle, plus size-independent properties on every head."""
+    from deltaattention_b200 import ops, synth
+    N = 32768
+    q, k, v = synth.layer_inputs(1, 32, 8, N, 128, torch.bfloat16, seed=1, device="cuda")
+    cos, sin = synth.rope_tables(N, 128, 5e5, torch.bfloat16, device="cuda")
+    out = ops.delta_prefill(q, k, v, cos, sin, keep_rate=0.25)
+    assert torch.isfinite(out.float()).all()
+    heads = [0, 13]
+    qc, kc, vc = q.cpu().contiguous(), k.cpu().contiguous(), v.cpu().contiguous()
+    cc, sc = cos.cpu(), sin.cpu()
+    q_ref, k_ref = O.apply_rope(qc, cc, sc), O.apply_rope(kc, cc, sc)
+    keep = O.periodic_keep_mask(1, 8, N, 0.25)
+    _, kp, vp, ts, counts = O.pack_from_keep(k_ref, vc, keep)
+    ref = O.hybrid_attention(q_ref, k_ref, vc, kp, vp, ts, counts.float(), 128 ** -0.5, 128, n_rep=4, heads=heads)
+    for h in heads:
+        _cmp(out[:, h], ref[:, h], torch.bfloat16, f"cfg2/head{h}")
+    # attention rows are convex combinations of V rows: bounded by V's range
+    vmax = v.abs().amax().float()
+    assert out.float().abs().amax() <= vmax * 1.01
+    _check_ws_clean()
+
+
+def test_dense_r1_matches_flash_kernel():
+    """r = 1 through the hybrid kernel equals plain causal flash (same kernel family)."""
+    from deltaattention_b200 import ops, synth
+    q, k, v = synth.layer_inputs(1, 8, 2, 2048, 128, torch.bfloat16, seed=3, device="cuda")
+    cos, sin = synth.rope_tables(2048, 128, 5e5, torch.bfloat16, device="cuda")
+    qr, kr = ops.rope(q, cos, sin), ops.rope(k, cos, sin)
+    dense = ops.flash(qr, kr, v)
+    ref = O.flash_attention(qr.cpu(), kr.cpu(), v.cpu().contiguous(), n_rep=4)
+    _cmp(dense, ref, torch.bfloat16, "flash-gqa")
+
+
+# ------------------------------------------------------------------ decoding
+@pytest.mark.parametrize("name,dt,use_cos", [("decode_fp32_euclid", torch.float32, False),
+                                             ("decode_fp16_cosine", torch.float16, True)])
+def test_decode_replay_matches_reference(golden, name, dt, use_cos):
+    import deltaDecoding as dd
+    g = golden(name)
+    st = I.decode_setup(dt, seed=31)
+    B, Hkv, Hq, D, W = st["B"], st["Hkv"], st["Hq"], st["D"], st["W"]
+    thr = float(g["threshold"])
+    c = lambda t: t.cuda()  # noqa: E731
+    kp, vp, cnt, tss, lens = c(st["kp"]), c(st["vp"]), c(st["counts"]), c(st["ts"]), c(st["lengths"])
+    ke, ve = c(st["ke"]), c(st["ve"])
+    exact_len, total = st["exact_len"], st["total"]
+    outs = []
+    for step in range(st["steps"]):
+        nk, nv = c(st["new_k"][step]), c(st["new_v"][step])
+        dd.fused_hybrid_decode_update_kernel[(B * Hkv,)](
+            nk, nv, ke, ve, kp, vp, cnt, tss, lens, exact_len, total, thr, W,
+            *nk.stride(), *ke.stride(), *kp.stride(), *cnt.stride(), Hkv, D, BLOCK_D=D, USE_COSINE=use_cos)
+        exact_len += 1
+        total += 1
+        np.testing.assert_array_equal(lens.cpu().numpy(), g["lengths"][step])
+        q = c(st["q"][step])
+        out = torch.empty_like(q)
+        lv = lens.view(B, Hkv)
+        dd.fused_hybrid_decode_kernel[(B, Hq)](
+            q, kp, vp, cnt, lv, ke, ve, out, *q.stride(), *kp.stride(), *vp.stride(), *cnt.stride(), *lv.stride(),
+            *ke.stride(), *ve.stride(), *out.stride(), D ** -0.5, min(exact_len, W), Hq // Hkv, head_dim=D,
+            BLOCK_M=16, BLOCK_N=128, BLOCK_D=D)
+        outs.append(out.float().cpu())
+    np.testing.assert_array_equal(cnt.cpu().numpy(), g["counts"])
+    np.testing.assert_array_equal(tss.cpu().numpy(), g["timestamps"])
+    np.testing.assert_array_equal(kp.float().cpu().numpy(), g["k_packed"])
+    np.testing.assert_array_equal(ke.float().cpu().numpy(), g["k_exact"])
+    _cmp(torch.stack(outs), torch.from_numpy(g["outputs"]), dt, name)
+
+
+def test_hybrid_cache_end_to_end():
+    """HybridCompressedCache: prefill hand-off then decode steps, against the oracle."""
+    import types
+    import deltaDecoding as dd
+    cfg = types.SimpleNamespace(hidden_size=8 * 128, num_attention_heads=8, num_key_value_heads=2,
+                                num_hidden_layers=1, head_dim=128)
+    cache = dd.HybridCompressedCache(cfg, batch_size=1, dtype=torch.bfloat16, exact_window_size=32,
+                                     initial_capacity=64)
+    N0, D = 300, 128
+    keys = torch.from_numpy(I.ar1_keys(1, 2, N0 + 20, D, seed=8)).bfloat16()
+    vals = torch.from_numpy(I.normal((1, 2, N0 + 20, D), seed=9)).bfloat16()
+    keep = O.periodic_keep_mask(1, 2, N0, 0.25)
+    _, kp, vp, ts, counts = O.pack_from_keep(keys[:, :, :N0], vals[:, :, :N0], keep)
+    cache.initialize_from_prefill(0, kp.cuda(), vp.cuda(), counts.cuda(), ts.cuda(), keys[:, :, N0 - 32:N0].cuda(),
+                                  vals[:, :, N0 - 32:N0].cuda(), N0)
+    assert cache.capacity >= kp.shape[2]
+    ref_state = [kp.clone(), vp.clone(), counts.clone(), ts.clone(),
+                 torch.tensor([kp.shape[2]] * 2, dtype=torch.int32), keys[:, :, N0 - 32:N0].clone(),
+                 vals[:, :, N0 - 32:N0].clone()]
+    cap = cache.capacity
+    pad = lambda t, n: torch.cat([t, torch.zeros((*t.shape[:2], n - t.shape[2], *t.shape[3:]), dtype=t.dtype)], 2)  # noqa
+    rk, rv, rc, rt = pad(ref_state[0], cap), pad(ref_state[1], cap), pad(ref_state[2], cap), pad(ref_state[3], cap)
+    rl, rke, rve = ref_state[4], ref_state[5], ref_state[6]
+    exact, total = 32, N0
+    for s in range(20):
+        nk, nv = keys[:, :, N0 + s:N0 + s + 1], vals[:, :, N0 + s:N0 + s + 1]
+        cache.update(nk.cuda(), nv.cuda(), 0)
+        O.decode_update(nk, nv, rke, rve, rk, rv, rc, rt, rl, exact, total, 0.0, 32, False)
+        exact += 1
+        total += 1
+    np.testing.assert_array_equal(cache.packed_lengths[0].cpu().numpy(), rl.numpy())
+    L = int(rl.max())
+    np.testing.assert_array_equal(cache.packed_counts[0][:, :, :L].cpu().numpy(), rc[:, :, :L].numpy())
+    np.testing.assert_array_equal(cache.packed_timestamps[0][:, :, :L].cpu().numpy(), rt[:, :, :L].numpy())
