@@ -239,6 +239,10 @@ def run_ours(args, world, rank, local):
     tokens = B * N * world
     value = tokens / (ms / 1000.0)
 
+    if args.only_step:
+        if rank == 0:
+            print(json.dumps({"ms_per_step": ms, "attn_ms": attn_ms}), flush=True)
+        return
     # dense (r = 1) comparator through the same kernel family: causal flash with GQA by index
     q_rot, k_rot = ops.rope(q, cos, sin), ops.rope(k, cos, sin)
     for _ in range(2):
@@ -319,10 +323,12 @@ def run_ours(args, world, rank, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only-step", action="store_true",
+                    help="time the hot-path step only (no comparator, e2e or CPU legs); for profiling")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":

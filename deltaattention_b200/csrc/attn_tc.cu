@@ -493,14 +493,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           cur_k = nk;
         }
         if (aborted) break;
-        // tile_free is consumed exactly once per unit and query tile
+        // Handshake per valid query tile and unit: the MMA waits tile_free once (before its
+        // first write to that tile's TMEM, or here) and always commits o_full; the epilogue
+        // always waits o_full before arriving on tile_free. An epilogue therefore never
+        // arrives before the MMA's matching wait, which keeps the parity waits unambiguous.
+        // Invalid tiles take no part.
         for (int x = 0; x < 2 && !aborted; ++x)
-          if (!ensure_free(x)) aborted = true;
+          if (U.valid[x] && !ensure_free(x)) aborted = true;
         if (aborted) break;
         // all S of this unit issued: the Q buffers may be refilled once they complete
         umma_commit(q_empty);
         for (int x = 0; x < 2; ++x)
-          if (o_init[x]) umma_commit(o_full + x);
+          if (U.valid[x]) umma_commit(o_full + x);
       }
       // wait for every MMA this thread issued before TMEM can be released
       umma_commit(mma_done);
@@ -645,12 +649,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         o_has = true;
       }
       if (!ok) break;
-      if (!U.valid[x]) {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(tile_free + x);
-        continue;
-      }
+      if (!U.valid[x]) continue;  // invalid tiles take no part in the o_full / tile_free handshake
       // ---------------- epilogue: O / l -> out
       float lf = l;
       if (p.variant == TC_PURE && !(lf > 0.f)) lf = 1.f;
@@ -659,10 +658,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
       T* orow = static_cast<T*>(p.out) + U.b * p.os_b + static_cast<int64_t>(U.hq[x]) * p.os_h +
                 static_cast<int64_t>(row) * p.os_m;
+      if (!warp_wait(o_full + x, o_par, ab, ERR_TIMEOUT_EPILOGUE)) break;
+      o_par ^= 1;
+      tc_fence_after();
       if (o_has) {
-        if (!warp_wait(o_full + x, o_par, ab, ERR_TIMEOUT_EPILOGUE)) break;
-        o_par ^= 1;
-        tc_fence_after();
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t ob[32];

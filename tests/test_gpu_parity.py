@@ -28,6 +28,16 @@ def lib():
     return d
 
 
+@pytest.fixture(autouse=True)
+def _fresh_error_words():
+    """Each test starts with cleared device error words (a failure cannot leak forward)."""
+    from deltaattention_b200 import _lib as L
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+        L.workspace_errors()
+    yield
+
+
 def _check_ws_clean():
     from deltaattention_b200 import _lib as L
     torch.cuda.synchronize()
