@@ -144,15 +144,23 @@ def max_over_ranks(x, world):
 
 
 # ------------------------------------------------------------------------------ CPU side
-def cpu_sample(heads=(0,), N=CFG["N"]):
-    """Oracle (CPU restatement of the reference path) on q-heads `heads` of one cfg2 layer.
+_CPU_INPUTS = {}
+
+
+def cpu_sample(heads=(0,), stride=1, N=CFG["N"]):
+    """Oracle (CPU restatement of the reference path) on q-heads `heads` of one cfg2 layer,
+    attention restricted to every `stride`-th 128-row query block.
 
     Returns (seconds, tokens-equivalent): the sample's share of one layer's N tokens."""
     from deltaattention_b200 import synth
     from oracle import delta_oracle as O
-    q, k, v = synth.layer_inputs(1, CFG["Hq"], CFG["Hkv"], N, CFG["D"], torch.bfloat16, seed=0, device="cpu")
-    cos, sin = synth.rope_tables(N, CFG["D"], CFG["theta"], torch.bfloat16)
+    if N not in _CPU_INPUTS:
+        q, k, v = synth.layer_inputs(1, CFG["Hq"], CFG["Hkv"], N, CFG["D"], torch.bfloat16, seed=0, device="cpu")
+        _CPU_INPUTS[N] = (q, k, v) + synth.rope_tables(N, CFG["D"], CFG["theta"], torch.bfloat16)
+    q, k, v, cos, sin = _CPU_INPUTS[N]
     kv_heads = sorted({h // (CFG["Hq"] // CFG["Hkv"]) for h in heads})
+    nmb = -(-N // 128)
+    blocks = list(range(0, nmb, stride))
     t0 = time.perf_counter()
     q_ref = O.apply_rope(q[:, list(heads)].contiguous(), cos, sin)
     k_ref = O.apply_rope(k[:, kv_heads].contiguous(), cos, sin)
@@ -160,9 +168,10 @@ def cpu_sample(heads=(0,), N=CFG["N"]):
     keep = O.periodic_keep_mask(1, len(kv_heads), N, 1.0 / CFG["r"])
     _, kp, vp, ts, counts = O.pack_from_keep(k_ref, vv, keep)
     n_rep = len(heads) if len(kv_heads) == 1 else 1
-    O.hybrid_attention(q_ref, k_ref, vv, kp, vp, ts, counts.float(), CFG["D"] ** -0.5, CFG["W"], n_rep=n_rep)
+    O.hybrid_attention(q_ref, k_ref, vv, kp, vp, ts, counts.float(), CFG["D"] ** -0.5, CFG["W"], n_rep=n_rep,
+                       query_blocks=blocks)
     dt = time.perf_counter() - t0
-    return dt, N * len(heads) / CFG["Hq"]
+    return dt, 128 * len(blocks) * len(heads) / CFG["Hq"]
 
 
 def run_reference(args, world, rank):
@@ -170,11 +179,17 @@ def run_reference(args, world, rank):
         return
     torch.set_num_threads(os.cpu_count() or 1)
     heads = (0,)
+    # size each step so the whole run stays near a minute: a full q-head costs ~1.5 s here,
+    # so long runs sample every `stride`-th query block (uniform over sequence positions)
+    t_head, _ = cpu_sample(heads, stride=8)
+    t_head *= 8
+    budget = 60.0 / (args.steps + args.warmup)
+    stride = max(1, min(64, int(-(-t_head // budget))))
     for _ in range(args.warmup):
-        cpu_sample(heads)
+        cpu_sample(heads, stride)
     secs, toks = 0.0, 0.0
     for _ in range(args.steps):
-        dt, tk = cpu_sample(heads)
+        dt, tk = cpu_sample(heads, stride)
         secs += dt
         toks += tk
     value = toks / secs
@@ -183,8 +198,9 @@ def run_reference(args, world, rank):
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, BASELINE cfg2)",
             "config": workload_config(world), "impl": "reference",
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": f"1 of 32 q-heads (its kv-head's RoPE, packing and attention) of one "
-                                       f"N={CFG['N']} layer per step; tokens scaled by 1/32"},
+                             "sample": f"per step: q-head 0 of 32 (its kv-head's RoPE and packing, attention "
+                                       f"on every {stride}th of 256 query blocks) of one N={CFG['N']} layer; "
+                                       f"tokens scaled accordingly"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -327,10 +343,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--n", type=int, default=None, help="sequence length override (profiling small cases)")
     ap.add_argument("--only-step", action="store_true",
                     help="time the hot-path step only (no comparator, e2e or CPU legs); for profiling")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.n:
+        CFG["N"] = args.n
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))

@@ -300,14 +300,14 @@ def _blk(x, a, b):
 def hybrid_attention(q, k_dense, v_dense, k_packed, v_packed, timestamps, counts,
                      sm_scale: float, dense_window: int, variant: str = "hybrid",
                      n_rep: int = 1, block_m: int = 128, block_n: int = 128,
-                     heads: Optional[list] = None):
+                     heads: Optional[list] = None, query_blocks: Optional[list] = None):
     """Two-phase count-weighted attention, one query block at a time.
 
     variant: 'hybrid' (deltaFlashAttention.py:9-146), 'sanity' (:149-259) or
     'pure_phase1' (:262-357). q is [B,Hq,Nq,d]; the K/V/ts/counts tensors have
     Hq/n_rep heads (q-head h reads kv-head h // n_rep; n_rep=1 is the reference's
-    repeat_kv-expanded call). ``heads`` optionally restricts the q-heads computed
-    (others are returned as zeros). Returns fp32-computed output in q's dtype.
+    repeat_kv-expanded call). ``heads`` / ``query_blocks`` optionally restrict the q-heads
+    and query blocks computed (others are returned as zeros). Returns the output in q's dtype.
     """
     B, Hq, Nq, D = q.shape
     Nk = k_dense.shape[2]
@@ -331,7 +331,8 @@ def hybrid_attention(q, k_dense, v_dense, k_packed, v_packed, timestamps, counts
             hs = [h for h in range(hk * n_rep, (hk + 1) * n_rep) if h in heads]
             if not hs:
                 continue
-            for pid in range(-(-Nq // block_m)):
+            pids = range(-(-Nq // block_m)) if query_blocks is None else query_blocks
+            for pid in pids:
                 m0 = pid * block_m
                 m1 = min(Nq, m0 + block_m)
                 rows = torch.arange(m0, m1)
