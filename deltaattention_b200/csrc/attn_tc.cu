@@ -343,28 +343,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         if (!t.needs_v) continue;
         ring.take(NS, slot, fpar, epar);
         if (!warp_wait(slot_empty + slot, epar, ab, ERR_TIMEOUT_PRODUCER)) goto producer_done;
+        uint32_t meta_bytes = 0;
         if (t.packed) {
-          // counts (and timestamps) of this packed block ride with its V tile
+          // counts (and timestamps) of this packed block ride with its V tile: bulk copies on
+          // the same barrier when rows are contiguous and aligned, else lane loads
           float* c = auxc + slot * TC_BN;
           int32_t* tt = auxt + slot * TC_BN;
-          for (int e = lane; e < TC_BN; e += 32) {
-            const int key = t.idx * TC_BN + e;
-            float cv = 0.f;
-            int32_t tv2 = 0;
-            if (key < p.num_packed) {
-              const int64_t off = U.b * p.cs_b + static_cast<int64_t>(hk) * p.cs_h + static_cast<int64_t>(key) * p.cs_n;
-              cv = p.counts_is_int ? static_cast<float>(static_cast<const int32_t*>(p.counts)[off])
-                                   : static_cast<const float*>(p.counts)[off];
-              if (p.variant == TC_PURE)
-                tv2 = p.ts[U.b * p.ts_b + static_cast<int64_t>(hk) * p.ts_h + static_cast<int64_t>(key) * p.ts_n];
+          const int nkeys = min(TC_BN, p.num_packed - t.idx * TC_BN);
+          if (p.meta_bulk) {
+            meta_bytes = static_cast<uint32_t>(nkeys) * 4u * (p.variant == TC_PURE ? 2u : 1u);
+            if (lane == 0) {
+              const int64_t off_c = U.b * p.cs_b + static_cast<int64_t>(hk) * p.cs_h + static_cast<int64_t>(t.idx) * TC_BN;
+              bulk_load(c, static_cast<const uint32_t*>(p.counts) + off_c, nkeys * 4u, slot_full + slot);
+              if (p.variant == TC_PURE) {
+                const int64_t off_t = U.b * p.ts_b + static_cast<int64_t>(hk) * p.ts_h + static_cast<int64_t>(t.idx) * TC_BN;
+                bulk_load(tt, p.ts + off_t, nkeys * 4u, slot_full + slot);
+              }
             }
-            c[e] = cv;
-            tt[e] = tv2;
+          } else {
+            for (int e = lane; e < TC_BN; e += 32) {
+              const int key = t.idx * TC_BN + e;
+              uint32_t cv = 0;
+              int32_t tv2 = 0;
+              if (key < p.num_packed) {
+                const int64_t off = U.b * p.cs_b + static_cast<int64_t>(hk) * p.cs_h + static_cast<int64_t>(key) * p.cs_n;
+                cv = static_cast<const uint32_t*>(p.counts)[off];
+                if (p.variant == TC_PURE)
+                  tv2 = p.ts[U.b * p.ts_b + static_cast<int64_t>(hk) * p.ts_h + static_cast<int64_t>(key) * p.ts_n];
+              }
+              reinterpret_cast<uint32_t*>(c)[e] = cv;
+              tt[e] = tv2;
+            }
+            __syncwarp();
           }
-          __syncwarp();
         }
         if (lane == 0) {
-          mbar_arrive_expect_tx(slot_full + slot, kv_bytes);
+          mbar_arrive_expect_tx(slot_full + slot, kv_bytes + meta_bytes);
           uint8_t* dst = smem + C::OFF_SLOT + slot * C::KVBYTES;
           for (int bx = 0; bx < D / 64; ++bx)
             tma_load_4d(dst + bx * (TC_BN * 128), tv, slot_full + slot, bx * 64, t.idx * TC_BN, hk, U.b);
@@ -542,7 +556,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         if (!warp_wait(s_full + x, s_par, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
         s_par ^= 1;
         tc_fence_after();
-        const float* cnt = auxc + vs * TC_BN;
+        const uint32_t* cnt = reinterpret_cast<const uint32_t*>(auxc + vs * TC_BN);
+        const bool cint = p.counts_is_int != 0;
         const int32_t* tsv = auxt + vs * TC_BN;
         if (t.packed) {
           // the packed block's counts arrive with its V tile
@@ -560,7 +575,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               const int j = w * 32 + e;
-              const bool v = (n0 + j < p.num_packed) && cnt[j] > 0.f && tsv[j] <= row;
+              const float cj = cint ? static_cast<float>(static_cast<int32_t>(cnt[j])) : __uint_as_float(cnt[j]);
+              const bool v = (n0 + j < p.num_packed) && cj > 0.f && tsv[j] <= row;
               bits |= (v ? 1u : 0u) << e;
             }
             if (w == 0) vm[0] = bits; else if (w == 1) vm[1] = bits; else if (w == 2) vm[2] = bits; else vm[3] = bits;
@@ -622,9 +638,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           for (int j = 0; j < TC_BN; j += 2) {
             // keep count loads next to their use (16 keys at a time)
             if ((j & 15) == 0) asm volatile("" ::: "memory");
-            const float2 cc = *reinterpret_cast<const float2*>(cnt + j);
-            const float a = ex2(fmaf(__uint_as_float(sr[j]), sl2, -msub)) * cc.x;
-            const float bq = ex2(fmaf(__uint_as_float(sr[j + 1]), sl2, -msub)) * cc.y;
+            const uint2 cb = *reinterpret_cast<const uint2*>(cnt + j);
+            const float c0 = cint ? static_cast<float>(static_cast<int32_t>(cb.x)) : __uint_as_float(cb.x);
+            const float c1 = cint ? static_cast<float>(static_cast<int32_t>(cb.y)) : __uint_as_float(cb.y);
+            const float a = ex2(fmaf(__uint_as_float(sr[j]), sl2, -msub)) * c0;
+            const float bq = ex2(fmaf(__uint_as_float(sr[j + 1]), sl2, -msub)) * c1;
             l0 += a;
             l1 += bq;
             sr[j / 2] = pack2(a, bq, BF16);

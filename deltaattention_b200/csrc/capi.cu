@@ -239,6 +239,11 @@ static int run_attention(int variant, int causal, const void* q, const void* kd,
       p.pair_heads = (kv_group % 2 == 0) ? 1 : 0;
       p.num_units = static_cast<int>(p.pair_heads ? nmb * B * Hts * (kv_group / 2) : ((nmb + 1) / 2) * B * num_heads);
       p.out_vec_ok = aligned16(out) && (os[0] * 2) % 16 == 0 && (os[1] * 2) % 16 == 0 && (os[2] * 2) % 16 == 0;
+      // counts (and timestamps) rows: contiguous along keys with 16-byte aligned block starts
+      p.meta_bulk = needs_packed && num_packed > 0 && counts && cs && cs[2] == 1 && num_packed % 4 == 0 &&
+                    aligned16(counts) && (cs[0] * 4) % 16 == 0 && (cs[1] * 4) % 16 == 0 &&
+                    (variant != 2 || (ts && tss && tss[2] == 1 && aligned16(ts) && (tss[0] * 4) % 16 == 0 &&
+                                      (tss[1] * 4) % 16 == 0));
       if (variant != 3 && num_packed > 0) {
         cudaError_t e = launch_schedule(ts, tss, counts, cs, counts_is_int, static_cast<int>(B),
                                         static_cast<int>(Hts), static_cast<int>(num_packed), static_cast<int>(seq_k),

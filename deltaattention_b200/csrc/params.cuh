@@ -39,6 +39,7 @@ struct TcParams {
   int variant, causal, counts_is_int, pair_heads;
   int num_units;
   int out_vec_ok;          // output rows are 16-byte aligned with unit d-stride
+  int meta_bulk;           // counts / timestamps rows can be bulk-copied (contiguous, 16-byte aligned)
 };
 
 }  // namespace dab
