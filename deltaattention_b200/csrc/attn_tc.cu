@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(256) schedule_kernel(const int32_t* __restrict
                                                        int64_t tsn, const void* counts, int64_t cb, int64_t ch,
                                                        int64_t cn, int counts_is_int, int Hts, int num_packed,
                                                        int seq_k, int window, int nmb, int nblk, int2* sched,
-                                                       int32_t* blkmin, int want_blkmin) {
+                                                       int32_t* blkmin, int want_blkmin, float* blkw) {
   extern __shared__ int32_t sT[];  // nblk block maxima
   const int bh = blockIdx.x;
   const int b = bh / Hts, h = bh % Hts;
@@ -62,17 +62,18 @@ __global__ void __launch_bounds__(256) schedule_kernel(const int32_t* __restrict
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int j = warp; j < nblk; j += blockDim.x >> 5) {
     int tmax = INT32_MIN, tmin = INT32_MAX;
+    float cmin = INFINITY, cmax = -INFINITY;
     for (int e = lane; e < TC_BN; e += 32) {
       const int key = j * TC_BN + e;
       int t;
       if (key < num_packed) {
         t = tsr[static_cast<int64_t>(key) * tsn];
-        if (want_blkmin) {
-          const int64_t off = b * cb + h * ch + static_cast<int64_t>(key) * cn;
-          const float c = counts_is_int ? static_cast<float>(static_cast<const int32_t*>(counts)[off])
-                                        : static_cast<const float*>(counts)[off];
-          if (c > 0.f) tmin = min(tmin, t);
-        }
+        const int64_t off = b * cb + h * ch + static_cast<int64_t>(key) * cn;
+        const float c = counts_is_int ? static_cast<float>(static_cast<const int32_t*>(counts)[off])
+                                      : static_cast<const float*>(counts)[off];
+        if (c > 0.f) tmin = min(tmin, t);
+        cmin = fminf(cmin, c);
+        cmax = fmaxf(cmax, c);
       } else {
         t = seq_k + 1;
       }
@@ -82,10 +83,15 @@ __global__ void __launch_bounds__(256) schedule_kernel(const int32_t* __restrict
     for (int o = 16; o; o >>= 1) {
       tmax = max(tmax, __shfl_xor_sync(0xFFFFFFFFu, tmax, o));
       tmin = min(tmin, __shfl_xor_sync(0xFFFFFFFFu, tmin, o));
+      cmin = fminf(cmin, __shfl_xor_sync(0xFFFFFFFFu, cmin, o));
+      cmax = fmaxf(cmax, __shfl_xor_sync(0xFFFFFFFFu, cmax, o));
     }
     if (lane == 0) {
       sT[j] = tmax;
       if (want_blkmin) blkmin[static_cast<int64_t>(bh) * nblk + j] = tmin;
+      // a block whose valid keys share one count c is weighted by adding log2(c) to the
+      // exponent (exact for powers of two); mixed counts are applied per key
+      blkw[static_cast<int64_t>(bh) * nblk + j] = (cmin == cmax) ? log2f(cmin) : __int_as_float(0x7FC00000);
     }
   }
   __syncthreads();
@@ -464,13 +470,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           tc_fence_after();
           for (int x = 0; x < 2; ++x) {
             if (!(cur.use >> x & 1)) continue;
-            if (!ensure_free(x)) { aborted = true; break; }
             issue_S(x, cur_k);
             if (!(sanity && cur.packed)) umma_commit(s_full + x);
           }
           if (aborted) break;
           umma_commit(slot_empty + cur_k);
         }
+        bool q_released = false;
         while (have_cur) {
           if (cur.needs_v) {
             ring.take(NS, cur_v, fp, ep);
@@ -478,6 +484,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             tc_fence_after();
           }
           const bool have_nxt = seq.next(p, U, nxt);
+          if (!have_nxt && !q_released) {
+            // every S of this unit is issued: Q may be refilled once they complete
+            umma_commit(q_empty);
+            q_released = true;
+          }
           int nk = -1;
           bool nk_ready = false;
           for (int x = 0; x < 2; ++x) {
@@ -485,6 +496,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
               if (!mbar_wait(p_full + x, p_par[x], ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
               p_par[x] ^= 1;
               tc_fence_after();
+              // the first PV of a unit overwrites O: the previous unit's epilogue must be done
+              if (!ensure_free(x)) { aborted = true; break; }
               issue_PV(x, cur_v);
             }
             if (have_nxt && (nxt.use >> x & 1)) {
@@ -494,7 +507,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
                 tc_fence_after();
                 nk_ready = true;
               }
-              if (!ensure_free(x)) { aborted = true; break; }
               issue_S(x, nk);
               if (!(sanity && nxt.packed)) umma_commit(s_full + x);
             }
@@ -507,16 +519,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           cur_k = nk;
         }
         if (aborted) break;
-        // Handshake per valid query tile and unit: the MMA waits tile_free once (before its
-        // first write to that tile's TMEM, or here) and always commits o_full; the epilogue
+        // Handshake per valid query tile and unit: the MMA waits tile_free once (before the
+        // unit's first PV into that tile's O, or here) and always commits o_full; the epilogue
         // always waits o_full before arriving on tile_free. An epilogue therefore never
         // arrives before the MMA's matching wait, which keeps the parity waits unambiguous.
         // Invalid tiles take no part.
         for (int x = 0; x < 2 && !aborted; ++x)
           if (U.valid[x] && !ensure_free(x)) aborted = true;
         if (aborted) break;
-        // all S of this unit issued: the Q buffers may be refilled once they complete
-        umma_commit(q_empty);
+        if (!q_released) umma_commit(q_empty);
         for (int x = 0; x < 2; ++x)
           if (U.valid[x]) umma_commit(o_full + x);
       }
@@ -558,6 +569,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         tc_fence_after();
         const uint32_t* cnt = reinterpret_cast<const uint32_t*>(auxc + vs * TC_BN);
         const bool cint = p.counts_is_int != 0;
+        // packed block with one common count: weight through the exponent (no per-key work)
+        const float lw = t.packed ? p.blkw[(static_cast<int64_t>(U.b) * p.Hts + U.hts[x]) * p.nblk + t.idx] : 0.f;
+        const bool perkey = t.packed && !(lw == lw);  // NaN: counts differ inside the block
         const int32_t* tsv = auxt + vs * TC_BN;
         if (t.packed) {
           // the packed block's counts arrive with its V tile
@@ -565,8 +579,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         }
         const int n0 = t.idx * TC_BN;
         const uint32_t NEG_INF = 0xFF800000u;
-        // pure-phase-1 validity (count > 0, index < num_packed, timestamp <= row) as a
-        // 128-bit mask, built before S is live to keep register pressure down
+        // pure-phase-1 validity (count > 0, index < num_packed, timestamp <= row): 32 bits per
+        // 32-column chunk, built before S is read
         uint32_t vm[4] = {~0u, ~0u, ~0u, ~0u};
         if (p.variant == TC_PURE) {
 #pragma unroll 1
@@ -582,84 +596,129 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             if (w == 0) vm[0] = bits; else if (w == 1) vm[1] = bits; else if (w == 2) vm[2] = bits; else vm[3] = bits;
           }
         }
-        uint32_t sr[TC_BN];  // raw S bits; later reused in place for the packed P
-#pragma unroll
-        for (int c = 0; c < TC_BN / 32; ++c) tmem_ld32(tS + c * 32, sr + c * 32);
-        if (p.variant == TC_PURE) {
-#pragma unroll
-          for (int j = 0; j < TC_BN; ++j) sr[j] = ((vm[j >> 5] >> (j & 31)) & 1u) ? sr[j] : NEG_INF;
-        } else {
-          int lim = TC_BN;
+        int lim = TC_BN;
+        if (p.variant != TC_PURE) {
           if (t.packed) {
             lim = p.num_packed - n0;
           } else {
             lim = p.seq_k - n0;
             if (p.variant != TC_DENSE || p.causal) lim = min(lim, row - n0 + 1);
           }
-          if (lim < TC_BN) {
-#pragma unroll
-            for (int j = 0; j < TC_BN; ++j) sr[j] = (j < lim) ? sr[j] : NEG_INF;
-          }
         }
-        float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
-        float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
+        // S chunk c (columns 32c..32c+31) with masked columns set to -inf
+        const bool any_mask = (p.variant == TC_PURE) || lim < TC_BN;  // only edge / diagonal tiles
+        auto load_chunk = [&](int c, uint32_t* sc) {
+          tmem_ld32(tS + c * 32, sc);
+          if (any_mask) {
+            const uint32_t bits = (c == 0) ? vm[0] : (c == 1) ? vm[1] : (c == 2) ? vm[2] : vm[3];
 #pragma unroll
-        for (int j = 4; j < TC_BN; j += 4) {
-          mx0 = fmaxf(mx0, __uint_as_float(sr[j]));
-          mx1 = fmaxf(mx1, __uint_as_float(sr[j + 1]));
-          mx2 = fmaxf(mx2, __uint_as_float(sr[j + 2]));
-          mx3 = fmaxf(mx3, __uint_as_float(sr[j + 3]));
-        }
-        const float mt = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
-        // bf16 keeps a stale max until it grows by 2^8; fp16 tracks the exact max because
-        // probabilities times counts must stay inside fp16 range
-        const bool need = mt > m_used + (BF16 ? 8.f : 0.f);
-        if (__any_sync(0xFFFFFFFFu, need)) {
-          const float m_new = need ? mt : m_used;
-          const float f = need ? ex2(m_used - m_new) : 1.f;
-          l *= f;
-          if (o_has) {
-#pragma unroll 1
-            for (int c = 0; c < D / 16; ++c) {
-              uint32_t o[16];
-              tmem_ld16(tO + c * 16, o);
-#pragma unroll
-              for (int j = 0; j < 16; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f);
-              tmem_st16(tO + c * 16, o);
+            for (int e = 0; e < 32; ++e) {
+              const bool v = ((bits >> e) & 1u) && (c * 32 + e < lim);
+              sc[e] = v ? sc[e] : NEG_INF;
             }
           }
-          m_used = m_new;
-        }
-        const float msub = (m_used == -INFINITY) ? 0.f : m_used;
-        float l0 = 0.f, l1 = 0.f;
-        // pair (2c, 2c+1) is packed in place into sr[c] as bf16x2 / f16x2
-        if (t.packed) {
+        };
+        auto chunk_max = [&](const uint32_t* sc) {
+          float m0 = __uint_as_float(sc[0]), m1 = __uint_as_float(sc[1]);
 #pragma unroll
-          for (int j = 0; j < TC_BN; j += 2) {
-            // keep count loads next to their use (16 keys at a time)
-            if ((j & 15) == 0) asm volatile("" ::: "memory");
-            const uint2 cb = *reinterpret_cast<const uint2*>(cnt + j);
-            const float c0 = cint ? static_cast<float>(static_cast<int32_t>(cb.x)) : __uint_as_float(cb.x);
-            const float c1 = cint ? static_cast<float>(static_cast<int32_t>(cb.y)) : __uint_as_float(cb.y);
-            const float a = ex2(fmaf(__uint_as_float(sr[j]), sl2, -msub)) * c0;
-            const float bq = ex2(fmaf(__uint_as_float(sr[j + 1]), sl2, -msub)) * c1;
-            l0 += a;
-            l1 += bq;
-            sr[j / 2] = pack2(a, bq, BF16);
+          for (int e = 2; e < 32; e += 4) {
+            m0 = fmax3(m0, __uint_as_float(sc[e]), __uint_as_float(sc[e + 1]));
+            m1 = fmax3(m1, __uint_as_float(sc[e + 2]), __uint_as_float(sc[e + 3]));
           }
-        } else {
+          return fmaxf(m0, m1);
+        };
+        // probabilities of chunk c against reference msub, count-weighted on packed blocks,
+        // packed as bf16x2 / f16x2 pairs into out[0..15]; row sums into la / lb
+        float2 la = make_float2(0.f, 0.f), lb = la;
+        auto exp_chunk = [&](int c, const uint32_t* sc, float msub, uint32_t* out) {
+          const float nb = (perkey ? 0.f : lw) - msub;
+          if (perkey) {
 #pragma unroll
-          for (int j = 0; j < TC_BN; j += 2) {
-            const float a = ex2(fmaf(__uint_as_float(sr[j]), sl2, -msub));
-            const float bq = ex2(fmaf(__uint_as_float(sr[j + 1]), sl2, -msub));
-            l0 += a;
-            l1 += bq;
-            sr[j / 2] = pack2(a, bq, BF16);
+            for (int e = 0; e < 32; e += 4) {
+              const uint4 cb = *reinterpret_cast<const uint4*>(cnt + c * 32 + e);
+              const uint32_t cu[4] = {cb.x, cb.y, cb.z, cb.w};
+              float pe[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float ck = cint ? static_cast<float>(static_cast<int32_t>(cu[k])) : __uint_as_float(cu[k]);
+                pe[k] = ex2(fmaf(__uint_as_float(sc[e + k]), sl2, nb)) * ck;
+              }
+              la.x += pe[0]; la.y += pe[1]; lb.x += pe[2]; lb.y += pe[3];
+              out[e / 2] = pack2(pe[0], pe[1], BF16);
+              out[e / 2 + 1] = pack2(pe[2], pe[3], BF16);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              float pe[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) pe[k] = ex2(fmaf(__uint_as_float(sc[e + k]), sl2, nb));
+              la.x += pe[0]; la.y += pe[1]; lb.x += pe[2]; lb.y += pe[3];
+              out[e / 2] = pack2(pe[0], pe[1], BF16);
+              out[e / 2 + 1] = pack2(pe[2], pe[3], BF16);
+            }
+          }
+        };
+        // fast path: exponentiate against the running reference while checking whether this
+        // tile raises the row maximum past it (+2^8 for bf16; fp16 takes the exact path)
+        bool over = !BF16 || (m_used == -INFINITY);
+        if (!over) {
+          uint32_t pk[TC_BN / 2];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t sc[32];
+            load_chunk(c, sc);
+            over |= chunk_max(sc) * sl2 > m_used + 8.f;
+            exp_chunk(c, sc, m_used, pk + c * 16);
+          }
+          if (!__any_sync(0xFFFFFFFFu, over)) {
+            tmem_st32(tS, pk);
+            tmem_st32(tS + 32, pk + 32);
+          } else {
+            over = true;
           }
         }
-        l += l0 + l1;
-        tmem_st32(tS, sr);
-        tmem_st32(tS + 32, sr + 32);
+        if (__any_sync(0xFFFFFFFFu, over)) {
+          // exact path: row maximum first (S is intact in TMEM: no P was stored), rescale,
+          // then recompute and store P chunk by chunk (P chunk c only overwrites S columns
+          // of chunks <= c, which are already read)
+          float mt = -INFINITY;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t sc[32];
+            load_chunk(c, sc);
+            mt = fmaxf(mt, chunk_max(sc));
+          }
+          mt *= sl2;
+          const bool need = mt > m_used + (BF16 ? 8.f : 0.f);
+          if (__any_sync(0xFFFFFFFFu, need)) {
+            const float m_new = need ? mt : m_used;
+            const float f = need ? ex2(m_used - m_new) : 1.f;
+            l *= f;
+            if (o_has) {
+#pragma unroll 1
+              for (int c = 0; c < D / 16; ++c) {
+                uint32_t o[16];
+                tmem_ld16(tO + c * 16, o);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f);
+                tmem_st16(tO + c * 16, o);
+              }
+            }
+            m_used = m_new;
+          }
+          const float msub = (m_used == -INFINITY) ? 0.f : m_used;
+          la = make_float2(0.f, 0.f);
+          lb = la;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t sc[32], pc[16];
+            load_chunk(c, sc);
+            exp_chunk(c, sc, msub, pc);
+            tmem_st16(tS + c * 16, pc);
+          }
+        }
+        l += (la.x + la.y) + (lb.x + lb.y);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -740,7 +799,8 @@ cudaError_t launch_attn_tc(int head_dim, bool bf16, const TcParams& p, int num_s
 
 cudaError_t launch_schedule(const int32_t* ts, const int64_t* tss, const void* counts, const int64_t* cs,
                             int counts_is_int, int B, int Hts, int num_packed, int seq_k, int window, int nmb,
-                            int nblk, int2* sched, int32_t* blkmin, int want_blkmin, cudaStream_t st) {
+                            int nblk, int2* sched, int32_t* blkmin, int want_blkmin, float* blkw,
+                            cudaStream_t st) {
   if (B * Hts == 0) return cudaSuccess;
   const size_t sm = static_cast<size_t>(nblk > 0 ? nblk : 1) * sizeof(int32_t);
   if (sm > 200 * 1024) return cudaErrorInvalidValue;
@@ -750,7 +810,8 @@ cudaError_t launch_schedule(const int32_t* ts, const int64_t* tss, const void* c
     if (e != cudaSuccess) return e;
   }
   schedule_kernel<<<B * Hts, 256, sm, st>>>(ts, tss[0], tss[1], tss[2], counts, cs[0], cs[1], cs[2], counts_is_int,
-                                            Hts, num_packed, seq_k, window, nmb, nblk, sched, blkmin, want_blkmin);
+                                            Hts, num_packed, seq_k, window, nmb, nblk, sched, blkmin, want_blkmin,
+                                            blkw);
   return cudaGetLastError();
 }
 

@@ -22,7 +22,7 @@ cudaError_t launch_scatter_pack(int, const void*, const void*, void*, void*, int
                                 int64_t, int64_t, cudaStream_t);
 cudaError_t launch_rope(int, const void*, const int64_t*, void*, const int64_t*, const void*, const void*,
                         const int64_t*, int64_t, int64_t, int64_t, int64_t, cudaStream_t);
-cudaError_t launch_periodic_meta(int32_t*, int32_t*, int64_t, int64_t, int64_t, int64_t, cudaStream_t);
+cudaError_t launch_periodic_meta(int32_t*, int32_t*, float*, int64_t, int64_t, int64_t, int64_t, cudaStream_t);
 cudaError_t launch_pack_from_keep(int, const int32_t*, const int64_t*, const void*, const int64_t*, const void*,
                                   const int64_t*, void*, void*, const int64_t*, int32_t*, int32_t*, const int64_t*,
                                   int32_t*, int64_t, int64_t, int64_t, int64_t, int64_t, int32_t*, int32_t*,
@@ -30,7 +30,7 @@ cudaError_t launch_pack_from_keep(int, const int32_t*, const int64_t*, const voi
 cudaError_t launch_attn_simt(int, const SimtParams&, cudaStream_t);
 cudaError_t launch_attn_tc(int, bool, const TcParams&, int, cudaStream_t);
 cudaError_t launch_schedule(const int32_t*, const int64_t*, const void*, const int64_t*, int, int, int, int, int,
-                            int, int, int, int2*, int32_t*, int, cudaStream_t);
+                            int, int, int, int2*, int32_t*, int, float*, cudaStream_t);
 cudaError_t launch_decode_update(int, int, bool, const void*, const void*, void*, void*, void*, void*, int32_t*,
                                  int32_t*, int32_t*, int64_t, int64_t, float, int64_t, const int64_t*,
                                  const int64_t*, const int64_t*, const int64_t*, int64_t, int64_t, int64_t, int64_t,
@@ -174,7 +174,7 @@ size_t dab_hybrid_flash_workspace_size(int64_t batch, int64_t ts_heads, int64_t 
   const int64_t nmb = (seq_len_q + 127) / 128;
   const int64_t nblk = (num_packed + 127) / 128;
   return WS_HEADER + round256(static_cast<size_t>(batch * ts_heads * nmb) * 8) +
-         round256(static_cast<size_t>(batch * ts_heads * (nblk > 0 ? nblk : 1)) * 4);
+         2 * round256(static_cast<size_t>(batch * ts_heads * (nblk > 0 ? nblk : 1)) * 4);
 }
 
 static int run_attention(int variant, int causal, const void* q, const void* kd, const void* vd, const void* kp,
@@ -224,6 +224,8 @@ static int run_attention(int variant, int causal, const void* q, const void* kd,
       p.err = reinterpret_cast<int*>(ws);
       p.sched = reinterpret_cast<const int2*>(ws + WS_HEADER);
       p.blkmin = reinterpret_cast<const int32_t*>(ws + WS_HEADER + round256(static_cast<size_t>(B * Hts * nmb) * 8));
+      p.blkw = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(p.blkmin) +
+                                              round256(static_cast<size_t>(B * Hts * (nblk > 0 ? nblk : 1)) * 4));
       p.out = out;
       p.os_b = os[0]; p.os_h = os[1]; p.os_m = os[2];
       p.ts = ts; p.ts_b = tss ? tss[0] : 0; p.ts_h = tss ? tss[1] : 0; p.ts_n = tss ? tss[2] : 0;
@@ -249,7 +251,8 @@ static int run_attention(int variant, int causal, const void* q, const void* kd,
                                         static_cast<int>(Hts), static_cast<int>(num_packed), static_cast<int>(seq_k),
                                         static_cast<int>(window), static_cast<int>(nmb), static_cast<int>(nblk),
                                         reinterpret_cast<int2*>(ws + WS_HEADER),
-                                        reinterpret_cast<int32_t*>(const_cast<int32_t*>(p.blkmin)), variant == 2, st);
+                                        reinterpret_cast<int32_t*>(const_cast<int32_t*>(p.blkmin)), variant == 2,
+                                        const_cast<float*>(p.blkw), st);
         if (e != cudaSuccess) return cuda_status(e, "schedule");
       } else if (variant != 3) {
         // no packed keys: phase 1 is empty and phase 2 starts at key 0
@@ -370,12 +373,13 @@ int dab_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* y_
                      "rope");
 }
 
-int dab_periodic_meta(int32_t* packed_ts, int32_t* packed_counts, int64_t batch_heads, int64_t num_packed,
-                      int64_t seq_len, int64_t period, void* stream) {
+int dab_periodic_meta(int32_t* packed_ts, int32_t* packed_counts, float* packed_counts_f32, int64_t batch_heads,
+                      int64_t num_packed, int64_t seq_len, int64_t period, void* stream) {
   if (!packed_ts || !packed_counts) return fail(1, "dab_periodic_meta: null pointer");
   if (period < 1) return fail(1, "dab_periodic_meta: period must be >= 1");
   if (num_packed != (seq_len + period - 1) / period) return fail(1, "dab_periodic_meta: num_packed != ceil(N/period)");
-  return cuda_status(launch_periodic_meta(packed_ts, packed_counts, batch_heads, num_packed, seq_len, period,
+  return cuda_status(launch_periodic_meta(packed_ts, packed_counts, packed_counts_f32, batch_heads, num_packed,
+                                          seq_len, period,
                                           static_cast<cudaStream_t>(stream)),
                      "periodic_meta");
 }

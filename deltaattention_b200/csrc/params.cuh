@@ -31,6 +31,7 @@ struct TcParams {
   int64_t cs_b, cs_h, cs_n;
   const int2* sched;       // [B*Hts][nmb] = (phase-1 blocks, dense start block)
   const int32_t* blkmin;   // [B*Hts][nblk] smallest valid timestamp of each packed block
+  const float* blkw;       // [B*Hts][nblk] log2 of the block's common count, NaN if counts differ
   int* err;
   float scale_log2;        // sm_scale * log2(e)
   int seq_q, seq_k, num_packed;

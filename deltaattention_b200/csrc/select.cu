@@ -289,20 +289,23 @@ cudaError_t launch_rope(int dtype, const void* x, const int64_t* xs, void* y, co
 // periodic packing metadata: anchor j sits at j*period and covers min(period, N - j*period)
 // tokens (modeling_llama.py:626-632 + :655-685 for keep = t % period == 0)
 // ---------------------------------------------------------------------------------------
-__global__ void periodic_meta_kernel(int32_t* ts, int32_t* counts, int64_t BH, int64_t M, int64_t N,
-                                     int64_t period) {
+__global__ void periodic_meta_kernel(int32_t* ts, int32_t* counts, float* counts_f, int64_t BH, int64_t M,
+                                     int64_t N, int64_t period) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= BH * M) return;
   const int64_t j = idx % M;
   const int64_t p = j * period;
+  const int64_t c = min(period, N - p);
   ts[idx] = static_cast<int32_t>(p);
-  counts[idx] = static_cast<int32_t>(min(period, N - p));
+  counts[idx] = static_cast<int32_t>(c);
+  if (counts_f) counts_f[idx] = static_cast<float>(c);
 }
 
-cudaError_t launch_periodic_meta(int32_t* ts, int32_t* counts, int64_t BH, int64_t M, int64_t N, int64_t period,
-                                 cudaStream_t st) {
+cudaError_t launch_periodic_meta(int32_t* ts, int32_t* counts, float* counts_f, int64_t BH, int64_t M, int64_t N,
+                                 int64_t period, cudaStream_t st) {
   if (BH * M == 0) return cudaSuccess;
-  periodic_meta_kernel<<<static_cast<unsigned>((BH * M + 255) / 256), 256, 0, st>>>(ts, counts, BH, M, N, period);
+  periodic_meta_kernel<<<static_cast<unsigned>((BH * M + 255) / 256), 256, 0, st>>>(ts, counts, counts_f, BH, M, N,
+                                                                                   period);
   return cudaGetLastError();
 }
 

@@ -52,8 +52,14 @@ class Packed:
     k: torch.Tensor          # [B, Hkv, M, d] (possibly a strided view)
     v: torch.Tensor
     timestamps: torch.Tensor  # [B, Hkv, M] int32
-    counts: torch.Tensor      # [B, Hkv, M] int32
+    counts: torch.Tensor      # [B, Hkv, M] int32 (the reference's format)
     keep_mask: Optional[torch.Tensor] = None
+    counts_f32: Optional[torch.Tensor] = None  # the same counts as fp32 (what attention weights with)
+
+    def weights(self) -> torch.Tensor:
+        if self.counts_f32 is None:
+            self.counts_f32 = self.counts.float()
+        return self.counts_f32
 
 
 def pack_periodic(k_rot: torch.Tensor, v: torch.Tensor, period: int) -> Packed:
@@ -62,9 +68,11 @@ def pack_periodic(k_rot: torch.Tensor, v: torch.Tensor, period: int) -> Packed:
     M = -(-N // period)
     ts = torch.empty((B, H, M), dtype=torch.int32, device=k_rot.device)
     cnt = torch.empty_like(ts)
+    cnt_f = torch.empty((B, H, M), dtype=torch.float32, device=k_rot.device)
     st = L.stream_of(k_rot)
-    L.check(L.load().dab_periodic_meta(L.ptr(ts), L.ptr(cnt), B * H, M, N, period, st), "periodic_meta")
-    return Packed(k_rot[:, :, ::period], v[:, :, ::period], ts, cnt)
+    L.check(L.load().dab_periodic_meta(L.ptr(ts), L.ptr(cnt), L.ptr(cnt_f), B * H, M, N, period, st),
+            "periodic_meta")
+    return Packed(k_rot[:, :, ::period], v[:, :, ::period], ts, cnt, counts_f32=cnt_f)
 
 
 def delta_keep_mask(k_rot: torch.Tensor, threshold: float, similarity: str = "euclidean", chunk_size: int = 512):
@@ -136,7 +144,7 @@ def attention(q_rot, k_rot, v, packed: Optional[Packed], *, sm_scale=None, dense
     vp = packed.v if packed is not None else v
     ts = packed.timestamps if packed is not None else torch.zeros((B, Hkv, 1), dtype=torch.int32,
                                                                    device=q_rot.device)
-    cnt = packed.counts if packed is not None else ts
+    cnt = packed.weights() if packed is not None else ts
     lib = L.load()
     st = L.stream_of(q_rot)
     wsb = lib.dab_hybrid_flash_workspace_size(B, Hkv, N, M)

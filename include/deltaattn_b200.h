@@ -138,10 +138,12 @@ int dab_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* y_
 /* Packed timestamps / counts of periodic packing (modeling_llama.py:626-632 followed by
  * :655-685): anchor j at j*period covering min(period, seq_len - j*period) tokens.
  * Buffers are [batch_heads][num_packed] contiguous; num_packed must be ceil(seq_len/period).
+ * `packed_counts_f32` (optional, may be NULL) receives the counts as fp32, the form the
+ * attention kernel weights probabilities with.
  * The packed K/V rows of periodic packing are a strided view of K/V (row stride x period),
  * so no copy is made. */
-int dab_periodic_meta(int32_t* packed_ts, int32_t* packed_counts, int64_t batch_heads, int64_t num_packed,
-                      int64_t seq_len, int64_t period, void* stream);
+int dab_periodic_meta(int32_t* packed_ts, int32_t* packed_counts, float* packed_counts_f32, int64_t batch_heads,
+                      int64_t num_packed, int64_t seq_len, int64_t period, void* stream);
 
 /* Scratch bytes dab_pack_from_keep needs. */
 size_t dab_pack_from_keep_workspace_size(int64_t batch, int64_t heads, int64_t seq_len);
