@@ -556,9 +556,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       bool o_has = false;
       TileSeq seq;
       seq.init(p, U);
+      const float* wrow = p.blkw + (static_cast<int64_t>(U.b) * p.Hts + U.hts[x]) * p.nblk;
       TileInfo t;
       bool ok = true;
       while (seq.next(p, U, t)) {
+        // log2 weight of a packed block (NaN when its counts differ)
+        const float lw = t.packed ? wrow[t.idx] : 0.f;
         int ks, vs = -1;
         uint32_t fp, ep, vfp = 0;
         ring.take(NS, ks, fp, ep);
@@ -569,12 +572,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         tc_fence_after();
         const uint32_t* cnt = reinterpret_cast<const uint32_t*>(auxc + vs * TC_BN);
         const bool cint = p.counts_is_int != 0;
-        // packed block with one common count: weight through the exponent (no per-key work)
-        const float lw = t.packed ? p.blkw[(static_cast<int64_t>(U.b) * p.Hts + U.hts[x]) * p.nblk + t.idx] : 0.f;
+        // a packed block with one common count is weighted through the exponent (no per-key work)
         const bool perkey = t.packed && !(lw == lw);  // NaN: counts differ inside the block
         const int32_t* tsv = auxt + vs * TC_BN;
-        if (t.packed) {
-          // the packed block's counts arrive with its V tile
+        if (perkey || (t.packed && p.variant == TC_PURE)) {
+          // per-key counts (and timestamps) arrive with the block's V tile
           if (!warp_wait(slot_full + vs, vfp, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
         }
         const int n0 = t.idx * TC_BN;
@@ -606,7 +608,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           }
         }
         // S chunk c (columns 32c..32c+31) with masked columns set to -inf
-        const bool any_mask = (p.variant == TC_PURE) || lim < TC_BN;  // only edge / diagonal tiles
+        const bool any_mask = __any_sync(0xFFFFFFFFu, (p.variant == TC_PURE) || lim < TC_BN);
         auto load_chunk = [&](int c, uint32_t* sc) {
           tmem_ld32(tS + c * 32, sc);
           if (any_mask) {
@@ -627,58 +629,59 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           }
           return fmaxf(m0, m1);
         };
-        // probabilities of chunk c against reference msub, count-weighted on packed blocks,
-        // packed as bf16x2 / f16x2 pairs into out[0..15]; row sums into la / lb
+        // probabilities 2^(s*scale + nb) of one 32-column chunk, packed as bf16x2 / f16x2
+        // pairs into out[0..15]; row sums into la / lb
         float2 la = make_float2(0.f, 0.f), lb = la;
-        auto exp_chunk = [&](int c, const uint32_t* sc, float msub, uint32_t* out) {
-          const float nb = (perkey ? 0.f : lw) - msub;
-          if (perkey) {
+        auto exp_plain = [&](const uint32_t* sc, float nb, uint32_t* out) {
 #pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              const uint4 cb = *reinterpret_cast<const uint4*>(cnt + c * 32 + e);
-              const uint32_t cu[4] = {cb.x, cb.y, cb.z, cb.w};
-              float pe[4];
+          for (int e = 0; e < 32; e += 4) {
+            float pe[4];
 #pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float ck = cint ? static_cast<float>(static_cast<int32_t>(cu[k])) : __uint_as_float(cu[k]);
-                pe[k] = ex2(fmaf(__uint_as_float(sc[e + k]), sl2, nb)) * ck;
-              }
-              la.x += pe[0]; la.y += pe[1]; lb.x += pe[2]; lb.y += pe[3];
-              out[e / 2] = pack2(pe[0], pe[1], BF16);
-              out[e / 2 + 1] = pack2(pe[2], pe[3], BF16);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              float pe[4];
-#pragma unroll
-              for (int k = 0; k < 4; ++k) pe[k] = ex2(fmaf(__uint_as_float(sc[e + k]), sl2, nb));
-              la.x += pe[0]; la.y += pe[1]; lb.x += pe[2]; lb.y += pe[3];
-              out[e / 2] = pack2(pe[0], pe[1], BF16);
-              out[e / 2 + 1] = pack2(pe[2], pe[3], BF16);
-            }
+            for (int k = 0; k < 4; ++k) pe[k] = ex2(fmaf(__uint_as_float(sc[e + k]), sl2, nb));
+            la.x += pe[0]; la.y += pe[1]; lb.x += pe[2]; lb.y += pe[3];
+            out[e / 2] = pack2(pe[0], pe[1], BF16);
+            out[e / 2 + 1] = pack2(pe[2], pe[3], BF16);
           }
         };
-        // fast path: exponentiate against the running reference while checking whether this
-        // tile raises the row maximum past it (+2^8 for bf16; fp16 takes the exact path)
-        bool over = !BF16 || (m_used == -INFINITY);
+        // the same with a per-key count weight (packed blocks whose counts differ)
+        auto exp_counted = [&](int c, const uint32_t* sc, float nb, uint32_t* out) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            const uint4 cb = *reinterpret_cast<const uint4*>(cnt + c * 32 + e);
+            const uint32_t cu[4] = {cb.x, cb.y, cb.z, cb.w};
+            float pe[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float ck = cint ? static_cast<float>(static_cast<int32_t>(cu[k])) : __uint_as_float(cu[k]);
+              pe[k] = ex2(fmaf(__uint_as_float(sc[e + k]), sl2, nb)) * ck;
+            }
+            la.x += pe[0]; la.y += pe[1]; lb.x += pe[2]; lb.y += pe[3];
+            out[e / 2] = pack2(pe[0], pe[1], BF16);
+            out[e / 2 + 1] = pack2(pe[2], pe[3], BF16);
+          }
+        };
+        // fast path (warp-uniform; bf16, unmasked tile, one weight per block, every row already
+        // holding a finite reference): exponentiate against the running reference while checking
+        // whether this tile raises the row maximum past it by more than 2^8. It is the only
+        // unrolled copy of the exponential loop, which keeps the hot code small.
+        bool over = !(BF16 && !perkey && !any_mask) || __any_sync(0xFFFFFFFFu, m_used == -INFINITY);
         if (!over) {
           uint32_t pk[TC_BN / 2];
+          const float nb = lw - m_used;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t sc[32];
-            load_chunk(c, sc);
+            tmem_ld32(tS + c * 32, sc);
             over |= chunk_max(sc) * sl2 > m_used + 8.f;
-            exp_chunk(c, sc, m_used, pk + c * 16);
+            exp_plain(sc, nb, pk + c * 16);
           }
-          if (!__any_sync(0xFFFFFFFFu, over)) {
+          over = __any_sync(0xFFFFFFFFu, over);
+          if (!over) {
             tmem_st32(tS, pk);
             tmem_st32(tS + 32, pk + 32);
-          } else {
-            over = true;
           }
         }
-        if (__any_sync(0xFFFFFFFFu, over)) {
+        if (over) {
           // exact path: row maximum first (S is intact in TMEM: no P was stored), rescale,
           // then recompute and store P chunk by chunk (P chunk c only overwrites S columns
           // of chunks <= c, which are already read)
@@ -714,7 +717,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           for (int c = 0; c < 4; ++c) {
             uint32_t sc[32], pc[16];
             load_chunk(c, sc);
-            exp_chunk(c, sc, msub, pc);
+            if (perkey) exp_counted(c, sc, -msub, pc);
+            else exp_plain(sc, lw - msub, pc);
             tmem_st16(tS + c * 16, pc);
           }
         }

@@ -109,10 +109,23 @@ struct Abort {
   int* err_gmem;            // caller-visible error word (first error wins)
 };
 
+// try_wait with a suspend-time hint: the hardware parks the thread until the phase completes
+// or ~`ns` nanoseconds pass, so a waiting warp takes no issue slots from warps sharing its
+// scheduler (a hint-less try_wait returns almost at once and the loop would spin hot)
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, const Abort& ab, int code) {
   const uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
     if (*ab.flag_smem) return false;
     if (globaltimer() - t0 > DAB_WAIT_TIMEOUT_NS) {
       *ab.flag_smem = 1;
