@@ -661,33 +661,48 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           }
         };
         // fast path (warp-uniform; bf16, unmasked tile, one weight per block, every row already
-        // holding a finite reference): exponentiate against the running reference while checking
-        // whether this tile raises the row maximum past it by more than 2^8. It is the only
-        // unrolled copy of the exponential loop, which keeps the hot code small.
-        bool over = !(BF16 && !perkey && !any_mask) || __any_sync(0xFFFFFFFFu, m_used == -INFINITY);
-        if (!over) {
-          uint32_t pk[TC_BN / 2];
+        // holding a finite reference): S streams through two register buffers (the load of chunk
+        // c+1 is in flight while chunk c is exponentiated against the running reference) and
+        // each P chunk is stored as soon as it is computed. P chunk c covers columns
+        // 16c..16c+15, below every S chunk not yet read. A chunk that raises some row's maximum
+        // more than 2^8 above its reference stops the stream: the repair path below takes over
+        // from that chunk. This is the only unrolled copy of the exponential loop.
+        const bool fast = BF16 && !perkey && !any_mask && !__any_sync(0xFFFFFFFFu, m_used == -INFINITY);
+        int stop = 0;  // first chunk the fast path did not finish
+        if (fast) {
           const float nb = lw - m_used;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t sc[32];
-            tmem_ld32(tS + c * 32, sc);
-            over |= chunk_max(sc) * sl2 > m_used + 8.f;
-            exp_plain(sc, nb, pk + c * 16);
-          }
-          over = __any_sync(0xFFFFFFFFu, over);
-          if (!over) {
-            tmem_st32(tS, pk);
-            tmem_st32(tS + 32, pk + 32);
-          }
+          const float lim_raise = m_used + 8.f;
+          uint32_t sa[32], sb[32];
+          tmem_ld32_async(tS, sa);
+          tmem_ld32_wait(sa);
+          tmem_ld32_async(tS + 32, sb);
+          // one chunk: false when it stops the stream (no load is left in flight then)
+          auto step = [&](int c, uint32_t(&sc)[32], uint32_t(&sn)[32]) -> bool {
+            if (__any_sync(0xFFFFFFFFu, chunk_max(sc) * sl2 > lim_raise)) {
+              if (c < 3) tmem_ld32_wait(sn);
+              stop = c;
+              return false;
+            }
+            uint32_t pc[16];
+            exp_plain(sc, nb, pc);
+            tmem_st16(tS + c * 16, pc);
+            if (c < 3) {
+              tmem_ld32_wait(sn);
+              if (c < 2) tmem_ld32_async(tS + (c + 2) * 32, sc);
+            }
+            return true;
+          };
+          if (step(0, sa, sb) && step(1, sb, sa) && step(2, sa, sb) && step(3, sb, sa)) stop = 4;
         }
-        if (over) {
-          // exact path: row maximum first (S is intact in TMEM: no P was stored), rescale,
-          // then recompute and store P chunk by chunk (P chunk c only overwrites S columns
-          // of chunks <= c, which are already read)
+        if (stop < 4) {
+          // exact / repair path from chunk `stop`: the row maximum over the chunks not yet done
+          // (their S columns are intact), then a rescale of everything accumulated so far, then
+          // P of the remaining chunks. After a fast-path stop the reference moves up by a whole
+          // number of octaves, so the P chunks already stored rescale exactly (power of two).
+          tmem_st_wait();
           float mt = -INFINITY;
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = stop; c < 4; ++c) {
             uint32_t sc[32];
             load_chunk(c, sc);
             mt = fmaxf(mt, chunk_max(sc));
@@ -695,9 +710,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           mt *= sl2;
           const bool need = mt > m_used + (BF16 ? 8.f : 0.f);
           if (__any_sync(0xFFFFFFFFu, need)) {
-            const float m_new = need ? mt : m_used;
-            const float f = need ? ex2(m_used - m_new) : 1.f;
+            float m_new = m_used, f = 1.f;
+            if (need) {
+              if (stop > 0) {
+                const int k = static_cast<int>(ceilf(mt - m_used));
+                m_new = m_used + static_cast<float>(k);
+                f = k < 127 ? __int_as_float((127 - k) << 23) : 0.f;
+              } else {
+                m_new = mt;
+                f = ex2(m_used - m_new);
+              }
+            }
             l *= f;
+            la.x *= f; la.y *= f; lb.x *= f; lb.y *= f;
             if (o_has) {
 #pragma unroll 1
               for (int c = 0; c < D / 16; ++c) {
@@ -708,13 +733,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
                 tmem_st16(tO + c * 16, o);
               }
             }
+            if (BF16) {
+#pragma unroll 1
+              for (int c = 0; c < stop; ++c) {
+                uint32_t pc[16];
+                tmem_ld16(tS + c * 16, pc);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const float lo = __uint_as_float(pc[j] << 16) * f;
+                  const float hi = __uint_as_float(pc[j] & 0xFFFF0000u) * f;
+                  pc[j] = pack2(lo, hi, true);
+                }
+                tmem_st16(tS + c * 16, pc);
+              }
+            }
             m_used = m_new;
           }
           const float msub = (m_used == -INFINITY) ? 0.f : m_used;
-          la = make_float2(0.f, 0.f);
-          lb = la;
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = stop; c < 4; ++c) {
             uint32_t sc[32], pc[16];
             load_chunk(c, sc);
             if (perkey) exp_counted(c, sc, -msub, pc);

@@ -243,6 +243,28 @@ def test_tcgen05_vs_simt_and_oracle(variant, dt, D):
     _check_ws_clean()
 
 
+@pytest.mark.parametrize("variant", ["hybrid", "sanity", "pure_phase1"])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_tcgen05_score_jumps(variant, dt):
+    """Keys planted with ever larger scores in the middle of blocks (later 32-column chunks of
+    packed and dense tiles): every row's running maximum jumps far past its reference mid-tile,
+    which exercises the rescale of partly written probabilities."""
+    H, N, D = 2, 1500, 128
+    q, k, v = I.attn_inputs(1, H, N, D, dt, 77)
+    q = (q.float() + 1.0).to(dt)
+    k = k.float()
+    for i, t in enumerate([300, 400, 680, 700, 1100, 1400]):  # dense chunks 1-3; packed t % 4 == 0
+        k[:, :, t, :] += 2.0 + 0.75 * i
+    k = k.to(dt)
+    keep = O.periodic_keep_mask(1, H, N, 0.25)
+    _, kp, vp, ts, counts = O.pack_from_keep(k, v, keep)
+    ref = O.hybrid_attention(q, k, v, kp, vp, ts, counts.float(), D ** -0.5, 128, variant)
+    c = lambda t: t.cuda().contiguous()  # noqa: E731
+    out = _launch_variant(variant, c(q), c(k), c(v), c(kp), c(vp), c(ts), c(counts.float()), 128)
+    _cmp(out, ref, dt, f"tc-jumps/{variant}")
+    _check_ws_clean()
+
+
 @pytest.mark.parametrize("mode", ["periodic", "delta"])
 def test_native_gqa_prefill_matches_oracle(mode):
     """ops.delta_prefill: RoPE + selection + device packing + GQA-by-index attention."""
