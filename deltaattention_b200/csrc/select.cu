@@ -262,12 +262,88 @@ __global__ void __launch_bounds__(256) rope_kernel(const T* __restrict__ x, int6
   yr[(i + half) * yd] = from_f32<T>(o2);
 }
 
+// Contiguous-row RoPE (unit stride along d in x, y and the tables): one thread loads 16 bytes
+// of the first half of a row and the matching 16 bytes of the second half, with the same
+// per-element rounding sequence as rope_kernel. Grid: (rows of one head / rows per block,
+// heads, batch), so no index division by runtime sizes.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) rope_rows_kernel(const T* __restrict__ x, int64_t xb, int64_t xh, int64_t xs,
+                                                        T* __restrict__ y, int64_t yb, int64_t yh, int64_t ys,
+                                                        const T* __restrict__ cs, const T* __restrict__ sn,
+                                                        int64_t cb, int64_t cs_s, int N) {
+  constexpr int V = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte vector
+  constexpr int HALF = D / 2;
+  constexpr int TPR = HALF / V;                          // threads per row
+  constexpr int RPB = 256 / TPR;                         // rows per block
+  const int s = blockIdx.x * RPB + static_cast<int>(threadIdx.x) / TPR;
+  if (s >= N) return;
+  const int i = (static_cast<int>(threadIdx.x) % TPR) * V;
+  const int64_t b = blockIdx.z, h = blockIdx.y;
+  const T* xr = x + b * xb + h * xh + s * xs;
+  T* yr = y + b * yb + h * yh + s * ys;
+  const int64_t c0 = b * cb + s * cs_s;
+  union Vec { uint4 u; T e[V]; };
+  Vec x1, x2, c1, c2, s1, s2, o1, o2;
+  x1.u = *reinterpret_cast<const uint4*>(xr + i);
+  x2.u = *reinterpret_cast<const uint4*>(xr + i + HALF);
+  c1.u = __ldg(reinterpret_cast<const uint4*>(cs + c0 + i));
+  c2.u = __ldg(reinterpret_cast<const uint4*>(cs + c0 + i + HALF));
+  s1.u = __ldg(reinterpret_cast<const uint4*>(sn + c0 + i));
+  s2.u = __ldg(reinterpret_cast<const uint4*>(sn + c0 + i + HALF));
+#pragma unroll
+  for (int e = 0; e < V; ++e) {
+    const float a1 = to_f32(x1.e[e]), a2 = to_f32(x2.e[e]);
+    o1.e[e] = from_f32<T>(__fadd_rn(round_as<T>(__fmul_rn(a1, to_f32(c1.e[e]))),
+                                    round_as<T>(__fmul_rn(-a2, to_f32(s1.e[e])))));
+    o2.e[e] = from_f32<T>(__fadd_rn(round_as<T>(__fmul_rn(a2, to_f32(c2.e[e]))),
+                                    round_as<T>(__fmul_rn(a1, to_f32(s2.e[e])))));
+  }
+  *reinterpret_cast<uint4*>(yr + i) = o1.u;
+  *reinterpret_cast<uint4*>(yr + i + HALF) = o2.u;
+}
+
+template <typename T, int D>
+static bool try_rope_rows(const void* x, const int64_t* xs, void* y, const int64_t* ys, const void* cs, const void* sn,
+                          const int64_t* css, int64_t B, int64_t H, int64_t N, cudaStream_t st, cudaError_t* err) {
+  constexpr int V = 16 / static_cast<int>(sizeof(T));
+  constexpr int RPB = 256 / (D / 2 / V);
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (xs[3] != 1 || ys[3] != 1 || css[2] != 1) return false;
+  if (!al(x) || !al(y) || !al(cs) || !al(sn)) return false;
+  for (int64_t v : {xs[0], xs[1], xs[2], ys[0], ys[1], ys[2], css[0], css[1]})
+    if (v % V != 0) return false;
+  if (B > 65535 || H > 65535 || N > (int64_t{1} << 30)) return false;
+  const dim3 grid(static_cast<unsigned>((N + RPB - 1) / RPB), static_cast<unsigned>(H), static_cast<unsigned>(B));
+  rope_rows_kernel<T, D><<<grid, 256, 0, st>>>(static_cast<const T*>(x), xs[0], xs[1], xs[2], static_cast<T*>(y), ys[0],
+                                               ys[1], ys[2], static_cast<const T*>(cs), static_cast<const T*>(sn),
+                                               css[0], css[1], static_cast<int>(N));
+  *err = cudaGetLastError();
+  return true;
+}
+
+template <typename T>
+static bool try_rope_rows_d(const void* x, const int64_t* xs, void* y, const int64_t* ys, const void* cs,
+                            const void* sn, const int64_t* css, int64_t B, int64_t H, int64_t N, int64_t D,
+                            cudaStream_t st, cudaError_t* err) {
+  switch (D) {
+    case 64: return try_rope_rows<T, 64>(x, xs, y, ys, cs, sn, css, B, H, N, st, err);
+    case 128: return try_rope_rows<T, 128>(x, xs, y, ys, cs, sn, css, B, H, N, st, err);
+    case 256: return try_rope_rows<T, 256>(x, xs, y, ys, cs, sn, css, B, H, N, st, err);
+    default: return false;
+  }
+}
+
 cudaError_t launch_rope(int dtype, const void* x, const int64_t* xs, void* y, const int64_t* ys, const void* cs,
                         const void* sn, const int64_t* css, int64_t B, int64_t H, int64_t N, int64_t D,
                         cudaStream_t st) {
   const int64_t rows = B * H * N;
   if (rows == 0) return cudaSuccess;
   if (D % 2) return cudaErrorInvalidValue;
+  cudaError_t e = cudaSuccess;
+  // in-place calls (y == x) are safe on both paths: every element is read and written by one thread
+  if (dtype == BF16 && try_rope_rows_d<__nv_bfloat16>(x, xs, y, ys, cs, sn, css, B, H, N, D, st, &e)) return e;
+  if (dtype == F16 && try_rope_rows_d<__half>(x, xs, y, ys, cs, sn, css, B, H, N, D, st, &e)) return e;
+  if (dtype == F32 && try_rope_rows_d<float>(x, xs, y, ys, cs, sn, css, B, H, N, D, st, &e)) return e;
   const int64_t work = rows * (D / 2);
   const unsigned blocks = static_cast<unsigned>((work + 255) / 256);
 #define DAB_RP(TY)                                                                                              \

@@ -155,6 +155,26 @@ def test_rope_matches_reference(golden, dt_name, dt):
     np.testing.assert_array_equal(y.float().cpu().numpy(), g["out"])
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("layout", ["contiguous", "projection", "d_strided", "d96"])
+def test_rope_layouts_match_oracle(dt, layout):
+    """Both RoPE kernels (16-byte rows and the generic strided one) against the oracle, bit-exact."""
+    from deltaattention_b200 import ops
+    D = 96 if layout == "d96" else 128
+    B, H, N = 2, 3, 257
+    base = torch.from_numpy(I.ar1_keys(B, H, N, D, seed=12, offset=True)).to(dt)
+    cos, sin = O.rope_cos_sin(N, D, 500000.0, dt)
+    ref = O.apply_rope(base, cos, sin)
+    if layout == "projection":      # [B, N, H, D] storage viewed as [B, H, N, D]
+        x = base.transpose(1, 2).contiguous().cuda().transpose(1, 2)
+    elif layout == "d_strided":     # d is not the unit-stride axis: generic kernel
+        x = base.transpose(2, 3).contiguous().cuda().transpose(2, 3)
+    else:
+        x = base.cuda()
+    y = ops.rope(x, cos.cuda(), sin.cuda())
+    np.testing.assert_array_equal(y.float().cpu().numpy(), ref.float().numpy())
+
+
 def test_nm_select_matches_oracle():
     from deltaattention_b200.dropin import nmDeltaFlashAttention as nm
     for (n, m, r, N) in [(2, 4, 4, 2000), (2, 4, 2, 777), (1, 4, 4, 1024), (3, 8, 8, 1500)]:
