@@ -138,7 +138,8 @@ def max_over_ranks(x, world):
     if world == 1:
         return x
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -167,7 +168,7 @@ def cpu_sample(heads=(0,), stride=1, N=CFG["N"]):
     vv = v[:, kv_heads].contiguous()
     keep = O.periodic_keep_mask(1, len(kv_heads), N, 1.0 / CFG["r"])
     _, kp, vp, ts, counts = O.pack_from_keep(k_ref, vv, keep)
-    n_rep = len(heads) if len(kv_heads) == 1 else 1
+    n_rep = len(heads) // len(kv_heads)  # heads are whole GQA groups, or part of one group
     O.hybrid_attention(q_ref, k_ref, vv, kp, vp, ts, counts.float(), CFG["D"] ** -0.5, CFG["W"], n_rep=n_rep,
                        query_blocks=blocks)
     dt = time.perf_counter() - t0
@@ -328,10 +329,10 @@ def run_ours(args, world, rank, local):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
-        dt, tk = cpu_sample((0,))
+        dt, tk = cpu_sample(tuple(range(8)))
         line["cpu_baseline"] = {"value": tk / dt, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                                "sample": f"1 of 32 q-heads of one N={N} layer (RoPE, packing, two-phase "
-                                          f"attention), {dt:.1f} s; tokens scaled by 1/32"}
+                                "sample": f"8 of 32 q-heads (2 whole GQA groups) of one N={N} layer (RoPE, "
+                                          f"packing, two-phase attention), {dt:.1f} s; tokens scaled by 8/32"}
     if rank == 0:
         print(json.dumps(line), flush=True)
 

@@ -64,6 +64,7 @@ class Packed:
 
 def pack_periodic(k_rot: torch.Tensor, v: torch.Tensor, period: int) -> Packed:
     """Periodic packing (modeling_llama.py:626-632 + :655-685) without copies."""
+    L.require_cuda(k_rot, v)
     B, H, N, D = k_rot.shape
     M = -(-N // period)
     ts = torch.empty((B, H, M), dtype=torch.int32, device=k_rot.device)
@@ -82,6 +83,7 @@ def delta_keep_mask(k_rot: torch.Tensor, threshold: float, similarity: str = "eu
     selects cosine, every other value selects squared Euclidean with threshold**2.
     """
     from .launch import chunked_eval_kernel
+    L.require_cuda(k_rot)
     B, H, N, D = k_rot.shape
     cs = min(chunk_size, N) if chunk_size > 0 else N
     nch = max(1, -(-N // cs))
@@ -99,6 +101,7 @@ def delta_keep_mask(k_rot: torch.Tensor, threshold: float, similarity: str = "eu
 def pack_from_keep(k_rot: torch.Tensor, v: torch.Tensor, keep: torch.Tensor, num_packed: Optional[int] = None,
                    want_index_map: bool = False) -> Packed:
     """Device-side index map + scatter + counts (modeling_llama.py:655-685)."""
+    L.require_cuda(k_rot, v, keep)
     B, H, N, D = k_rot.shape
     if num_packed is None:
         num_packed = int(keep.sum(-1).max().item())  # the reference's packed length (modeling_llama.py:656)
@@ -131,6 +134,7 @@ def attention(q_rot, k_rot, v, packed: Optional[Packed], *, sm_scale=None, dense
 
     q_rot [B, Hq, N, d]; k_rot / v / packed tensors [B, Hkv, ...]; out any [B, Hq, N, d] view.
     """
+    L.require_cuda(q_rot, k_rot, v, out)
     B, Hq, N, D = q_rot.shape
     Hkv = k_rot.shape[1]
     if Hq % Hkv:
@@ -162,6 +166,7 @@ def attention(q_rot, k_rot, v, packed: Optional[Packed], *, sm_scale=None, dense
 
 def flash(q_rot, k_rot, v, *, causal=True, sm_scale=None, out=None, force_simt=False):
     """Dense flash attention (flashAttention.py:5-91) with GQA by index: the r = 1 comparator."""
+    L.require_cuda(q_rot, k_rot, v, out)
     B, Hq, N, D = q_rot.shape
     Hkv = k_rot.shape[1]
     if sm_scale is None:
@@ -190,6 +195,7 @@ def delta_prefill(q, k, v, cos, sin, *, mode="periodic", keep_rate=0.25, thresho
     'delta' (threshold selection in chunks of ``chunk_size``) or 'mask' (``keep_mask``).
     Returns the attention output [B, Hq, N, d] (and the packed history when requested).
     """
+    L.require_cuda(q, k, v, cos, sin)
     q_rot = rope(q, cos, sin)
     k_rot = rope(k, cos, sin)
     if mode == "periodic":

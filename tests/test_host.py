@@ -1,0 +1,126 @@
+"""CPU tests of the host side: the C-ABI library, the drop-in shims' argument handling and
+the multi-process plumbing of bench.py (gloo, world size 2). No GPU is touched."""
+import ctypes
+import os
+import re
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+from deltaattention_b200 import _lib as L  # noqa: E402
+
+HEADER = os.path.join(ROOT, "include", "deltaattn_b200.h")
+
+
+def _header_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = re.sub(r"//[^\n]*", "", text)
+    return sorted(set(re.findall(r"\b(dab_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib_path():
+    if not os.path.exists(L.LIB_PATH):
+        from deltaattention_b200 import build
+        build.build()
+    return L.LIB_PATH
+
+
+def test_library_exports_every_header_symbol(lib_path):
+    syms = _header_symbols()
+    assert len(syms) >= 15, syms
+    so = ctypes.CDLL(lib_path)
+    missing = [s for s in syms if not hasattr(so, s)]
+    assert not missing, missing
+    # the ctypes table binds exactly the declared ABI
+    assert sorted(L.SIGNATURES) == syms
+
+
+def test_host_only_entry_points(lib_path):
+    lib = L.load()
+    assert lib.dab_abi_version() >= 1
+    r256 = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    for (B, H, N, M) in [(1, 8, 32768, 8192), (2, 3, 1000, 250), (1, 1, 1, 0)]:
+        nmb, nblk = -(-N // 128), max(1, -(-M // 128))
+        want = 256 + r256(B * H * nmb * 8) + 2 * r256(B * H * nblk * 4)
+        assert lib.dab_hybrid_flash_workspace_size(B, H, N, M) == want
+    assert lib.dab_pack_from_keep_workspace_size(2, 3, 5000) == 4 * 2 * 3 * 5 * 4
+
+
+@pytest.mark.parametrize("n,m,r,N", [(2, 4, 4, 2000), (2, 4, 2, 777), (1, 4, 4, 1024), (3, 8, 8, 1500)])
+def test_nm_packed_length_matches_oracle(lib_path, n, m, r, N):
+    """dab_nm_num_packed (host arithmetic) equals the oracle's kept count per head."""
+    from oracle import delta_oracle as O
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import _inputs as I
+    from deltaattention_b200.dropin import nmDeltaFlashAttention as nm
+    k = I.post_rope_keys(1, 2, N, 64, 5e5, torch.float32, seed=N)
+    keep = O.nm_keep_mask(k, n, m, r)
+    counts = keep.sum(-1).flatten().tolist()
+    assert len(set(counts)) == 1
+    assert nm.nm_num_packed(N, n, m, r) == counts[0]
+
+
+def test_product_path_refuses_cpu_tensors(lib_path):
+    """No CPU fallback: the ops raise instead of computing on host tensors."""
+    from deltaattention_b200 import ops
+    x = torch.zeros(1, 2, 256, 128, dtype=torch.bfloat16)
+    cos = torch.ones(1, 256, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.rope(x, cos, cos)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.flash(x, x, x)
+
+
+def test_kernel_shim_binds_reference_argument_lists():
+    """The drop-in kernel objects accept the reference launch's positional / keyword split and
+    reject a call with a missing argument the way a Triton launch does (TypeError)."""
+    from deltaattention_b200 import launch
+    names = launch.HYBRID_PARAMS
+    args = tuple(range(len(names) - 3))  # everything but BLOCK_M, BLOCK_N, BLOCK_D
+    b = launch._bind(names, args, dict(BLOCK_M=128, BLOCK_N=128, BLOCK_D=64), "hybrid")
+    assert b["BLOCK_D"] == 64 and b[names[0]] == 0 and b[names[len(args) - 1]] == len(args) - 1
+    with pytest.raises(TypeError):
+        launch._bind(names, args[:-1], dict(BLOCK_M=128, BLOCK_N=128, BLOCK_D=64), "hybrid")
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import bench
+        bench.barrier(world)
+        # the bench's timing rule: every rank reports its own time, the job takes the maximum
+        got = bench.max_over_ranks(1.5 + rank, world)
+        out[rank] = got
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bench_max_over_ranks_gloo_world2():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert dict(out) == {0: 2.5, 1: 2.5}
