@@ -298,6 +298,58 @@ int dab_hybrid_flash(int variant, const void* q, const void* k_dense, const void
                        static_cast<cudaStream_t>(stream), "hybrid_flash");
 }
 
+// Static scratch of dab_hybrid_flash_noalloc (one copy per device, zeroed at module load).
+static __device__ __align__(256) uint8_t g_noalloc_scratch[DAB_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+}  // namespace
+
+int dab_hybrid_flash_noalloc(int variant, const void* q, const void* k_dense, const void* v_dense,
+                             const void* k_packed, const void* v_packed, const int32_t* packed_ts,
+                             const void* packed_counts, int counts_is_int, void* out, int dtype,
+                             const int64_t* strides, float sm_scale, int64_t seq_len_q, int64_t seq_len_k,
+                             int64_t num_packed, int64_t head_dim, int64_t num_heads, int64_t dense_window,
+                             int64_t grid_m, int64_t grid_bh, int64_t block_m, int64_t block_n, int64_t block_d,
+                             int64_t kv_group, int force_simt, void* stream) {
+  if (variant < 0 || variant > 2) return fail(1, "dab_hybrid_flash_noalloc: variant must be 0, 1 or 2");
+  if (!strides) return fail(1, "dab_hybrid_flash_noalloc: null strides");
+  if (num_heads <= 0 || kv_group <= 0 || num_heads % kv_group || grid_bh <= 0 || grid_bh % num_heads)
+    return fail(1, "dab_hybrid_flash_noalloc: bad heads / grid");
+  const size_t need = dab_hybrid_flash_workspace_size(grid_bh / num_heads, num_heads / kv_group, seq_len_q,
+                                                      num_packed);
+  if (need > DAB_NOALLOC_SCRATCH_BYTES)
+    return fail(1, "dab_hybrid_flash_noalloc: this call needs " + std::to_string(need) +
+                       " bytes of scratch but the static scratch holds " +
+                       std::to_string(static_cast<size_t>(DAB_NOALLOC_SCRATCH_BYTES)) +
+                       " (batch x heads x query blocks too large); use dab_hybrid_flash with a workspace");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "dab_hybrid_flash_noalloc (cudaGetDevice)");
+  if (dev < 0 || dev >= kMaxDevices) return fail(1, "dab_hybrid_flash_noalloc: device ordinal out of range");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      // resolved with `dev` current: the address is that device's copy of the array
+      e = cudaGetSymbolAddress(&g_noalloc_ptr[dev], g_noalloc_scratch);
+      if (e != cudaSuccess) {
+        g_noalloc_ptr[dev] = nullptr;
+        return cuda_status(e, "dab_hybrid_flash_noalloc (cudaGetSymbolAddress)");
+      }
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  const int64_t* s = strides;
+  return run_attention(variant, 1, q, k_dense, v_dense, k_packed, v_packed, packed_ts, packed_counts,
+                       counts_is_int, out, dtype, s + 0, s + 4, s + 8, s + 12, s + 16, s + 20, s + 23, s + 26,
+                       sm_scale, seq_len_q, seq_len_k, num_packed, head_dim, num_heads, dense_window, grid_m,
+                       grid_bh, block_m, block_n, block_d, kv_group, scratch, DAB_NOALLOC_SCRATCH_BYTES,
+                       force_simt, static_cast<cudaStream_t>(stream), "hybrid_flash_noalloc");
+}
+
 int dab_attn_fwd_flat(const void* q, const void* k, const void* v, float sm_scale, void* out, int dtype,
                       const int64_t* strides, int64_t Z, int64_t H, int64_t n_ctx, int64_t head_dim,
                       int64_t block_m, int64_t block_n, int is_causal, int64_t grid_m, int64_t grid_zh,

@@ -91,6 +91,33 @@ int dab_hybrid_flash(int variant, const void* q, const void* k_dense, const void
                      int64_t grid_m, int64_t grid_bh, int64_t block_m, int64_t block_n, int64_t block_d,
                      int64_t kv_group, void* workspace, size_t workspace_bytes, int force_simt, void* stream);
 
+/* Bytes of the library's static device scratch behind dab_hybrid_flash_noalloc. */
+#define DAB_NOALLOC_SCRATCH_BYTES (1u << 20)
+
+/* No counterpart in the reference (the reference's kernels need no scratch). The same call as
+ * dab_hybrid_flash without the caller workspace: the phase schedule, the per-block
+ * timestamp minima and count weights live in a file-scope device array of
+ * DAB_NOALLOC_SCRATCH_BYTES per device, and the call allocates nothing (no cudaMalloc, no
+ * allocator of any framework). For callers that hold no device allocator: a binding written
+ * against the reference's launch signature alone, which has no scratch argument.
+ * - Limit: dab_hybrid_flash_workspace_size(grid_bh / num_heads, num_heads / kv_group,
+ *   seq_len_q, num_packed) must not exceed DAB_NOALLOC_SCRATCH_BYTES; larger calls return 1
+ *   with a message naming both sizes (e.g. 128 k queries x 64 timestamp heads still fit).
+ * - The first call on a device resolves the scratch address for that device (with that
+ *   device current); make it before any stream capture.
+ * - Zero at start: only the first 4 bytes (the device error word a timed-out in-kernel wait
+ *   sets, never cleared by this entry point); static storage starts zeroed. Every other
+ *   scratch byte a call reads is written earlier in the same call.
+ * - Calls that overlap on one device (other streams or threads) share the scratch and race;
+ *   serialise them. */
+int dab_hybrid_flash_noalloc(int variant, const void* q, const void* k_dense, const void* v_dense,
+                             const void* k_packed, const void* v_packed, const int32_t* packed_ts,
+                             const void* packed_counts, int counts_is_int, void* out, int dtype,
+                             const int64_t* strides, float sm_scale, int64_t seq_len_q, int64_t seq_len_k,
+                             int64_t num_packed, int64_t head_dim, int64_t num_heads, int64_t dense_window,
+                             int64_t grid_m, int64_t grid_bh, int64_t block_m, int64_t block_n, int64_t block_d,
+                             int64_t kv_group, int force_simt, void* stream);
+
 /* _attn_fwd_flat[grid](Q, K, V, sm_scale, Out, 16 strides (q, k, v, out), Z, H, N_CTX,
  *   HEAD_DIM, BLOCK_M, BLOCK_N, IS_CAUSAL) - flashAttention.py:5-91, wrapper
  * triton_flash_attention flashAttention.py:94-130, grid (grid_m, grid_zh). */
