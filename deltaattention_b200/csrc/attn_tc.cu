@@ -33,14 +33,18 @@ constexpr int TC_BN = 128;
 template <int D> struct TcCfg {
   static constexpr int QBYTES = TC_BM * D * 2;
   static constexpr int KVBYTES = TC_BN * D * 2;
-  static constexpr int NSLOT = (D == 128) ? 4 : 8;
+  // separate K and V rings, each with its own producer warp: the K tile of the next block is
+  // loaded as soon as QK^T of the block two back completes, independent of V slot releases
+  static constexpr int NK = (D == 128) ? 2 : 4;
+  static constexpr int NV = (D == 128) ? 2 : 4;
   static constexpr int OFF_Q0 = 0;
   static constexpr int OFF_Q1 = QBYTES;
-  static constexpr int OFF_SLOT = 2 * QBYTES;
-  static constexpr int OFF_AUXC = OFF_SLOT + NSLOT * KVBYTES;
-  static constexpr int OFF_AUXT = OFF_AUXC + NSLOT * TC_BN * 4;
-  static constexpr int OFF_BAR = OFF_AUXT + NSLOT * TC_BN * 4;
-  static constexpr int NBAR = 2 + 2 * NSLOT + 2 * 4 + 1;
+  static constexpr int OFF_K = 2 * QBYTES;
+  static constexpr int OFF_V = OFF_K + NK * KVBYTES;
+  static constexpr int OFF_AUXC = OFF_V + NV * KVBYTES;
+  static constexpr int OFF_AUXT = OFF_AUXC + NV * TC_BN * 4;
+  static constexpr int OFF_BAR = OFF_AUXT + NV * TC_BN * 4;
+  static constexpr int NBAR = 2 + 2 * NK + 2 * NV + 2 * 4 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 64 + 1024;  // + alignment slack
 };
@@ -233,30 +237,21 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t par, const Abo
   return __all_sync(0xFFFFFFFFu, ok);
 }
 
-// ring of K/V slots: the k-th use maps to slot k % NS in round k / NS
-struct Ring {
-  int k;
-  __device__ __forceinline__ void take(int NS, int& slot, uint32_t& full_par, uint32_t& empty_par) {
-    slot = k % NS;
-    const int round = k / NS;
-    full_par = round & 1;
-    empty_par = (round & 1) ^ 1;
-    ++k;
-  }
-};
 
 template <int D, bool BF16>
 __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_constant__ TcParams p) {
   using C = TcCfg<D>;
-  constexpr int NS = C::NSLOT;
+  constexpr int NK = C::NK, NV = C::NV;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
-  uint64_t* slot_full = bars + 2;
-  uint64_t* slot_empty = bars + 2 + NS;
-  uint64_t* s_full = bars + 2 + 2 * NS;       // [2]
+  uint64_t* k_full = bars + 2;                // [NK]
+  uint64_t* k_empty = k_full + NK;            // [NK]
+  uint64_t* v_full = k_empty + NK;            // [NV]
+  uint64_t* v_empty = v_full + NV;            // [NV]
+  uint64_t* s_full = v_empty + NV;            // [2]
   uint64_t* p_full = s_full + 2;              // [2]
   uint64_t* o_full = p_full + 2;              // [2]
   uint64_t* tile_free = o_full + 2;           // [2]
@@ -270,9 +265,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(slot_full + s, 1);
-      mbar_init(slot_empty + s, 1);
+    for (int s = 0; s < NK; ++s) {
+      mbar_init(k_full + s, 1);
+      mbar_init(k_empty + s, 1);
+    }
+    for (int s = 0; s < NV; ++s) {
+      mbar_init(v_full + s, 1);
+      mbar_init(v_empty + s, 1);
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(s_full + x, 1);
@@ -304,18 +303,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
   const int n_iter = (p.num_units + G - 1) / G;
 
   if (warp == 0) {
-    // ================================================================ producer
-    Ring ring{0};
+    // ================================================================ Q + K producer
     uint32_t q_par = 1;
-    int armed[NS];
-    for (int s = 0; s < NS; ++s) armed[s] = -1;
-    int q_issued = 0;
-    const uint32_t kv_bytes = C::KVBYTES;
+    int k_armed[NK];
+    for (int s = 0; s < NK; ++s) k_armed[s] = -1;
+    int kpos = 0, q_issued = 0;
     for (int it = 0; it < n_iter; ++it) {
       const int u = unit_of(it, blockIdx.x, G);
       if (u >= p.num_units) continue;
       const Unit U = decode_unit(p, u);
-      if (!warp_wait(q_empty, q_par, ab, ERR_TIMEOUT_PRODUCER)) goto producer_done;
+      if (!warp_wait(q_empty, q_par, ab, ERR_TIMEOUT_PRODUCER)) goto kprod_done;
       q_par ^= 1;
       if (lane == 0) {
         const uint32_t qb = (U.valid[0] ? C::QBYTES : 0) + (U.valid[1] ? C::QBYTES : 0);
@@ -332,23 +329,50 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       seq.init(p, U);
       TileInfo t;
       while (seq.next(p, U, t)) {
-        const int hk = U.hts[0];  // both tiles of a unit share the K/V head
-        const CUtensorMap* tk = t.packed ? &p.tm_kp : &p.tm_kd;
-        const CUtensorMap* tv = t.packed ? &p.tm_vp : &p.tm_vd;
-        int slot;
-        uint32_t fpar, epar;
-        ring.take(NS, slot, fpar, epar);
-        if (!warp_wait(slot_empty + slot, epar, ab, ERR_TIMEOUT_PRODUCER)) goto producer_done;
+        const int slot = kpos % NK;
+        if (!warp_wait(k_empty + slot, ((kpos / NK) & 1) ^ 1, ab, ERR_TIMEOUT_PRODUCER)) goto kprod_done;
         if (lane == 0) {
-          mbar_arrive_expect_tx(slot_full + slot, kv_bytes);
-          uint8_t* dst = smem + C::OFF_SLOT + slot * C::KVBYTES;
+          const CUtensorMap* tk = t.packed ? &p.tm_kp : &p.tm_kd;
+          mbar_arrive_expect_tx(k_full + slot, C::KVBYTES);
+          uint8_t* dst = smem + C::OFF_K + slot * C::KVBYTES;
           for (int bx = 0; bx < D / 64; ++bx)
-            tma_load_4d(dst + bx * (TC_BN * 128), tk, slot_full + slot, bx * 64, t.idx * TC_BN, hk, U.b);
-          armed[slot] = ring.k - 1;
+            tma_load_4d(dst + bx * (TC_BN * 128), tk, k_full + slot, bx * 64, t.idx * TC_BN, U.hts[0], U.b);
+          k_armed[slot] = kpos;
         }
+        ++kpos;
+      }
+    }
+  kprod_done:
+    // drain: every copy this warp issued must land before the CTA exits
+    if (lane == 0) {
+      for (int s = 0; s < NK; ++s) {
+        if (k_armed[s] < 0) continue;
+        const uint32_t par = (k_armed[s] / NK) & 1;
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(k_full + s, par) && globaltimer() - t0 < 50000000ull) {}
+      }
+      if (q_issued > 0) {
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(q_full, (q_issued - 1) & 1) && globaltimer() - t0 < 50000000ull) {}
+      }
+    }
+  } else if (warp == 3) {
+    // ================================================================ V (+ counts) producer
+    int v_armed[NV];
+    for (int s = 0; s < NV; ++s) v_armed[s] = -1;
+    int vpos = 0;
+    for (int it = 0; it < n_iter; ++it) {
+      const int u = unit_of(it, blockIdx.x, G);
+      if (u >= p.num_units) continue;
+      const Unit U = decode_unit(p, u);
+      const int hk = U.hts[0];  // both tiles of a unit share the K/V head
+      TileSeq seq;
+      seq.init(p, U);
+      TileInfo t;
+      while (seq.next(p, U, t)) {
         if (!t.needs_v) continue;
-        ring.take(NS, slot, fpar, epar);
-        if (!warp_wait(slot_empty + slot, epar, ab, ERR_TIMEOUT_PRODUCER)) goto producer_done;
+        const int slot = vpos % NV;
+        if (!warp_wait(v_empty + slot, ((vpos / NV) & 1) ^ 1, ab, ERR_TIMEOUT_PRODUCER)) goto vprod_done;
         uint32_t meta_bytes = 0;
         if (t.packed) {
           // counts (and timestamps) of this packed block ride with its V tile: bulk copies on
@@ -360,10 +384,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             meta_bytes = static_cast<uint32_t>(nkeys) * 4u * (p.variant == TC_PURE ? 2u : 1u);
             if (lane == 0) {
               const int64_t off_c = U.b * p.cs_b + static_cast<int64_t>(hk) * p.cs_h + static_cast<int64_t>(t.idx) * TC_BN;
-              bulk_load(c, static_cast<const uint32_t*>(p.counts) + off_c, nkeys * 4u, slot_full + slot);
+              bulk_load(c, static_cast<const uint32_t*>(p.counts) + off_c, nkeys * 4u, v_full + slot);
               if (p.variant == TC_PURE) {
                 const int64_t off_t = U.b * p.ts_b + static_cast<int64_t>(hk) * p.ts_h + static_cast<int64_t>(t.idx) * TC_BN;
-                bulk_load(tt, p.ts + off_t, nkeys * 4u, slot_full + slot);
+                bulk_load(tt, p.ts + off_t, nkeys * 4u, v_full + slot);
               }
             }
           } else {
@@ -384,26 +408,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           }
         }
         if (lane == 0) {
-          mbar_arrive_expect_tx(slot_full + slot, kv_bytes + meta_bytes);
-          uint8_t* dst = smem + C::OFF_SLOT + slot * C::KVBYTES;
+          const CUtensorMap* tv = t.packed ? &p.tm_vp : &p.tm_vd;
+          mbar_arrive_expect_tx(v_full + slot, C::KVBYTES + meta_bytes);
+          uint8_t* dst = smem + C::OFF_V + slot * C::KVBYTES;
           for (int bx = 0; bx < D / 64; ++bx)
-            tma_load_4d(dst + bx * (TC_BN * 128), tv, slot_full + slot, bx * 64, t.idx * TC_BN, hk, U.b);
-          armed[slot] = ring.k - 1;
+            tma_load_4d(dst + bx * (TC_BN * 128), tv, v_full + slot, bx * 64, t.idx * TC_BN, hk, U.b);
+          v_armed[slot] = vpos;
         }
+        ++vpos;
       }
     }
-  producer_done:
-    // drain: every copy this warp issued must land before the CTA exits
+  vprod_done:
     if (lane == 0) {
-      for (int s = 0; s < NS; ++s) {
-        if (armed[s] < 0) continue;
-        const uint32_t par = (armed[s] / NS) & 1;
+      for (int s = 0; s < NV; ++s) {
+        if (v_armed[s] < 0) continue;
+        const uint32_t par = (v_armed[s] / NV) & 1;
         const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(slot_full + s, par) && globaltimer() - t0 < 50000000ull) {}
-      }
-      if (q_issued > 0) {
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(q_full, (q_issued - 1) & 1) && globaltimer() - t0 < 50000000ull) {}
+        while (!mbar_try_wait(v_full + s, par) && globaltimer() - t0 < 50000000ull) {}
       }
     }
   } else if (warp == 1) {
@@ -412,10 +433,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       constexpr uint32_t IDESC_S = umma_idesc_f16(TC_BM, TC_BN, BF16, false);
       constexpr uint32_t IDESC_PV = umma_idesc_f16(TC_BM, D, BF16, true);
       const uint32_t q_addr[2] = {smem_u32(smem + C::OFF_Q0), smem_u32(smem + C::OFF_Q1)};
-      const uint32_t slot_addr0 = smem_u32(smem + C::OFF_SLOT);
+      const uint32_t k_addr0 = smem_u32(smem + C::OFF_K);
+      const uint32_t v_addr0 = smem_u32(smem + C::OFF_V);
       const uint32_t tS[2] = {tmem + 0, tmem + 128};
       const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
-      Ring ring{0};
+      int kpos = 0, vpos = 0;  // K / V ring positions
       uint32_t q_par = 0;
       uint32_t free_par[2] = {1, 1};
       uint32_t p_par[2] = {0, 0};
@@ -438,7 +460,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           return true;
         };
         auto issue_S = [&](int x, int kslot) {
-          const uint32_t kbase = slot_addr0 + kslot * C::KVBYTES;
+          const uint32_t kbase = k_addr0 + kslot * C::KVBYTES;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * (TC_BM * 128) + (kk & 3) * 32;
@@ -448,7 +470,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           }
         };
         auto issue_PV = [&](int x, int vslot) {
-          const uint32_t vbase = slot_addr0 + vslot * C::KVBYTES;
+          const uint32_t vbase = v_addr0 + vslot * C::KVBYTES;
 #pragma unroll
           for (int kk = 0; kk < TC_BN / 16; ++kk) {
             const uint64_t bd = umma_desc_sw128(vbase + kk * 2048, TC_BN * 128, 1024);
@@ -462,11 +484,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         TileInfo cur, nxt;
         bool have_cur = seq.next(p, U, cur);
         int cur_k, cur_v = -1;
-        uint32_t fp, ep;
         const bool sanity = p.variant == TC_SANITY;
         if (have_cur) {
-          ring.take(NS, cur_k, fp, ep);
-          if (!mbar_wait(slot_full + cur_k, fp, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+          cur_k = kpos % NK;
+          if (!mbar_wait(k_full + cur_k, (kpos / NK) & 1, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+          ++kpos;
           tc_fence_after();
           for (int x = 0; x < 2; ++x) {
             if (!(cur.use >> x & 1)) continue;
@@ -474,13 +496,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             if (!(sanity && cur.packed)) umma_commit(s_full + x);
           }
           if (aborted) break;
-          umma_commit(slot_empty + cur_k);
+          umma_commit(k_empty + cur_k);
         }
         bool q_released = false;
         while (have_cur) {
           if (cur.needs_v) {
-            ring.take(NS, cur_v, fp, ep);
-            if (!mbar_wait(slot_full + cur_v, fp, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+            cur_v = vpos % NV;
+            if (!mbar_wait(v_full + cur_v, (vpos / NV) & 1, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+            ++vpos;
             tc_fence_after();
           }
           const bool have_nxt = seq.next(p, U, nxt);
@@ -502,8 +525,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             }
             if (have_nxt && (nxt.use >> x & 1)) {
               if (!nk_ready) {
-                ring.take(NS, nk, fp, ep);
-                if (!mbar_wait(slot_full + nk, fp, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+                nk = kpos % NK;
+                if (!mbar_wait(k_full + nk, (kpos / NK) & 1, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+                ++kpos;
                 tc_fence_after();
                 nk_ready = true;
               }
@@ -512,8 +536,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             }
           }
           if (aborted) break;
-          if (cur.needs_v) umma_commit(slot_empty + cur_v);
-          if (nk_ready) umma_commit(slot_empty + nk);
+          if (cur.needs_v) umma_commit(v_empty + cur_v);
+          if (nk_ready) umma_commit(k_empty + nk);
           if (!have_nxt) break;
           cur = nxt;
           cur_k = nk;
@@ -545,7 +569,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
     const uint32_t tS = tmem + lane_base + 128 * x;
     const uint32_t tO = tmem + lane_base + 256 + D * x;
     const float sl2 = p.scale_log2;
-    Ring ring{0};
+    int vpos = 0;  // V ring position (the packed block's counts travel with its V tile)
     uint32_t s_par = 0, o_par = 0;
     for (int it = 0; it < n_iter; ++it) {
       const int u = unit_of(it, blockIdx.x, G);
@@ -562,11 +586,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       while (seq.next(p, U, t)) {
         // log2 weight of a packed block (NaN when its counts differ)
         const float lw = t.packed ? wrow[t.idx] : 0.f;
-        int ks, vs = -1;
-        uint32_t fp, ep, vfp = 0;
-        ring.take(NS, ks, fp, ep);
-        if (t.needs_v) ring.take(NS, vs, vfp, ep);
-        if (!U.valid[x] || !(t.use >> x & 1) || !t.needs_v) continue;
+        if (!t.needs_v) continue;
+        const int vs = vpos % NV;
+        const uint32_t vfp = (vpos / NV) & 1;
+        ++vpos;
+        if (!U.valid[x] || !(t.use >> x & 1)) continue;
         if (!warp_wait(s_full + x, s_par, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
         s_par ^= 1;
         tc_fence_after();
@@ -577,7 +601,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         const int32_t* tsv = auxt + vs * TC_BN;
         if (perkey || (t.packed && p.variant == TC_PURE)) {
           // per-key counts (and timestamps) arrive with the block's V tile
-          if (!warp_wait(slot_full + vs, vfp, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
+          if (!warp_wait(v_full + vs, vfp, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
         }
         const int n0 = t.idx * TC_BN;
         const uint32_t NEG_INF = 0xFF800000u;
