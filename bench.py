@@ -51,6 +51,98 @@ def peaks():
         return 1590.0, 1400.0, "fallback"
 
 
+def hbm_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def hbm_kernels(dev, seed):
+    """HBM-bound kernels of the path, each launch timed alone with L2 flushed before it.
+
+    Returns {name: {"us": t, "bytes": algorithmic bytes, "gbs": bytes / t, "frac": gbs / peak}}:
+    delta selection (chunked_eval, cfg2 keys), device packing from a keep mask (cfg2 K/V),
+    decode attention (16 sequences, packed lengths U[1024, 8192], window 100, 32 q-heads) and
+    the decode cache update (one token per sequence)."""
+    from deltaattention_b200 import ops, synth
+    from deltaattention_b200.launch import fused_hybrid_decode_kernel, fused_hybrid_decode_update_kernel
+    peak, _ = hbm_peak()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, reps=10):
+        ts = []
+        for _ in range(reps + 2):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(ts[2:])
+
+    out = {}
+    Hkv, N, D = CFG["Hkv"], CFG["N"], CFG["D"]
+    _, k, v = synth.layer_inputs(1, Hkv, Hkv, N, D, torch.bfloat16, seed=seed, device=dev)
+    cos, sin = synth.rope_tables(N, D, CFG["theta"], torch.bfloat16, device=dev)
+    k_rot = ops.rope(k, cos, sin)
+    thr = 11.0  # raw Euclidean threshold (squared inside, as the reference): keeps about 1 key in 4 here
+    us = timed(lambda: ops.delta_keep_mask(k_rot, thr, "euclidean", 512))
+    nbytes = k_rot.numel() * 2 + Hkv * N * 4
+    out["delta_select"] = {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / peak}
+    keep, _ = ops.delta_keep_mask(k_rot, thr, "euclidean", 512)
+    M = int(keep.sum(-1).max().item())
+    kept = int(keep.sum().item())
+    us = timed(lambda: ops.pack_from_keep(k_rot, v, keep, num_packed=M))
+    nbytes = Hkv * N * 4 + kept * D * 2 * 2 * 2 + Hkv * M * 8
+    out["pack_from_keep"] = {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / peak,
+                             "kept_fraction": kept / (Hkv * N)}
+    del k, v, k_rot, keep
+    # decode: cfg5-like cache state
+    g = torch.Generator(device=dev).manual_seed(seed)
+    Bd, Hq, W, cap = 16, CFG["Hq"], 100, N // CFG["r"]
+    rnd = lambda *shape: torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)  # noqa: E731
+    lens = torch.randint(1024, cap + 1, (Bd, Hkv), generator=g, device=dev, dtype=torch.int32)
+    kp, vp = rnd(Bd, Hkv, cap, D), rnd(Bd, Hkv, cap, D)
+    cnt = torch.full((Bd, Hkv, cap), CFG["r"], dtype=torch.int32, device=dev)
+    ke, ve = rnd(Bd, Hkv, W, D), rnd(Bd, Hkv, W, D)
+    q = rnd(Bd, Hq, D)
+    o = torch.empty_like(q)
+
+    def dec():
+        fused_hybrid_decode_kernel[(Bd, Hq)](
+            q, kp, vp, cnt, lens, ke, ve, o, *q.stride(), *kp.stride(), *vp.stride(), *cnt.stride(), *lens.stride(),
+            *ke.stride(), *ve.stride(), *o.stride(), D ** -0.5, W, Hq // Hkv, head_dim=D, BLOCK_M=16, BLOCK_N=128,
+            BLOCK_D=D)
+    us = timed(dec)
+    nbytes = int(lens.sum().item()) * (D * 2 * 2 + 4) + Bd * Hkv * W * D * 2 * 2 + 2 * q.numel() * 2
+    out["decode_attention"] = {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / peak,
+                               "shape": f"B={Bd} Hq={Hq} Hkv={Hkv} d={D} packed U[1024,{cap}] window {W}"}
+    nk, nv = rnd(Bd, Hkv, 1, D), rnd(Bd, Hkv, 1, D)
+    lens_flat = lens.view(-1).clone()
+    # every update may append one anchor and the kernel (like the reference's) has no capacity
+    # argument: leave room for all timed calls
+    spare = 32
+    kp2 = torch.zeros((Bd, Hkv, cap + spare, D), dtype=torch.bfloat16, device=dev)
+    vp2 = torch.zeros_like(kp2)
+    cnt2 = torch.zeros((Bd, Hkv, cap + spare), dtype=torch.int32, device=dev)
+    tss2 = torch.zeros_like(cnt2)
+    kp2[:, :, :cap] = kp
+    vp2[:, :, :cap] = vp
+    cnt2[:, :, :cap] = cnt
+
+    def upd():
+        fused_hybrid_decode_update_kernel[(Bd * Hkv,)](
+            nk, nv, ke, ve, kp2, vp2, cnt2, tss2, lens_flat, W, 100000, 16.0, W,
+            *nk.stride(), *ke.stride(), *kp2.stride(), *cnt2.stride(), Hkv, D, BLOCK_D=D, USE_COSINE=False)
+    us = timed(upd, reps=10)  # 12 calls in all: at most 12 appends per (sequence, kv-head)
+    out["decode_update"] = {"us": us, "note": "one token per (sequence, kv-head); latency-bound"}
+    return out
+
+
 def traffic_per_launch():
     """DRAM bytes per attention launch from the committed ncu summary, if present."""
     try:
@@ -327,6 +419,8 @@ def run_ours(args, world, rank, local):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }
+    hk = hbm_kernels(dev, 2000 + rank)
+    line["hbm_kernels"] = {"peak_gbs": hbm_peak()[0], "peak_kind": hbm_peak()[1], **hk}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
         dt, tk = cpu_sample(tuple(range(8)))

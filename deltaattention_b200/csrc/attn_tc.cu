@@ -169,6 +169,7 @@ struct TileSeq {
   int mb_lo[2];
 
   __device__ __forceinline__ void init(const TcParams& p, const Unit& U) {
+    #pragma unroll
     for (int x = 0; x < 2; ++x) {
       n1[x] = 0; ds[x] = 0; de[x] = 0;
       mb_lo[x] = U.mb[x] * TC_BM;
@@ -190,6 +191,7 @@ struct TileSeq {
     const bool v0 = U.valid[0], v1 = U.valid[1];
     pmax = max(v0 ? n1[0] : 0, v1 ? n1[1] : 0);
     dlo = INT32_MAX; dhi = 0;
+    #pragma unroll
     for (int x = 0; x < 2; ++x)
       if (U.valid[x] && de[x] > ds[x]) { dlo = min(dlo, ds[x]); dhi = max(dhi, de[x]); }
     if (dlo == INT32_MAX) { dlo = 0; dhi = 0; }
@@ -202,6 +204,7 @@ struct TileSeq {
       if (cur >= pmax) { state = 1; cur = dlo; break; }
       const int j = cur++;
       int use = 0;
+      #pragma unroll
       for (int x = 0; x < 2; ++x) {
         if (!U.valid[x] || j >= n1[x]) continue;
         if (p.variant == TC_PURE) {
@@ -218,6 +221,7 @@ struct TileSeq {
       while (cur < dhi) {
         const int tb = cur++;
         int use = 0;
+        #pragma unroll
         for (int x = 0; x < 2; ++x)
           if (U.valid[x] && tb >= ds[x] && tb < de[x]) use |= 1 << x;
         if (!use) continue;
@@ -273,6 +277,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       mbar_init(v_full + s, 1);
       mbar_init(v_empty + s, 1);
     }
+    #pragma unroll
     for (int x = 0; x < 2; ++x) {
       mbar_init(s_full + x, 1);
       mbar_init(p_full + x, 4);
@@ -305,9 +310,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
   if (warp == 0) {
     // ================================================================ Q + K producer
     uint32_t q_par = 1;
-    int k_armed[NK];
-    for (int s = 0; s < NK; ++s) k_armed[s] = -1;
-    int kpos = 0, q_issued = 0;
+    int kpos = 0, q_issued = 0;  // K ring positions issued so far (the last NK may be in flight)
     for (int it = 0; it < n_iter; ++it) {
       const int u = unit_of(it, blockIdx.x, G);
       if (u >= p.num_units) continue;
@@ -317,6 +320,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       if (lane == 0) {
         const uint32_t qb = (U.valid[0] ? C::QBYTES : 0) + (U.valid[1] ? C::QBYTES : 0);
         mbar_arrive_expect_tx(q_full, qb);
+        #pragma unroll
         for (int x = 0; x < 2; ++x) {
           if (!U.valid[x]) continue;
           uint8_t* dst = smem + (x ? C::OFF_Q1 : C::OFF_Q0);
@@ -337,7 +341,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           uint8_t* dst = smem + C::OFF_K + slot * C::KVBYTES;
           for (int bx = 0; bx < D / 64; ++bx)
             tma_load_4d(dst + bx * (TC_BN * 128), tk, k_full + slot, bx * 64, t.idx * TC_BN, U.hts[0], U.b);
-          k_armed[slot] = kpos;
         }
         ++kpos;
       }
@@ -345,11 +348,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
   kprod_done:
     // drain: every copy this warp issued must land before the CTA exits
     if (lane == 0) {
-      for (int s = 0; s < NK; ++s) {
-        if (k_armed[s] < 0) continue;
-        const uint32_t par = (k_armed[s] / NK) & 1;
+      for (int q = (kpos > NK ? kpos - NK : 0); q < kpos; ++q) {
         const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(k_full + s, par) && globaltimer() - t0 < 50000000ull) {}
+        while (!mbar_try_wait(k_full + q % NK, (q / NK) & 1) && globaltimer() - t0 < 50000000ull) {}
       }
       if (q_issued > 0) {
         const uint64_t t0 = globaltimer();
@@ -358,9 +359,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
     }
   } else if (warp == 3) {
     // ================================================================ V (+ counts) producer
-    int v_armed[NV];
-    for (int s = 0; s < NV; ++s) v_armed[s] = -1;
-    int vpos = 0;
+    int vpos = 0;  // V ring positions issued so far (the last NV may be in flight)
     for (int it = 0; it < n_iter; ++it) {
       const int u = unit_of(it, blockIdx.x, G);
       if (u >= p.num_units) continue;
@@ -413,18 +412,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           uint8_t* dst = smem + C::OFF_V + slot * C::KVBYTES;
           for (int bx = 0; bx < D / 64; ++bx)
             tma_load_4d(dst + bx * (TC_BN * 128), tv, v_full + slot, bx * 64, t.idx * TC_BN, hk, U.b);
-          v_armed[slot] = vpos;
         }
         ++vpos;
       }
     }
   vprod_done:
     if (lane == 0) {
-      for (int s = 0; s < NV; ++s) {
-        if (v_armed[s] < 0) continue;
-        const uint32_t par = (v_armed[s] / NV) & 1;
+      for (int q = (vpos > NV ? vpos - NV : 0); q < vpos; ++q) {
         const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(v_full + s, par) && globaltimer() - t0 < 50000000ull) {}
+        while (!mbar_try_wait(v_full + q % NV, (q / NV) & 1) && globaltimer() - t0 < 50000000ull) {}
       }
     }
   } else if (warp == 1) {
@@ -490,6 +486,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           if (!mbar_wait(k_full + cur_k, (kpos / NK) & 1, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
           ++kpos;
           tc_fence_after();
+          #pragma unroll
           for (int x = 0; x < 2; ++x) {
             if (!(cur.use >> x & 1)) continue;
             issue_S(x, cur_k);
@@ -514,6 +511,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           }
           int nk = -1;
           bool nk_ready = false;
+          #pragma unroll
           for (int x = 0; x < 2; ++x) {
             if (cur.needs_v && (cur.use >> x & 1)) {
               if (!mbar_wait(p_full + x, p_par[x], ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
@@ -548,10 +546,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         // always waits o_full before arriving on tile_free. An epilogue therefore never
         // arrives before the MMA's matching wait, which keeps the parity waits unambiguous.
         // Invalid tiles take no part.
+        #pragma unroll
         for (int x = 0; x < 2 && !aborted; ++x)
           if (U.valid[x] && !ensure_free(x)) aborted = true;
         if (aborted) break;
         if (!q_released) umma_commit(q_empty);
+        #pragma unroll
         for (int x = 0; x < 2; ++x)
           if (U.valid[x]) umma_commit(o_full + x);
       }

@@ -9,6 +9,8 @@
 //    group, so the packed cache is read from HBM once per kv-head (the reference reads it
 //    once per q-head). Each lane scores one key for every head; chunk max / sum use warp
 //    shuffles; partials (m, l, acc) are merged by decode_combine.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace dab {
@@ -296,6 +298,144 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
   }
 }
 
+// Vectorised split-K decode for 16-bit types with unit head-dim strides: a CTA (8 warps)
+// scores 256 keys of one (batch, kv-head) for all G q-heads. QK: each lane owns one key and
+// reads its row with 16-byte loads; PV: each warp reads whole V rows (every lane 8 bytes of a
+// row, coalesced) for its 32 keys. Per-warp partial O are summed in shared memory.
+constexpr int DEC_VKC = 256;
+template <typename T, int D, int G>
+__global__ void __launch_bounds__(256) decode_attn_vec_kernel(
+    const T* __restrict__ q, int64_t qs_b, int64_t qs_h, const T* __restrict__ kp, int64_t kps_b, int64_t kps_h,
+    int64_t kps_n, const T* __restrict__ vp, int64_t vps_b, int64_t vps_h, int64_t vps_n,
+    const int32_t* __restrict__ counts, int64_t cs_b, int64_t cs_h, int64_t cs_n, const int32_t* __restrict__ lengths,
+    int64_t ls_b, int64_t ls_h, const T* __restrict__ ke, int64_t kes_b, int64_t kes_h, int64_t kes_n,
+    const T* __restrict__ ve, int64_t ves_b, int64_t ves_h, int64_t ves_n, float sm_scale, int64_t exact_len,
+    int64_t Hkv, int64_t nchunk, float* __restrict__ part) {
+  constexpr int NW = 8;
+  constexpr int VE = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte load
+  constexpr int PL = D / 32;                            // head-dim elements per lane in PV
+  __shared__ float sq[G][D];
+  __shared__ float sp[G][DEC_VKC];
+  __shared__ float swm[NW][G], swl[NW][G];
+  __shared__ float so[NW][G][D];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t chunk = blockIdx.x;
+  const int64_t bk = blockIdx.y;
+  const int64_t b = bk / Hkv, hk = bk % Hkv;
+  const int64_t plen = lengths[b * ls_b + hk * ls_h];
+  const int64_t total = plen + exact_len;
+  const int64_t k0 = chunk * DEC_VKC;
+  float* pout = part + ((bk * nchunk + chunk) * G) * (D + 2);
+  if (k0 >= total) {
+    if (tid < G) { pout[tid * (D + 2)] = -INFINITY; pout[tid * (D + 2) + 1] = 0.f; }
+    return;
+  }
+  for (int i = tid; i < G * D; i += 256) sq[i / D][i % D] = to_f32(q[b * qs_b + (hk * G + i / D) * qs_h + i % D]);
+  __syncthreads();
+  // ---- scores: this lane's key
+  const int64_t key = k0 + warp * 32 + lane;
+  const bool valid = key < total;
+  const bool packed = key < plen;
+  float s[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) s[g] = 0.f;
+  if (valid) {
+    const T* kr = packed ? kp + b * kps_b + hk * kps_h + key * kps_n : ke + b * kes_b + hk * kes_h + (key - plen) * kes_n;
+    // the whole row is requested before any of it is used (one memory round trip per key)
+    union { uint4 u; T e[VE]; } raw[D / VE];
+#pragma unroll
+    for (int v = 0; v < D / VE; ++v) raw[v].u = __ldg(reinterpret_cast<const uint4*>(kr) + v);
+#pragma unroll
+    for (int v = 0; v < D / VE; ++v) {
+#pragma unroll
+      for (int e = 0; e < VE; ++e) {
+        const float kv = to_f32(raw[v].e[e]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) s[g] = fmaf(sq[g][v * VE + e], kv, s[g]);
+      }
+    }
+  }
+  const float bias = (valid && packed) ? logf(static_cast<float>(counts[b * cs_b + hk * cs_h + key * cs_n])) : 0.f;
+  // each warp runs its own softmax over its 32 keys (no CTA-wide step between QK and PV, so
+  // one warp's V loads overlap another warp's K loads); the CTA merges the warps at the end
+  float mw[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    s[g] = valid ? s[g] * sm_scale + bias : -INFINITY;
+    float m = s[g];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    mw[g] = m;
+    const float ref = (m == -INFINITY) ? 0.f : m;
+    const float pv = valid ? expf(s[g] - ref) : 0.f;
+    sp[g][warp * 32 + lane] = round_as<T>(pv);  // P is cast to V's dtype before the PV product
+    float l = pv;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+    if (lane == 0) { swm[warp][g] = m; swl[warp][g] = l; }
+  }
+  __syncwarp();
+  // ---- PV over this warp's 32 keys: lane owns head-dim elements [lane * PL, lane * PL + PL)
+  float o[G][PL];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int e = 0; e < PL; ++e) o[g][e] = 0.f;
+  const int64_t kw = k0 + warp * 32;
+  const int nk = static_cast<int>((total - kw) < 32 ? (total - kw) : 32);
+  // all of this warp's V rows are requested first (rows past the end read row 0, weighted 0)
+  using VU = typename std::conditional<PL == 4, uint2, uint32_t>::type;
+  union { VU u; T e[PL]; } vraw[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int64_t kk = (j < nk) ? kw + j : 0;
+    const T* vr = (kk < plen) ? vp + b * vps_b + hk * vps_h + kk * vps_n : ve + b * ves_b + hk * ves_h + (kk - plen) * ves_n;
+    vraw[j].u = __ldg(reinterpret_cast<const VU*>(vr + lane * PL));
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float pj = (j < nk) ? sp[g][warp * 32 + j] : 0.f;
+#pragma unroll
+      for (int e = 0; e < PL; ++e) o[g][e] = fmaf(pj, to_f32(vraw[j].e[e]), o[g][e]);
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int e = 0; e < PL; ++e) so[warp][g][lane * PL + e] = o[g][e];
+  __syncthreads();
+  // merge the warps: reference = the chunk maximum, each warp's partial scaled to it
+  for (int i = tid; i < G * D; i += 256) {
+    const int g = i / D, d = i % D;
+    float M = swm[0][g];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) M = fmaxf(M, swm[w][g]);
+    float acc = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < NW; ++w)
+        if (swm[w][g] != -INFINITY) acc = fmaf(so[w][g][d], expf(swm[w][g] - M), acc);
+    }
+    pout[g * (D + 2) + 2 + d] = acc;
+  }
+  if (tid < G) {
+    float M = swm[0][tid];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) M = fmaxf(M, swm[w][tid]);
+    float l = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < NW; ++w)
+        if (swm[w][tid] != -INFINITY) l = fmaf(swl[w][tid], expf(swm[w][tid] - M), l);
+    }
+    pout[tid * (D + 2)] = M;
+    pout[tid * (D + 2) + 1] = l;
+  }
+  (void)mw;
+}
+
 size_t decode_attn_workspace(int64_t B, int64_t Hq, int64_t capacity, int64_t exact_len, int64_t head_dim) {
   int bd = 16;
   while (bd < head_dim) bd <<= 1;
@@ -311,6 +451,36 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
                                int64_t capacity, float* part, cudaStream_t st) {
   if (B * Hkv == 0) return cudaSuccess;
   if (G < 1 || G > DEC_GMAX) return cudaErrorInvalidValue;
+  {
+    // vectorised path: 16-bit types, head_dim 64 / 128, unit head-dim strides, 16-byte rows
+    auto a16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+    const bool shape_ok = (dtype == BF16 || dtype == F16) && (head_dim == 64 || head_dim == 128) &&
+                          (G == 1 || G == 2 || G == 4 || G == 8);
+    const bool layout_ok = qs[2] == 1 && kps[3] == 1 && vps[3] == 1 && kes[3] == 1 && ves[3] == 1 && a16(kp) &&
+                           a16(vp) && a16(ke) && a16(ve) && (kps[0] % 8 | kps[1] % 8 | kps[2] % 8) == 0 &&
+                           (vps[0] % 8 | vps[1] % 8 | vps[2] % 8) == 0 && (kes[0] % 8 | kes[1] % 8 | kes[2] % 8) == 0 &&
+                           (ves[0] % 8 | ves[1] % 8 | ves[2] % 8) == 0 && (reinterpret_cast<uintptr_t>(vp) & 7) == 0;
+    if (shape_ok && layout_ok) {
+      int64_t nc = (capacity + exact_len + DEC_VKC - 1) / DEC_VKC;
+      if (nc < 1) nc = 1;
+      dim3 g2(static_cast<unsigned>(nc), static_cast<unsigned>(B * Hkv));
+#define DAB_DECV(TY, DD, GG)                                                                                       decode_attn_vec_kernel<TY, DD, GG><<<g2, 256, 0, st>>>(                                                             static_cast<const TY*>(q), qs[0], qs[1], static_cast<const TY*>(kp), kps[0], kps[1], kps[2],                    static_cast<const TY*>(vp), vps[0], vps[1], vps[2], counts, cs[0], cs[1], cs[2], lengths, ls[0], ls[1],         static_cast<const TY*>(ke), kes[0], kes[1], kes[2], static_cast<const TY*>(ve), ves[0], ves[1], ves[2],         sm_scale, exact_len, Hkv, nc, part);                                                                         decode_combine_kernel<TY, DD><<<static_cast<unsigned>(B * Hkv * GG), 128, 0, st>>>(                                part, static_cast<TY*>(out), os[0], os[1], os[2], GG, Hkv, nc, head_dim);                                    return cudaGetLastError();
+#define DAB_DECV_G(TY, DD) \
+  switch (G) {             \
+    case 1: DAB_DECV(TY, DD, 1) \
+    case 2: DAB_DECV(TY, DD, 2) \
+    case 4: DAB_DECV(TY, DD, 4) \
+    default: DAB_DECV(TY, DD, 8) \
+  }
+#define DAB_DECV_D(TY)                         \
+  if (head_dim == 64) { DAB_DECV_G(TY, 64) } \
+  else { DAB_DECV_G(TY, 128) }
+      if (dtype == BF16) { DAB_DECV_D(__nv_bfloat16) } else { DAB_DECV_D(__half) }
+#undef DAB_DECV_D
+#undef DAB_DECV_G
+#undef DAB_DECV
+    }
+  }
   int bd = 16;
   while (bd < head_dim) bd <<= 1;
   if (bd > 256) return cudaErrorInvalidValue;

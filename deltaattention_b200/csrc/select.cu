@@ -16,6 +16,68 @@ namespace dab {
 // ---------------------------------------------------------------------------------------
 // delta scan
 // ---------------------------------------------------------------------------------------
+// One step of the delta scan for one 8-lane group: lane g holds elements g, g + 8, ... of the
+// current row and of the anchor (two halves of 128 for BD = 256). Returns whether the row is
+// kept (a new anchor), computed in the reference's summation order.
+template <typename T, int BD, bool COS>
+__device__ __forceinline__ bool delta_decide(const float (&cur)[BD > 128 ? 2 : 1][BD / 8 / (BD > 128 ? 2 : 1)],
+                                             const float (&ref)[BD > 128 ? 2 : 1][BD / 8 / (BD > 128 ? 2 : 1)],
+                                             unsigned gmask, float thr) {
+  constexpr int NH = BD > 128 ? 2 : 1;
+  constexpr int PER = BD / 8 / NH;
+  auto tree = [&](float v) {
+    v = __fadd_rn(v, __shfl_xor_sync(gmask, v, 1));
+    v = __fadd_rn(v, __shfl_xor_sync(gmask, v, 2));
+    v = __fadd_rn(v, __shfl_xor_sync(gmask, v, 4));
+    return v;
+  };
+  bool kp;
+  if constexpr (COS) {
+    float dot = 0.f, cc = 0.f, rr = 0.f;
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh) {
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+#pragma unroll
+      for (int m = 0; m < PER; ++m) {
+        const float p0 = __fmul_rn(cur[hh][m], ref[hh][m]);
+        const float p1 = __fmul_rn(cur[hh][m], cur[hh][m]);
+        const float p2 = __fmul_rn(ref[hh][m], ref[hh][m]);
+        a0 = m ? __fadd_rn(a0, p0) : p0;
+        a1 = m ? __fadd_rn(a1, p1) : p1;
+        a2 = m ? __fadd_rn(a2, p2) : p2;
+      }
+      a0 = tree(a0);
+      a1 = tree(a1);
+      a2 = tree(a2);
+      dot = hh ? __fadd_rn(dot, a0) : a0;
+      cc = hh ? __fadd_rn(cc, a1) : a1;
+      rr = hh ? __fadd_rn(rr, a2) : a2;
+    }
+    const float nc = __fsqrt_rn(__fadd_rn(cc, 1e-8f));
+    const float nr = __fsqrt_rn(__fadd_rn(rr, 1e-8f));
+    const float cs = __fdiv_rn(dot, __fmul_rn(nc, nr));
+    kp = cs < thr;
+  } else {
+    float tot = 0.f;
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh) {
+      float acc = 0.f;
+#pragma unroll
+      for (int m = 0; m < PER; ++m) {
+        // elementwise ops round to the input dtype (fp32 math, then RNE)
+        const float d = round_as<T>(__fsub_rn(cur[hh][m], ref[hh][m]));
+        const float sq = round_as<T>(__fmul_rn(d, d));
+        acc = m ? __fadd_rn(acc, sq) : sq;
+      }
+      acc = tree(acc);
+      tot = hh ? __fadd_rn(tot, acc) : acc;
+    }
+    tot = round_as<T>(tot);
+    kp = tot > thr;
+  }
+  return kp;
+}
+
 template <typename T, int BD, bool COS>
 __global__ void __launch_bounds__(256) chunked_eval_kernel(
     const T* __restrict__ x, int64_t xs_b, int64_t xs_h, int64_t xs_s, int64_t xs_d,
@@ -49,63 +111,13 @@ __global__ void __launch_bounds__(256) chunked_eval_kernel(
         dst[hh][m] = (e < head_dim) ? to_f32(r[e * xs_d]) : 0.f;
       }
   };
-  auto tree = [&](float v) {
-    v = __fadd_rn(v, __shfl_xor_sync(gmask, v, 1));
-    v = __fadd_rn(v, __shfl_xor_sync(gmask, v, 2));
-    v = __fadd_rn(v, __shfl_xor_sync(gmask, v, 4));
-    return v;
-  };
-
   load(start, ref);
   if (g == 0) krow[start * km_s] = 1;
   int local = 1;
   if (start + 1 < end) load(start + 1, cur);
   for (int64_t i = start + 1; i < end; ++i) {
     if (i + 1 < end) load(i + 1, nxt);
-    bool kp;
-    if constexpr (COS) {
-      float dot = 0.f, cc = 0.f, rr = 0.f;
-#pragma unroll
-      for (int hh = 0; hh < NH; ++hh) {
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f;
-#pragma unroll
-        for (int m = 0; m < PER; ++m) {
-          const float p0 = __fmul_rn(cur[hh][m], ref[hh][m]);
-          const float p1 = __fmul_rn(cur[hh][m], cur[hh][m]);
-          const float p2 = __fmul_rn(ref[hh][m], ref[hh][m]);
-          a0 = m ? __fadd_rn(a0, p0) : p0;
-          a1 = m ? __fadd_rn(a1, p1) : p1;
-          a2 = m ? __fadd_rn(a2, p2) : p2;
-        }
-        a0 = tree(a0);
-        a1 = tree(a1);
-        a2 = tree(a2);
-        dot = hh ? __fadd_rn(dot, a0) : a0;
-        cc = hh ? __fadd_rn(cc, a1) : a1;
-        rr = hh ? __fadd_rn(rr, a2) : a2;
-      }
-      const float nc = __fsqrt_rn(__fadd_rn(cc, 1e-8f));
-      const float nr = __fsqrt_rn(__fadd_rn(rr, 1e-8f));
-      const float cs = __fdiv_rn(dot, __fmul_rn(nc, nr));
-      kp = cs < thr;
-    } else {
-      float tot = 0.f;
-#pragma unroll
-      for (int hh = 0; hh < NH; ++hh) {
-        float acc = 0.f;
-#pragma unroll
-        for (int m = 0; m < PER; ++m) {
-          // elementwise ops round to the input dtype (fp32 math, then RNE)
-          const float d = round_as<T>(__fsub_rn(cur[hh][m], ref[hh][m]));
-          const float sq = round_as<T>(__fmul_rn(d, d));
-          acc = m ? __fadd_rn(acc, sq) : sq;
-        }
-        acc = tree(acc);
-        tot = hh ? __fadd_rn(tot, acc) : acc;
-      }
-      tot = round_as<T>(tot);
-      kp = tot > thr;
-    }
+    const bool kp = delta_decide<T, BD, COS>(cur, ref, gmask, thr);
     if (g == 0) krow[i * km_s] = kp ? 1 : 0;
     if (kp) {
 #pragma unroll
@@ -122,11 +134,119 @@ __global__ void __launch_bounds__(256) chunked_eval_kernel(
   if (g == 0) ccount[b * cc_b + h * cc_h + chunk * cc_c] = local;
 }
 
+// The same scan with rows staged through shared memory: each 8-lane group keeps a ring of
+// ROWS rows filled by 16-byte cp.async copies (one commit group per row), so the row a step
+// needs was requested ROWS steps earlier and the serial chain is no longer one memory latency
+// per token. Used when the head dimension is the power of two BD with unit stride and rows
+// start on 16-byte boundaries.
+constexpr int CE_ROWS = 16;   // rows in flight per chain
+constexpr int CE_GROUPS = 4;  // chains per block (one warp)
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <typename T, int BD, bool COS>
+__global__ void __launch_bounds__(CE_GROUPS * 8) chunked_eval_staged_kernel(
+    const T* __restrict__ x, int64_t xs_b, int64_t xs_h, int64_t xs_s,
+    int32_t* __restrict__ keep, int64_t km_b, int64_t km_h, int64_t km_s,
+    int32_t* __restrict__ ccount, int64_t cc_b, int64_t cc_h, int64_t cc_c,
+    float thr, int64_t seq_len, int64_t chunk_size, int64_t num_heads, int64_t grid_bh, int64_t grid_chunks) {
+  constexpr int NH = BD > 128 ? 2 : 1;
+  constexpr int PER = BD / 8 / NH;
+  constexpr int ROWB = BD * static_cast<int>(sizeof(T));  // bytes per row
+  constexpr int NCP = ROWB / 16;                           // 16-byte copies per row
+  constexpr int PITCH = ROWB + 16;                         // padded row pitch (bank spread)
+  extern __shared__ __align__(16) uint8_t ce_smem[];
+  const int lane = threadIdx.x & 31;
+  const int g = lane & 7;
+  const int grp = threadIdx.x >> 3;
+  const unsigned gmask = 0xFFu << (lane & 24);
+  uint8_t* ring = ce_smem + grp * (CE_ROWS * PITCH + 16);
+  const int64_t chunk = static_cast<int64_t>(blockIdx.x) * CE_GROUPS + grp;
+  const int64_t bh = blockIdx.y;
+  if (chunk >= grid_chunks || bh >= grid_bh) return;
+  const int64_t b = bh / num_heads, h = bh % num_heads;
+  const int64_t start = chunk * chunk_size;
+  if (start >= seq_len) return;
+  const int64_t end = min(start + chunk_size, seq_len);
+  const uint8_t* row0 = reinterpret_cast<const uint8_t*>(x + b * xs_b + h * xs_h);
+  const int64_t rstride = xs_s * static_cast<int64_t>(sizeof(T));
+  int32_t* krow = keep + b * km_b + h * km_h;
+
+  // request row pos into its ring slot (lane g copies 16-byte pieces g, g + 8, ...); one
+  // commit group per call, empty past the end, so the group count stays uniform
+  auto request = [&](int64_t pos) {
+    if (pos < end) {
+      const uint8_t* src = row0 + pos * rstride;
+      uint8_t* dst = ring + (pos % CE_ROWS) * PITCH;
+#pragma unroll
+      for (int c = g; c < NCP; c += 8) cp_async16(dst + c * 16, src + c * 16);
+    }
+    cp_async_commit();
+  };
+  auto read = [&](int64_t pos, float (&dst)[NH][PER]) {
+    const T* r = reinterpret_cast<const T*>(ring + (pos % CE_ROWS) * PITCH);
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh)
+#pragma unroll
+      for (int m = 0; m < PER; ++m) dst[hh][m] = to_f32(r[hh * 128 + g + 8 * m]);
+  };
+
+  for (int k = 0; k < CE_ROWS; ++k) request(start + k);
+  float ref[NH][PER], cur[NH][PER];
+  cp_async_wait<CE_ROWS - 1>();
+  __syncwarp(gmask);
+  read(start, ref);
+  __syncwarp(gmask);
+  request(start + CE_ROWS);
+  if (g == 0) krow[start * km_s] = 1;
+  int local = 1;
+  for (int64_t i = start + 1; i < end; ++i) {
+    cp_async_wait<CE_ROWS - 1>();  // row i has landed (its group is the oldest pending)
+    __syncwarp(gmask);
+    read(i, cur);
+    __syncwarp(gmask);             // every lane has read slot i before it is refilled
+    request(i + CE_ROWS);
+    const bool kp = delta_decide<T, BD, COS>(cur, ref, gmask, thr);
+    if (g == 0) krow[i * km_s] = kp ? 1 : 0;
+    if (kp) {
+#pragma unroll
+      for (int hh = 0; hh < NH; ++hh)
+#pragma unroll
+        for (int m = 0; m < PER; ++m) ref[hh][m] = cur[hh][m];
+      ++local;
+    }
+  }
+  cp_async_wait<0>();
+  if (g == 0) ccount[b * cc_b + h * cc_h + chunk * cc_c] = local;
+}
+
 template <typename T, int BD, bool COS>
 static cudaError_t launch_chunked_eval_t(const void* x, const int64_t* xs, int32_t* keep, const int64_t* km,
                                          int32_t* cc, const int64_t* ccs, float thr, int64_t seq_len,
                                          int64_t head_dim, int64_t chunk_size, int64_t num_heads,
                                          int64_t grid_bh, int64_t grid_chunks, cudaStream_t st) {
+  const bool staged = head_dim == BD && xs[3] == 1 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                      (xs[0] * static_cast<int64_t>(sizeof(T))) % 16 == 0 &&
+                      (xs[1] * static_cast<int64_t>(sizeof(T))) % 16 == 0 &&
+                      (xs[2] * static_cast<int64_t>(sizeof(T))) % 16 == 0 && BD * sizeof(T) >= 128;
+  if (staged) {
+    const int smem = CE_GROUPS * (CE_ROWS * (BD * static_cast<int>(sizeof(T)) + 16) + 16);
+    auto kfn = chunked_eval_staged_kernel<T, BD, COS>;
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+    }
+    dim3 g2(static_cast<unsigned>((grid_chunks + CE_GROUPS - 1) / CE_GROUPS), static_cast<unsigned>(grid_bh));
+    kfn<<<g2, CE_GROUPS * 8, smem, st>>>(static_cast<const T*>(x), xs[0], xs[1], xs[2], keep, km[0], km[1], km[2], cc,
+                                         ccs[0], ccs[1], ccs[2], thr, seq_len, chunk_size, num_heads, grid_bh,
+                                         grid_chunks);
+    return cudaGetLastError();
+  }
   const int groups_per_block = 8;  // 64 threads
   dim3 grid(static_cast<unsigned>((grid_chunks + groups_per_block - 1) / groups_per_block),
             static_cast<unsigned>(grid_bh));
