@@ -143,6 +143,46 @@ def hbm_kernels(dev, seed):
     return out
 
 
+def sweep(dev, seed, reps=3):
+    """cfg3: the same layer-op at N in {8k .. 128k} and r in {2, 4, 8}, each against the same
+    kernel family run dense (r = 1). Attention only, CUDA events, median of `reps` launches
+    (every input is larger than L2 from N = 16k on; one head group per point is enough for
+    the per-head rate, so the sweep uses B=1, Hq=32, Hkv=8 as cfg2)."""
+    from deltaattention_b200 import ops, synth
+    burst, _, _ = peaks()
+    stream = torch.cuda.current_stream(dev)
+    out = []
+    for N in (8192, 16384, 32768, 65536, 131072):
+        q, k, v = synth.layer_inputs(1, CFG["Hq"], CFG["Hkv"], N, CFG["D"], torch.bfloat16, seed=seed, device=dev)
+        cos, sin = synth.rope_tables(N, CFG["D"], CFG["theta"], torch.bfloat16, device=dev)
+        qr, kr = ops.rope(q, cos, sin), ops.rope(k, cos, sin)
+        del q, k
+
+        def timed(fn):
+            fn()
+            ts = []
+            for _ in range(reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            return statistics.median(ts)
+        dense = timed(lambda: ops.flash(qr, kr, v))
+        row = {"N": N, "dense_r1_ms": dense}
+        for r in (2, 4, 8):
+            pk = ops.pack_periodic(kr, v, r)
+            ms = timed(lambda: ops.attention(qr, kr, v, pk, dense_window=CFG["W"]))
+            flops = CFG["Hq"] * ops.tile_count_periodic(N, r, CFG["W"]) * 4 * 128 * 128 * CFG["D"]
+            row[f"r{r}"] = {"ms": ms, "tflops": flops / ms / 1e9, "frac": flops / ms / 1e9 / burst,
+                            "speedup_vs_dense": dense / ms, "tokens_per_s": N / (ms / 1e3)}
+        out.append(row)
+        del qr, kr, v
+        torch.cuda.empty_cache()
+    return out
+
+
 def traffic_per_launch():
     """DRAM bytes per attention launch from the committed ncu summary, if present."""
     try:
@@ -419,6 +459,8 @@ def run_ours(args, world, rank, local):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }
+    if not args.no_sweep:
+        line["sweep"] = sweep(dev, 3000 + rank)
     hk = hbm_kernels(dev, 2000 + rank)
     line["hbm_kernels"] = {"peak_gbs": hbm_peak()[0], "peak_kind": hbm_peak()[1], **hk}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -438,6 +480,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the cfg3 N / r sweep")
     ap.add_argument("--n", type=int, default=None, help="sequence length override (profiling small cases)")
     ap.add_argument("--only-step", action="store_true",
                     help="time the hot-path step only (no comparator, e2e or CPU legs); for profiling")
