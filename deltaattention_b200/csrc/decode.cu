@@ -276,42 +276,68 @@ template <typename T, int BD>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __restrict__ part, T* __restrict__ out,
                                                              int64_t os_b, int64_t os_h, int64_t os_d, int64_t G,
                                                              int64_t Hkv, int64_t nchunk, int64_t head_dim) {
+  // four warps take every fourth chunk, so the partials stream in parallel; a shared-memory
+  // step merges the four running sums
+  __shared__ float sm[4], sl[4];
+  __shared__ float sacc[4][BD];
   const int64_t bh = blockIdx.x;  // (b, q-head)
   const int64_t Hq = Hkv * G;
   const int64_t b = bh / Hq, h = bh % Hq;
   const int64_t hk = h / G, g = h % G;
   const int64_t bk = b * Hkv + hk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* base = part + (bk * nchunk * G + g) * (BD + 2);
+  const int64_t cstride = G * (BD + 2);
   float m = -INFINITY;
-  for (int64_t c = 0; c < nchunk; ++c) m = fmaxf(m, part[((bk * nchunk + c) * G + g) * (BD + 2)]);
+  for (int64_t c = warp; c < nchunk; c += 4) m = fmaxf(m, base[c * cstride]);
+  if (lane == 0) sm[warp] = m;
+  __syncthreads();
+  m = fmaxf(fmaxf(sm[0], sm[1]), fmaxf(sm[2], sm[3]));
   const float ref = (m == -INFINITY) ? 0.f : m;
-  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
-    float l = 0.f, acc = 0.f;
-    for (int64_t c = 0; c < nchunk; ++c) {
-      const float* pc = part + ((bk * nchunk + c) * G + g) * (BD + 2);
-      const float mc = pc[0];
-      if (mc == -INFINITY) continue;
-      const float f = expf(mc - ref);
-      l += pc[1] * f;
-      acc += pc[2 + d] * f;
+  float l = 0.f;
+  float acc[BD / 32 > 0 ? BD / 32 : 1];
+#pragma unroll
+  for (int j = 0; j < (BD / 32 > 0 ? BD / 32 : 1); ++j) acc[j] = 0.f;
+  for (int64_t c = warp; c < nchunk; c += 4) {
+    const float* pc = base + c * cstride;
+    const float mc = pc[0];
+    if (mc == -INFINITY) continue;
+    const float f = expf(mc - ref);
+    l = fmaf(pc[1], f, l);
+#pragma unroll
+    for (int j = 0; j < (BD / 32 > 0 ? BD / 32 : 1); ++j) {
+      const int d = j * 32 + lane;
+      if (d < head_dim) acc[j] = fmaf(pc[2 + d], f, acc[j]);
     }
-    out[b * os_b + h * os_h + d * os_d] = from_f32<T>(acc / l);
+  }
+  if (lane == 0) sl[warp] = l;
+#pragma unroll
+  for (int j = 0; j < (BD / 32 > 0 ? BD / 32 : 1); ++j) {
+    const int d = j * 32 + lane;
+    if (d < BD) sacc[warp][d] = acc[j];
+  }
+  __syncthreads();
+  const float lt = (sl[0] + sl[1]) + (sl[2] + sl[3]);
+  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+    const float a = (sacc[0][d] + sacc[1][d]) + (sacc[2][d] + sacc[3][d]);
+    out[b * os_b + h * os_h + d * os_d] = from_f32<T>(a / lt);
   }
 }
 
-// Vectorised split-K decode for 16-bit types with unit head-dim strides: a CTA (8 warps)
-// scores 256 keys of one (batch, kv-head) for all G q-heads. QK: each lane owns one key and
+// Vectorised split-K decode for 16-bit types with unit head-dim strides: a CTA (4 warps)
+// scores 128 keys of one (batch, kv-head) for all G q-heads. QK: each lane owns one key and
 // reads its row with 16-byte loads; PV: each warp reads whole V rows (every lane 8 bytes of a
 // row, coalesced) for its 32 keys. Per-warp partial O are summed in shared memory.
-constexpr int DEC_VKC = 256;
+constexpr int DEC_VKC = 128;
 template <typename T, int D, int G>
-__global__ void __launch_bounds__(256) decode_attn_vec_kernel(
+__global__ void __launch_bounds__(128) decode_attn_vec_kernel(
     const T* __restrict__ q, int64_t qs_b, int64_t qs_h, const T* __restrict__ kp, int64_t kps_b, int64_t kps_h,
     int64_t kps_n, const T* __restrict__ vp, int64_t vps_b, int64_t vps_h, int64_t vps_n,
     const int32_t* __restrict__ counts, int64_t cs_b, int64_t cs_h, int64_t cs_n, const int32_t* __restrict__ lengths,
     int64_t ls_b, int64_t ls_h, const T* __restrict__ ke, int64_t kes_b, int64_t kes_h, int64_t kes_n,
     const T* __restrict__ ve, int64_t ves_b, int64_t ves_h, int64_t ves_n, float sm_scale, int64_t exact_len,
     int64_t Hkv, int64_t nchunk, float* __restrict__ part) {
-  constexpr int NW = 8;
+  constexpr int NW = DEC_VKC / 32;
   constexpr int VE = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte load
   constexpr int PL = D / 32;                            // head-dim elements per lane in PV
   __shared__ float sq[G][D];
@@ -330,7 +356,7 @@ __global__ void __launch_bounds__(256) decode_attn_vec_kernel(
     if (tid < G) { pout[tid * (D + 2)] = -INFINITY; pout[tid * (D + 2) + 1] = 0.f; }
     return;
   }
-  for (int i = tid; i < G * D; i += 256) sq[i / D][i % D] = to_f32(q[b * qs_b + (hk * G + i / D) * qs_h + i % D]);
+  for (int i = tid; i < G * D; i += DEC_VKC) sq[i / D][i % D] = to_f32(q[b * qs_b + (hk * G + i / D) * qs_h + i % D]);
   __syncthreads();
   // ---- scores: this lane's key
   const int64_t key = k0 + warp * 32 + lane;
@@ -407,7 +433,7 @@ __global__ void __launch_bounds__(256) decode_attn_vec_kernel(
     for (int e = 0; e < PL; ++e) so[warp][g][lane * PL + e] = o[g][e];
   __syncthreads();
   // merge the warps: reference = the chunk maximum, each warp's partial scaled to it
-  for (int i = tid; i < G * D; i += 256) {
+  for (int i = tid; i < G * D; i += DEC_VKC) {
     const int g = i / D, d = i % D;
     float M = swm[0][g];
 #pragma unroll
@@ -464,7 +490,7 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
       int64_t nc = (capacity + exact_len + DEC_VKC - 1) / DEC_VKC;
       if (nc < 1) nc = 1;
       dim3 g2(static_cast<unsigned>(nc), static_cast<unsigned>(B * Hkv));
-#define DAB_DECV(TY, DD, GG)                                                                                       decode_attn_vec_kernel<TY, DD, GG><<<g2, 256, 0, st>>>(                                                             static_cast<const TY*>(q), qs[0], qs[1], static_cast<const TY*>(kp), kps[0], kps[1], kps[2],                    static_cast<const TY*>(vp), vps[0], vps[1], vps[2], counts, cs[0], cs[1], cs[2], lengths, ls[0], ls[1],         static_cast<const TY*>(ke), kes[0], kes[1], kes[2], static_cast<const TY*>(ve), ves[0], ves[1], ves[2],         sm_scale, exact_len, Hkv, nc, part);                                                                         decode_combine_kernel<TY, DD><<<static_cast<unsigned>(B * Hkv * GG), 128, 0, st>>>(                                part, static_cast<TY*>(out), os[0], os[1], os[2], GG, Hkv, nc, head_dim);                                    return cudaGetLastError();
+#define DAB_DECV(TY, DD, GG)                                                                                       decode_attn_vec_kernel<TY, DD, GG><<<g2, DEC_VKC, 0, st>>>(                                                             static_cast<const TY*>(q), qs[0], qs[1], static_cast<const TY*>(kp), kps[0], kps[1], kps[2],                    static_cast<const TY*>(vp), vps[0], vps[1], vps[2], counts, cs[0], cs[1], cs[2], lengths, ls[0], ls[1],         static_cast<const TY*>(ke), kes[0], kes[1], kes[2], static_cast<const TY*>(ve), ves[0], ves[1], ves[2],         sm_scale, exact_len, Hkv, nc, part);                                                                         decode_combine_kernel<TY, DD><<<static_cast<unsigned>(B * Hkv * GG), 128, 0, st>>>(                                part, static_cast<TY*>(out), os[0], os[1], os[2], GG, Hkv, nc, head_dim);                                    return cudaGetLastError();
 #define DAB_DECV_G(TY, DD) \
   switch (G) {             \
     case 1: DAB_DECV(TY, DD, 1) \
