@@ -656,13 +656,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         // probabilities 2^(s*scale + nb) of one 32-column chunk, packed as bf16x2 / f16x2
         // pairs into out[0..15]; row sums into la / lb
         float2 la = make_float2(0.f, 0.f), lb = la;
+        // exponent arguments and row sums on packed fp32x2 FMA / add (one instruction per pair):
+        // the softmax warps are issue-bound
         auto exp_plain = [&](const uint32_t* sc, float nb, uint32_t* out) {
+          const float2 s2 = make_float2(sl2, sl2), n2 = make_float2(nb, nb);
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
+            const float2 a01 = ffma2(make_float2(__uint_as_float(sc[e]), __uint_as_float(sc[e + 1])), s2, n2);
+            const float2 a23 = ffma2(make_float2(__uint_as_float(sc[e + 2]), __uint_as_float(sc[e + 3])), s2, n2);
             float pe[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) pe[k] = ex2(fmaf(__uint_as_float(sc[e + k]), sl2, nb));
-            la.x += pe[0]; la.y += pe[1]; lb.x += pe[2]; lb.y += pe[3];
+            pe[0] = ex2(a01.x); pe[1] = ex2(a01.y); pe[2] = ex2(a23.x); pe[3] = ex2(a23.y);
+            la = fadd2(la, make_float2(pe[0], pe[1]));
+            lb = fadd2(lb, make_float2(pe[2], pe[3]));
             out[e / 2] = pack2(pe[0], pe[1], BF16);
             out[e / 2 + 1] = pack2(pe[2], pe[3], BF16);
           }
