@@ -342,6 +342,10 @@ int dab_hybrid_flash_noalloc(int variant, const void* q, const void* k_dense, co
     }
     scratch = g_noalloc_ptr[dev];
   }
+  // the array keeps the previous call's contents: the header (device error word) must start
+  // at zero so a timed-out wait of this call is recorded; everything else is written before read
+  e = cudaMemsetAsync(scratch, 0, 256, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_status(e, "dab_hybrid_flash_noalloc (clearing the scratch header)");
   const int64_t* s = strides;
   return run_attention(variant, 1, q, k_dense, v_dense, k_packed, v_packed, packed_ts, packed_counts,
                        counts_is_int, out, dtype, s + 0, s + 4, s + 8, s + 12, s + 16, s + 20, s + 23, s + 26,

@@ -105,9 +105,9 @@ int dab_hybrid_flash(int variant, const void* q, const void* k_dense, const void
  *   with a message naming both sizes (e.g. 128 k queries x 64 timestamp heads still fit).
  * - The first call on a device resolves the scratch address for that device (with that
  *   device current); make it before any stream capture.
- * - Zero at start: only the first 4 bytes (the device error word a timed-out in-kernel wait
- *   sets, never cleared by this entry point); static storage starts zeroed. Every other
- *   scratch byte a call reads is written earlier in the same call.
+ * - The array keeps the last call's contents. Only its 256-byte header (the device error word
+ *   a timed-out in-kernel wait sets) must start at zero, and every call clears it on its stream
+ *   first; every other scratch byte a call reads is written earlier in the same call.
  * - Calls that overlap on one device (other streams or threads) share the scratch and race;
  *   serialise them. */
 int dab_hybrid_flash_noalloc(int variant, const void* q, const void* k_dense, const void* v_dense,
