@@ -455,23 +455,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           freed[x] = true;
           return true;
         };
+        // shared-memory descriptors as base + constant: the start-address field (bits 0-13, in
+        // 16-byte units) of every operand is the base's plus a fixed offset
+        const uint64_t qdesc[2] = {umma_desc_sw128(q_addr[0], 16, 1024), umma_desc_sw128(q_addr[1], 16, 1024)};
+        const uint64_t kdesc0 = umma_desc_sw128(k_addr0, 16, 1024);
+        const uint64_t vdesc0 = umma_desc_sw128(v_addr0, TC_BN * 128, 1024);
         auto issue_S = [&](int x, int kslot) {
-          const uint32_t kbase = k_addr0 + kslot * C::KVBYTES;
+          const uint64_t kb = kdesc0 + static_cast<uint64_t>(kslot * (C::KVBYTES >> 4));
+          const uint64_t qb = qdesc[x];
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * (TC_BM * 128) + (kk & 3) * 32;
-            const uint64_t ad = umma_desc_sw128(q_addr[x] + off, 16, 1024);
-            const uint64_t bd = umma_desc_sw128(kbase + off, 16, 1024);
-            umma_ss(tS[x], ad, bd, IDESC_S, kk > 0);
+            const uint64_t off = ((kk >> 2) * (TC_BM * 128) + (kk & 3) * 32) >> 4;
+            umma_ss(tS[x], qb + off, kb + off, IDESC_S, kk > 0);
           }
         };
         auto issue_PV = [&](int x, int vslot) {
-          const uint32_t vbase = v_addr0 + vslot * C::KVBYTES;
+          const uint64_t vb = vdesc0 + static_cast<uint64_t>(vslot * (C::KVBYTES >> 4));
 #pragma unroll
-          for (int kk = 0; kk < TC_BN / 16; ++kk) {
-            const uint64_t bd = umma_desc_sw128(vbase + kk * 2048, TC_BN * 128, 1024);
-            umma_ts(tO[x], tS[x] + kk * 8, bd, IDESC_PV, (o_init[x] || kk > 0) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < TC_BN / 16; ++kk)
+            umma_ts(tO[x], tS[x] + kk * 8, vb + static_cast<uint64_t>((kk * 2048) >> 4), IDESC_PV,
+                    (o_init[x] || kk > 0) ? 1u : 0u);
           o_init[x] = true;
         };
 
@@ -591,9 +594,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         const uint32_t vfp = (vpos / NV) & 1;
         ++vpos;
         if (!U.valid[x] || !(t.use >> x & 1)) continue;
-        if (!warp_wait(s_full + x, s_par, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
-        s_par ^= 1;
-        tc_fence_after();
+        // everything up to the first read of S depends only on the block: it is done before
+        // waiting for S, off the softmax -> PV -> QK^T -> softmax chain
         const uint32_t* cnt = reinterpret_cast<const uint32_t*>(auxc + vs * TC_BN);
         const bool cint = p.counts_is_int != 0;
         // a packed block with one common count is weighted through the exponent (no per-key work)
@@ -697,6 +699,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         // more than 2^8 above its reference stops the stream: the repair path below takes over
         // from that chunk. This is the only unrolled copy of the exponential loop.
         const bool fast = BF16 && !perkey && !any_mask && !__any_sync(0xFFFFFFFFu, m_used == -INFINITY);
+        if (!warp_wait(s_full + x, s_par, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
+        s_par ^= 1;
+        tc_fence_after();
         int stop = 0;  // first chunk the fast path did not finish
         if (fast) {
           const float nb = lw - m_used;
@@ -788,11 +793,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             tmem_st16(tS + c * 16, pc);
           }
         }
-        l += (la.x + la.y) + (lb.x + lb.y);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full + x);
+        l += (la.x + la.y) + (lb.x + lb.y);
         o_has = true;
       }
       if (!ok) break;
