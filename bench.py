@@ -484,6 +484,8 @@ def main():
     ap.add_argument("--n", type=int, default=None, help="sequence length override (profiling small cases)")
     ap.add_argument("--only-step", action="store_true",
                     help="time the hot-path step only (no comparator, e2e or CPU legs); for profiling")
+    ap.add_argument("--only-hbm", action="store_true",
+                    help="run the HBM-bound kernel measurements alone and print them; for profiling")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.n:
@@ -494,6 +496,9 @@ def main():
         run_reference(args, world, rank)
         return
     world, rank, local = dist_setup()
+    if args.only_hbm:
+        print(json.dumps(hbm_kernels(torch.device("cuda", local), 2000 + rank)), flush=True)
+        return
     try:
         run_ours(args, world, rank, local)
     finally:
