@@ -216,6 +216,86 @@ def delta_prefill(q, k, v, cos, sin, *, mode="periodic", keep_rate=0.25, thresho
     return o
 
 
+_side_streams = {}
+
+
+def _streams_for(dev: torch.device):
+    """One host->device and one device->host copy stream per device, created on first use."""
+    key = dev.index
+    if key not in _side_streams:
+        _side_streams[key] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return _side_streams[key]
+
+
+def delta_prefill_host(q, k, v, cos, sin, *, out, kv_heads_per_group=1, **kw):
+    """delta_prefill on host-resident inputs, writing a host-resident output.
+
+    q [B, Hq, N, d], k / v [B, Hkv, N, d] and out [B, Hq, N, d] are CPU tensors in head-major
+    layout, pinned (``pin_memory()``) so that the copies run asynchronously; cos / sin are
+    the device RoPE tables. Keyword arguments go to ``delta_prefill``.
+
+    Every kv-head (with its group of query heads) is independent in this layer-op with periodic
+    selection: packing and attention of kv-head h read only k / v head h and q heads
+    h*G .. h*G+G-1. The
+    heads are therefore processed in groups of ``kv_heads_per_group`` kv-heads, and group g's
+    host->device copies, group g-1's compute and group g-2's device->host copy run at the same
+    time on three streams. Results equal one ``delta_prefill`` call on the whole tensors.
+
+    Ordering: the copy streams first wait for the caller's current stream, and the current
+    stream waits for the last device->host copy before this returns, so work enqueued on the
+    current stream afterwards (an event, a synchronize) covers the whole layer-op.
+
+    Only ``mode="periodic"``: the delta and mask modes size the packed history by the largest
+    kept count over all heads (modeling_llama.py:656), and a head's padding changes its
+    schedule, so their heads are not independent.
+    """
+    if kw.get("mode", "periodic") != "periodic":
+        raise ValueError("delta_prefill_host: only mode='periodic' splits by kv-head (the delta and mask "
+                         "modes pad every head to the largest kept count); use delta_prefill")
+    for t in (q, k, v, out):
+        if t.is_cuda or not t.is_pinned():
+            raise RuntimeError("delta_prefill_host: q, k, v and out must be pinned host tensors")
+    L.require_cuda(cos, sin)
+    B, Hq, N, D = q.shape
+    Hkv = k.shape[1]
+    if Hq % Hkv or tuple(out.shape) != (B, Hq, N, D) or k.shape != v.shape or k.shape[0] != B:
+        raise ValueError("delta_prefill_host: shapes must be q/out [B, Hq, N, d], k/v [B, Hkv, N, d]")
+    G = Hq // Hkv
+    dev = cos.device
+    cur = torch.cuda.current_stream(dev)
+    h2d, d2h = _streams_for(dev)
+    dq = torch.empty(q.shape, dtype=q.dtype, device=dev)
+    dk = torch.empty(k.shape, dtype=k.dtype, device=dev)
+    dv = torch.empty(v.shape, dtype=v.dtype, device=dev)
+    do = torch.empty(out.shape, dtype=out.dtype, device=dev)
+    # the device buffers come from the current stream's pool: the copy streams start after it
+    h2d.wait_stream(cur)
+    d2h.wait_stream(cur)
+    step = max(1, int(kv_heads_per_group))
+    groups = [(a, min(Hkv, a + step)) for a in range(0, Hkv, step)]
+    ev_in = []
+    with torch.cuda.stream(h2d):
+        for a, b in groups:
+            for bi in range(B):
+                dk[bi, a:b].copy_(k[bi, a:b], non_blocking=True)
+                dv[bi, a:b].copy_(v[bi, a:b], non_blocking=True)
+                dq[bi, a * G:b * G].copy_(q[bi, a * G:b * G], non_blocking=True)
+            e = torch.cuda.Event()
+            e.record(h2d)
+            ev_in.append(e)
+    for (a, b), e in zip(groups, ev_in):
+        cur.wait_event(e)
+        delta_prefill(dq[:, a * G:b * G], dk[:, a:b], dv[:, a:b], cos, sin, out=do[:, a * G:b * G], **kw)
+        done = torch.cuda.Event()
+        done.record(cur)
+        d2h.wait_event(done)
+        with torch.cuda.stream(d2h):
+            for bi in range(B):
+                out[bi, a * G:b * G].copy_(do[bi, a * G:b * G], non_blocking=True)
+    cur.wait_stream(d2h)
+    return out
+
+
 def tile_count_periodic(N: int, r: int, W: int = 128) -> int:
     """128x128 tiles one head runs under the reference schedule with periodic-r packing."""
     nb = -(-N // 128)

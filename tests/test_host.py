@@ -80,6 +80,15 @@ def test_product_path_refuses_cpu_tensors(lib_path):
         ops.flash(x, x, x)
 
 
+def test_host_prefill_refuses_unpinned_or_device_buffers(lib_path):
+    """delta_prefill_host takes pinned host q / k / v / out only (no silent synchronous copies)."""
+    from deltaattention_b200 import ops
+    x = torch.zeros(1, 2, 128, 64, dtype=torch.bfloat16)
+    cos = torch.ones(128, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="pinned"):
+        ops.delta_prefill_host(x, x, x, cos, cos, out=x)
+
+
 def test_kernel_shim_binds_reference_argument_lists():
     """The drop-in kernel objects accept the reference launch's positional / keyword split and
     reject a call with a missing argument the way a Triton launch does (TypeError)."""
