@@ -7,10 +7,10 @@
 // per-(query block, head) tile list is exactly the reference's.
 //
 // Structure (persistent, one CTA per SM, 384 threads):
-//   warp 0      TMA producer: Q tiles, K/V tiles into a ring of shared-memory slots, and
-//               the packed tile's counts (and timestamps) next to its V tile
-//   warp 1      MMA issuer (one thread): S = Q K^T into TMEM, O += P V with P read from TMEM
-//   warp 2      TMEM allocator
+//   warp 0      TMA producer: Q tiles and K tiles into a ring of shared-memory slots
+//   warp 3      TMA producer: V tiles (ring), with the packed tile's counts (and timestamps)
+//   warps 1, 2  MMA issuers for query tile 0 / 1 (one elected lane each): S = Q K^T into
+//               TMEM, O += P V with P read from TMEM; warp 2 also allocates TMEM
 //   warps 4-7   softmax + epilogue for query tile 0 (TMEM lanes 0..127, one row per thread)
 //   warps 8-11  softmax + epilogue for query tile 1
 // A work unit is two 128-row query tiles that share every K/V tile: two q-heads of one
@@ -44,7 +44,7 @@ template <int D> struct TcCfg {
   static constexpr int OFF_AUXC = OFF_V + NV * KVBYTES;
   static constexpr int OFF_AUXT = OFF_AUXC + NV * TC_BN * 4;
   static constexpr int OFF_BAR = OFF_AUXT + NV * TC_BN * 4;
-  static constexpr int NBAR = 2 + 2 * NK + 2 * NV + 2 * 4 + 1;
+  static constexpr int NBAR = 2 + 2 * NK + 2 * NV + 2 * 6 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 64 + 1024;  // + alignment slack
 };
@@ -256,10 +256,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
   uint64_t* v_full = k_empty + NK;            // [NV]
   uint64_t* v_empty = v_full + NV;            // [NV]
   uint64_t* s_full = v_empty + NV;            // [2]
-  uint64_t* p_full = s_full + 2;              // [2]
-  uint64_t* o_full = p_full + 2;              // [2]
+  uint64_t* p_full = s_full + 2;              // [2] every P column of the block stored
+  uint64_t* p_lo = p_full + 2;                // [2] P of keys 0..63 stored
+  uint64_t* o_full = p_lo + 2;                // [2]
   uint64_t* tile_free = o_full + 2;           // [2]
   uint64_t* mma_done = tile_free + 2;
+  uint64_t* turn = mma_done + 1;              // [2] MMA warp x finished issuing a batch
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
   float* auxc = reinterpret_cast<float*>(smem + C::OFF_AUXC);
@@ -268,23 +270,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    mbar_init(q_empty, 2);  // one commit per MMA warp
     for (int s = 0; s < NK; ++s) {
       mbar_init(k_full + s, 1);
-      mbar_init(k_empty + s, 1);
+      mbar_init(k_empty + s, 2);
     }
     for (int s = 0; s < NV; ++s) {
       mbar_init(v_full + s, 1);
-      mbar_init(v_empty + s, 1);
+      mbar_init(v_empty + s, 2);
     }
     #pragma unroll
     for (int x = 0; x < 2; ++x) {
       mbar_init(s_full + x, 1);
       mbar_init(p_full + x, 4);
+      mbar_init(p_lo + x, 4);
       mbar_init(o_full + x, 1);
       mbar_init(tile_free + x, 4);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, 2);
+    mbar_init(turn + 0, 1);
+    mbar_init(turn + 1, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -423,83 +428,102 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         while (!mbar_try_wait(v_full + q % NV, (q / NV) & 1) && globaltimer() - t0 < 50000000ull) {}
       }
     }
-  } else if (warp == 1) {
-    // ================================================================ MMA issuer
-    // The whole warp runs this role converged (waits are warp-uniform); the tcgen05 helpers
-    // issue from one elected lane. Issue from a converged warp keeps descriptors and TMEM
-    // addresses warp-uniform: about 60 cycles per MMA issued instead of 75 from a lone lane.
+  } else if (warp == 1 || warp == 2) {
+    // ================================================================ MMA issuers
+    // One warp per query tile: warp 1 issues tile 0's MMAs, warp 2 tile 1's. Issuing tcgen05.mma
+    // slows the other warps on the issuing warp's scheduler (the softmax warps of lane quarter
+    // 1 ran ~300 cycles per block behind the others with one issuer for both tiles), so the
+    // load is split over two schedulers. The tiles use disjoint TMEM columns, so the two issue
+    // streams need no ordering between them; the K / V / Q slot releases take one commit from
+    // each warp (barrier counts of 2). Both warps wait on every K / V fill they release, even
+    // for blocks their tile skips, so a warp can never arrive for a later fill of a slot.
+    // The two warps issue their batches (a block's PV plus the next block's S) strictly in
+    // turn, tile 0 first, through the `turn` barriers: the tensor pipe then finishes tile 0's
+    // S about one batch before tile 1's, and the two tiles' softmax passes stay half a period
+    // apart instead of locking in phase and sharing the exponential unit.
+    // Each warp runs converged (waits are warp-uniform) and the tcgen05 helpers issue from one
+    // elected lane, which keeps descriptors and TMEM addresses warp-uniform.
     {
+      const int x = warp - 1;
       constexpr uint32_t IDESC_S = umma_idesc_f16(TC_BM, TC_BN, BF16, false);
       constexpr uint32_t IDESC_PV = umma_idesc_f16(TC_BM, D, BF16, true);
-      const uint32_t q_addr[2] = {smem_u32(smem + C::OFF_Q0), smem_u32(smem + C::OFF_Q1)};
-      const uint32_t k_addr0 = smem_u32(smem + C::OFF_K);
-      const uint32_t v_addr0 = smem_u32(smem + C::OFF_V);
-      const uint32_t tS[2] = {tmem + 0, tmem + 128};
-      const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
+      const uint32_t tS = tmem + 128 * x;
+      const uint32_t tO = tmem + 256 + D * x;
+      // shared-memory descriptors as base + constant: the start-address field (bits 0-13, in
+      // 16-byte units) of every operand is the base's plus a fixed offset
+      const uint64_t qdesc = umma_desc_sw128(smem_u32(smem + (x ? C::OFF_Q1 : C::OFF_Q0)), 16, 1024);
+      const uint64_t kdesc0 = umma_desc_sw128(smem_u32(smem + C::OFF_K), 16, 1024);
+      const uint64_t vdesc0 = umma_desc_sw128(smem_u32(smem + C::OFF_V), TC_BN * 128, 1024);
+      const bool sanity = p.variant == TC_SANITY;
       int kpos = 0, vpos = 0;  // K / V ring positions
-      uint32_t q_par = 0;
-      uint32_t free_par[2] = {1, 1};
-      uint32_t p_par[2] = {0, 0};
+      uint32_t q_par = 0, free_par = 1, p_par = 0;
+      uint32_t nbatch = 0;  // batches this warp has issued
       bool aborted = false;
+      // before batch k: tile 1 waits for tile 0's batch k, tile 0 for tile 1's batch k-1
+      auto my_turn = [&]() -> bool {
+        if (x == 1) return warp_wait(turn + 0, nbatch & 1, ab, ERR_TIMEOUT_MMA);
+        return nbatch == 0 || warp_wait(turn + 1, (nbatch - 1) & 1, ab, ERR_TIMEOUT_MMA);
+      };
+      auto end_turn = [&]() {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(turn + x);
+        ++nbatch;
+      };
       for (int it = 0; it < n_iter && !aborted; ++it) {
         const int u = unit_of(it, blockIdx.x, G);
         if (u >= p.num_units) continue;
         const Unit U = decode_unit(p, u);
+        const bool mine = U.valid[x];
         if (!warp_wait(q_full, q_par, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
         q_par ^= 1;
         tc_fence_after();
-        bool freed[2] = {false, false};
-        bool o_init[2] = {false, false};
-        auto ensure_free = [&](int x) -> bool {
-          if (freed[x]) return true;
-          if (!warp_wait(tile_free + x, free_par[x], ab, ERR_TIMEOUT_MMA)) return false;
-          free_par[x] ^= 1;
+        bool freed = false, o_init = false;
+        auto ensure_free = [&]() -> bool {
+          if (freed) return true;
+          if (!warp_wait(tile_free + x, free_par, ab, ERR_TIMEOUT_MMA)) return false;
+          free_par ^= 1;
           tc_fence_after();
-          freed[x] = true;
+          freed = true;
           return true;
         };
-        // shared-memory descriptors as base + constant: the start-address field (bits 0-13, in
-        // 16-byte units) of every operand is the base's plus a fixed offset
-        const uint64_t qdesc[2] = {umma_desc_sw128(q_addr[0], 16, 1024), umma_desc_sw128(q_addr[1], 16, 1024)};
-        const uint64_t kdesc0 = umma_desc_sw128(k_addr0, 16, 1024);
-        const uint64_t vdesc0 = umma_desc_sw128(v_addr0, TC_BN * 128, 1024);
-        auto issue_S = [&](int x, int kslot) {
+        auto issue_S = [&](int kslot) {
           const uint64_t kb = kdesc0 + static_cast<uint64_t>(kslot * (C::KVBYTES >> 4));
-          const uint64_t qb = qdesc[x];
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint64_t off = ((kk >> 2) * (TC_BM * 128) + (kk & 3) * 32) >> 4;
-            umma_ss(tS[x], qb + off, kb + off, IDESC_S, kk > 0);
+            umma_ss(tS, qdesc + off, kb + off, IDESC_S, kk > 0);
           }
         };
-        auto issue_PV = [&](int x, int vslot) {
+        // PV over keys 64*half .. 64*half+63 (P columns 32*half .. 32*half+31)
+        auto issue_PV = [&](int vslot, int half) {
           const uint64_t vb = vdesc0 + static_cast<uint64_t>(vslot * (C::KVBYTES >> 4));
 #pragma unroll
-          for (int kk = 0; kk < TC_BN / 16; ++kk)
-            umma_ts(tO[x], tS[x] + kk * 8, vb + static_cast<uint64_t>((kk * 2048) >> 4), IDESC_PV,
-                    (o_init[x] || kk > 0) ? 1u : 0u);
-          o_init[x] = true;
+          for (int k4 = 0; k4 < TC_BN / 32; ++k4) {
+            const int kk = half * (TC_BN / 32) + k4;
+            umma_ts(tO, tS + kk * 8, vb + static_cast<uint64_t>((kk * 2048) >> 4), IDESC_PV,
+                    (o_init || kk > 0) ? 1u : 0u);
+          }
+          o_init = true;
         };
+        auto uses = [&](const TileInfo& t) { return mine && (t.use >> x & 1); };
 
         TileSeq seq;
         seq.init(p, U);
         TileInfo cur, nxt;
         bool have_cur = seq.next(p, U, cur);
-        int cur_k, cur_v = -1;
-        const bool sanity = p.variant == TC_SANITY;
+        int cur_v = -1;
         if (have_cur) {
-          cur_k = kpos % NK;
-          if (!warp_wait(k_full + cur_k, (kpos / NK) & 1, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+          const int ck = kpos % NK;
+          if (!warp_wait(k_full + ck, (kpos / NK) & 1, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
           ++kpos;
           tc_fence_after();
-          #pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            if (!(cur.use >> x & 1)) continue;
-            issue_S(x, cur_k);
+          if (!my_turn()) { aborted = true; break; }
+          if (uses(cur)) {
+            issue_S(ck);
             if (!(sanity && cur.packed)) umma_commit(s_full + x);
           }
-          if (aborted) break;
-          umma_commit(k_empty + cur_k);
+          end_turn();
+          umma_commit(k_empty + ck);
         }
         bool q_released = false;
         while (have_cur) {
@@ -515,53 +539,51 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             umma_commit(q_empty);
             q_released = true;
           }
+          if (!my_turn()) { aborted = true; break; }
+          if (cur.needs_v && uses(cur)) {
+            // the first half of PV starts once the softmax has stored P of keys 0..63 (and
+            // has checked that keys 64..127 need no rescale), overlapping the second half's
+            // exponentials
+            if (!warp_wait(p_lo + x, p_par, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+            tc_fence_after();
+            // the first PV of a unit overwrites O: the previous unit's epilogue must be done
+            if (!ensure_free()) { aborted = true; break; }
+            issue_PV(cur_v, 0);
+            if (!warp_wait(p_full + x, p_par, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+            p_par ^= 1;
+            tc_fence_after();
+            issue_PV(cur_v, 1);
+          }
           int nk = -1;
-          bool nk_ready = false;
-          #pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            if (cur.needs_v && (cur.use >> x & 1)) {
-              if (!warp_wait(p_full + x, p_par[x], ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
-              p_par[x] ^= 1;
-              tc_fence_after();
-              // the first PV of a unit overwrites O: the previous unit's epilogue must be done
-              if (!ensure_free(x)) { aborted = true; break; }
-              issue_PV(x, cur_v);
-            }
-            if (have_nxt && (nxt.use >> x & 1)) {
-              if (!nk_ready) {
-                nk = kpos % NK;
-                if (!warp_wait(k_full + nk, (kpos / NK) & 1, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
-                ++kpos;
-                tc_fence_after();
-                nk_ready = true;
-              }
-              issue_S(x, nk);
+          if (have_nxt) {
+            nk = kpos % NK;
+            if (!warp_wait(k_full + nk, (kpos / NK) & 1, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
+            ++kpos;
+            tc_fence_after();
+            if (uses(nxt)) {
+              issue_S(nk);
               if (!(sanity && nxt.packed)) umma_commit(s_full + x);
             }
           }
-          if (aborted) break;
+          end_turn();
           if (cur.needs_v) umma_commit(v_empty + cur_v);
-          if (nk_ready) umma_commit(k_empty + nk);
+          if (have_nxt) umma_commit(k_empty + nk);
           if (!have_nxt) break;
           cur = nxt;
-          cur_k = nk;
         }
         if (aborted) break;
-        // Handshake per valid query tile and unit: the MMA waits tile_free once (before the
-        // unit's first PV into that tile's O, or here) and always commits o_full; the epilogue
-        // always waits o_full before arriving on tile_free. An epilogue therefore never
-        // arrives before the MMA's matching wait, which keeps the parity waits unambiguous.
-        // Invalid tiles take no part.
-        #pragma unroll
-        for (int x = 0; x < 2 && !aborted; ++x)
-          if (U.valid[x] && !ensure_free(x)) aborted = true;
-        if (aborted) break;
         if (!q_released) umma_commit(q_empty);
-        #pragma unroll
-        for (int x = 0; x < 2; ++x)
-          if (U.valid[x]) umma_commit(o_full + x);
+        // Handshake per valid query tile and unit: the MMA warp waits tile_free once (before
+        // the unit's first PV into the tile's O, or here) and always commits o_full; the
+        // epilogue always waits o_full before arriving on tile_free. An epilogue therefore
+        // never arrives before the matching wait, which keeps the parity waits unambiguous.
+        // Invalid tiles take no part.
+        if (mine) {
+          if (!ensure_free()) { aborted = true; break; }
+          umma_commit(o_full + x);
+        }
       }
-      // wait for every MMA this warp issued before TMEM can be released
+      // wait for every MMA this warp issued before TMEM can be released (one commit per warp)
       umma_commit(mma_done);
       const uint64_t t0 = globaltimer();
       while (!mbar_try_wait(mma_done, 0) && globaltimer() - t0 < 50000000ull) {}
@@ -700,12 +722,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         // each P chunk is stored as soon as it is computed. P chunk c covers columns
         // 16c..16c+15, below every S chunk not yet read. A chunk that raises some row's maximum
         // more than 2^8 above its reference stops the stream: the repair path below takes over
-        // from that chunk. This is the only unrolled copy of the exponential loop.
+        // from that chunk. P of keys 0..63 (chunks 0 and 1) is released to the MMA warp (p_lo)
+        // only after chunks 2 and 3 have passed the same check, so released P is final.
         const bool fast = BF16 && !perkey && !any_mask && !__any_sync(0xFFFFFFFFu, m_used == -INFINITY);
         if (!warp_wait(s_full + x, s_par, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
         s_par ^= 1;
         tc_fence_after();
         int stop = 0;  // first chunk the fast path did not finish
+        bool lo_sent = false;  // p_lo arrived (P of keys 0..63 final)
         if (fast) {
           const float nb = lw - m_used;
           const float lim_raise = m_used + 8.f;
@@ -713,23 +737,41 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           tmem_ld32_async(tS, sa);
           tmem_ld32_wait(sa);
           tmem_ld32_async(tS + 32, sb);
-          // one chunk: false when it stops the stream (no load is left in flight then)
+          // chunk c (0 or 1); false when it stops the stream (no load is left in flight then). On
+          // success chunk c+1 has landed in sn and chunk c+2 is loading into sc.
           auto step = [&](int c, uint32_t(&sc)[32], uint32_t(&sn)[32]) -> bool {
             if (__any_sync(0xFFFFFFFFu, chunk_max(sc) * sl2 > lim_raise)) {
-              if (c < 3) tmem_ld32_wait(sn);
+              tmem_ld32_wait(sn);
               stop = c;
               return false;
             }
             uint32_t pc[16];
             exp_plain(sc, nb, pc);
             tmem_st16(tS + c * 16, pc);
-            if (c < 3) {
-              tmem_ld32_wait(sn);
-              if (c < 2) tmem_ld32_async(tS + (c + 2) * 32, sc);
-            }
+            tmem_ld32_wait(sn);
+            tmem_ld32_async(tS + (c + 2) * 32, sc);
             return true;
           };
-          if (step(0, sa, sb) && step(1, sb, sa) && step(2, sa, sb) && step(3, sb, sa)) stop = 4;
+          if (step(0, sa, sb) && step(1, sb, sa)) {
+            // chunk 2 is in sa, chunk 3 lands in sb: both are checked before P of keys 0..63
+            // is released to the first half of PV, so nothing released is ever rescaled
+            tmem_ld32_wait(sb);
+            if (__any_sync(0xFFFFFFFFu, fmaxf(chunk_max(sa), chunk_max(sb)) * sl2 > lim_raise)) {
+              stop = 2;
+            } else {
+              tmem_st_wait();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(p_lo + x);
+              lo_sent = true;
+              uint32_t pc[16];
+              exp_plain(sa, nb, pc);
+              tmem_st16(tS + 32, pc);
+              exp_plain(sb, nb, pc);
+              tmem_st16(tS + 48, pc);
+              stop = 4;
+            }
+          }
         }
         if (stop < 4) {
           // exact / repair path from chunk `stop`: the row maximum over the chunks not yet done
@@ -799,7 +841,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(p_full + x);
+        if (lane == 0) {
+          if (!lo_sent) mbar_arrive(p_lo + x);
+          mbar_arrive(p_full + x);
+        }
         l += (la.x + la.y) + (lb.x + lb.y);
         o_has = true;
       }
