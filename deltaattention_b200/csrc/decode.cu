@@ -9,6 +9,7 @@
 //    group, so the packed cache is read from HBM once per kv-head (the reference reads it
 //    once per q-head). Each lane scores one key for every head; chunk max / sum use warp
 //    shuffles; partials (m, l, acc) are merged by decode_combine.
+#include <atomic>
 #include <type_traits>
 
 #include "common.cuh"
@@ -324,26 +325,80 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
   }
 }
 
-// Vectorised split-K decode for 16-bit types with unit head-dim strides: a CTA (4 warps)
-// scores 128 keys of one (batch, kv-head) for all G q-heads. QK: each lane owns one key and
-// reads its row with 16-byte loads; PV: each warp reads whole V rows (every lane 8 bytes of a
-// row, coalesced) for its 32 keys. Per-warp partial O are summed in shared memory.
+// Tensor-core split-K decode for 16-bit types with unit head-dim strides and 16-byte rows.
+// A CTA (4 warps) takes 128 keys of one (batch, kv-head) for all G (<= 8) q-heads:
+//   * every thread copies 16-byte row segments of the block's K and V rows into shared memory
+//     with cp.async (one memory round trip per CTA; rows past the end are zero-filled), with
+//     the segment index XOR-swizzled by the row so that ldmatrix reads are conflict-free;
+//   * each warp scores its 32 keys with mma.sync m16n8k16 (A = the q-heads padded to 16 rows,
+//     B = K rows via ldmatrix), runs the softmax of its 32 keys per head on the accumulator
+//     fragments (P cast to V's dtype, as the reference does before its PV product), and
+//     multiplies P by its V rows (ldmatrix.trans) with the P fragments reused in place as the
+//     A operand;
+//   * the four warps' (max, sum, O) are merged in shared memory into one partial per chunk.
+// The instruction count per key drops ~6x against scoring one key per lane on CUDA cores,
+// which left the kernel issue-bound at ~0.3 of HBM bandwidth.
 constexpr int DEC_VKC = 128;
-template <typename T, int D, int G>
-__global__ void __launch_bounds__(128) decode_attn_vec_kernel(
+
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t* r, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t* r, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// C (f32, 16x8) += A (16x16) * B (16x8), A row-major / B column-major, 16-bit inputs
+template <typename T>
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack_t2(float lo, float hi) {
+  return pack2(lo, hi, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
+}
+
+template <int D>
+constexpr int decode_mma_smem() {
+  return 256 * D * 2 + 8 * D * 2 + 128 * 4 + 2 * 4 * 8 * 4;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128) decode_attn_mma_kernel(
     const T* __restrict__ q, int64_t qs_b, int64_t qs_h, const T* __restrict__ kp, int64_t kps_b, int64_t kps_h,
     int64_t kps_n, const T* __restrict__ vp, int64_t vps_b, int64_t vps_h, int64_t vps_n,
     const int32_t* __restrict__ counts, int64_t cs_b, int64_t cs_h, int64_t cs_n, const int32_t* __restrict__ lengths,
     int64_t ls_b, int64_t ls_h, const T* __restrict__ ke, int64_t kes_b, int64_t kes_h, int64_t kes_n,
     const T* __restrict__ ve, int64_t ves_b, int64_t ves_h, int64_t ves_n, float sm_scale, int64_t exact_len,
-    int64_t Hkv, int64_t nchunk, float* __restrict__ part) {
-  constexpr int NW = DEC_VKC / 32;
-  constexpr int VE = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte load
-  constexpr int PL = D / 32;                            // head-dim elements per lane in PV
-  __shared__ float sq[G][D];
-  __shared__ float sp[G][DEC_VKC];
-  __shared__ float swm[NW][G], swl[NW][G];
-  __shared__ float so[NW][G][D];
+    int G, int64_t Hkv, int64_t nchunk, float* __restrict__ part) {
+  constexpr int ROWB = D * 2;   // bytes per K / V row
+  constexpr int SEGS = D / 8;   // 16-byte segments per row
+  extern __shared__ __align__(128) uint8_t dsm[];
+  uint8_t* Ks = dsm;                                          // [128][D], swizzled segments
+  uint8_t* Vs = dsm + DEC_VKC * ROWB;                         // [128][D], swizzled segments
+  T* qsm = reinterpret_cast<T*>(dsm + 2 * DEC_VKC * ROWB);    // [8][D], rows >= G zero
+  float* bias = reinterpret_cast<float*>(qsm + 8 * D);        // [128] log(count) of packed keys
+  float* swm = bias + DEC_VKC;                                // [4][8] per-warp max
+  float* swl = swm + 32;                                      // [4][8] per-warp sum
+  float* so = reinterpret_cast<float*>(Ks);                   // [4][G][D] per-warp O (after QK)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t chunk = blockIdx.x;
   const int64_t bk = blockIdx.y;
@@ -356,110 +411,162 @@ __global__ void __launch_bounds__(128) decode_attn_vec_kernel(
     if (tid < G) { pout[tid * (D + 2)] = -INFINITY; pout[tid * (D + 2) + 1] = 0.f; }
     return;
   }
-  for (int i = tid; i < G * D; i += DEC_VKC) sq[i / D][i % D] = to_f32(q[b * qs_b + (hk * G + i / D) * qs_h + i % D]);
-  __syncthreads();
-  // ---- scores: this lane's key
-  const int64_t key = k0 + warp * 32 + lane;
-  const bool valid = key < total;
-  const bool packed = key < plen;
-  float s[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) s[g] = 0.f;
-  if (valid) {
-    const T* kr = packed ? kp + b * kps_b + hk * kps_h + key * kps_n : ke + b * kes_b + hk * kes_h + (key - plen) * kes_n;
-    // the whole row is requested before any of it is used (one memory round trip per key)
-    union { uint4 u; T e[VE]; } raw[D / VE];
-#pragma unroll
-    for (int v = 0; v < D / VE; ++v) raw[v].u = __ldg(reinterpret_cast<const uint4*>(kr) + v);
-#pragma unroll
-    for (int v = 0; v < D / VE; ++v) {
-#pragma unroll
-      for (int e = 0; e < VE; ++e) {
-        const float kv = to_f32(raw[v].e[e]);
-#pragma unroll
-        for (int g = 0; g < G; ++g) s[g] = fmaf(sq[g][v * VE + e], kv, s[g]);
+  // ---- the block's K and V rows into shared memory (one round trip), q and the count biases.
+  // Thread t always copies 16-byte segment t % SEGS of rows t / SEGS + RPP*i; RPP is a multiple
+  // of 8, so the swizzled segment (s ^ (row & 7)) is the same for all of this thread's rows.
+  {
+    constexpr int RPP = 128 / SEGS;
+    const int s = tid % SEGS, r0 = tid / SEGS;
+    const uint32_t soff = static_cast<uint32_t>(r0 * ROWB + ((s ^ (r0 & 7)) << 4));
+    const uint32_t kd = smem_u32(Ks) + soff, vd = smem_u32(Vs) + soff;
+    const T* kb = kp + b * kps_b + hk * kps_h + s * 8;
+    const T* vb = vp + b * vps_b + hk * vps_h + s * 8;
+    if (k0 + DEC_VKC <= plen) {
+      // whole block in the packed history: fixed strides
+      const T* ks = kb + (k0 + r0) * kps_n;
+      const T* vs = vb + (k0 + r0) * vps_n;
+#pragma unroll 8
+      for (int i = 0; i < DEC_VKC / RPP; ++i) {
+        cp_async16_zfill(kd + i * RPP * ROWB, ks + i * RPP * kps_n, true);
+        cp_async16_zfill(vd + i * RPP * ROWB, vs + i * RPP * vps_n, true);
+      }
+    } else {
+      // packed tail, exact window, or past the end (zero-filled)
+      const T* keb = ke + b * kes_b + hk * kes_h + s * 8;
+      const T* veb = ve + b * ves_b + hk * ves_h + s * 8;
+      for (int i = 0; i < DEC_VKC / RPP; ++i) {
+        const int64_t key = k0 + r0 + i * RPP;
+        const bool ok = key < total;
+        const bool pk = key < plen;
+        const T* ks = !ok ? kb : (pk ? kb + key * kps_n : keb + (key - plen) * kes_n);
+        const T* vs = !ok ? vb : (pk ? vb + key * vps_n : veb + (key - plen) * ves_n);
+        cp_async16_zfill(kd + i * RPP * ROWB, ks, ok);
+        cp_async16_zfill(vd + i * RPP * ROWB, vs, ok);
       }
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  const float bias = (valid && packed) ? logf(static_cast<float>(counts[b * cs_b + hk * cs_h + key * cs_n])) : 0.f;
-  // each warp runs its own softmax over its 32 keys (no CTA-wide step between QK and PV, so
-  // one warp's V loads overlap another warp's K loads); the CTA merges the warps at the end
-  float mw[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    s[g] = valid ? s[g] * sm_scale + bias : -INFINITY;
-    float m = s[g];
-#pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-    mw[g] = m;
-    const float ref = (m == -INFINITY) ? 0.f : m;
-    const float pv = valid ? expf(s[g] - ref) : 0.f;
-    sp[g][warp * 32 + lane] = round_as<T>(pv);  // P is cast to V's dtype before the PV product
-    float l = pv;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
-    if (lane == 0) { swm[warp][g] = m; swl[warp][g] = l; }
+  // q rows 0..G-1 (A-fragment rows 0..7; rows 8..15 are never read, their fragments are 0)
+  for (int i = tid; i < 8 * D; i += 128) {
+    const int g = i / D, d = i % D;
+    qsm[i] = g < G ? q[b * qs_b + (hk * G + g) * qs_h + d] : from_f32<T>(0.f);
   }
-  __syncwarp();
-  // ---- PV over this warp's 32 keys: lane owns head-dim elements [lane * PL, lane * PL + PL)
-  float o[G][PL];
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int e = 0; e < PL; ++e) o[g][e] = 0.f;
-  const int64_t kw = k0 + warp * 32;
-  const int nk = static_cast<int>((total - kw) < 32 ? (total - kw) : 32);
-  // all of this warp's V rows are requested first (rows past the end read row 0, weighted 0)
-  using VU = typename std::conditional<PL == 4, uint2, uint32_t>::type;
-  union { VU u; T e[PL]; } vraw[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const int64_t kk = (j < nk) ? kw + j : 0;
-    const T* vr = (kk < plen) ? vp + b * vps_b + hk * vps_h + kk * vps_n : ve + b * ves_b + hk * ves_h + (kk - plen) * ves_n;
-    vraw[j].u = __ldg(reinterpret_cast<const VU*>(vr + lane * PL));
+  {
+    const int64_t key = k0 + tid;
+    bias[tid] = (key < plen) ? logf(static_cast<float>(counts[b * cs_b + hk * cs_h + key * cs_n])) : 0.f;
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+
+  const int g = lane >> 2;        // head row of this thread's accumulator fragments (rows g+8 are padding)
+  const int c2 = (lane & 3) * 2;  // first of the two key / head-dim columns this thread holds
+  // ---- S^T = q . K^T for this warp's 32 keys: four n-tiles of 8 keys
+  float acc[4][4];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
+  for (int j = 0; j < 4; ++j)
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float pj = (j < nk) ? sp[g][warp * 32 + j] : 0.f;
+    for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
 #pragma unroll
-      for (int e = 0; e < PL; ++e) o[g][e] = fmaf(pj, to_f32(vraw[j].e[e]), o[g][e]);
+  for (int kp2 = 0; kp2 < D / 32; ++kp2) {
+    uint32_t qa[2][2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const T* qr = qsm + g * D + (2 * kp2 + h) * 16 + c2;
+      qa[h][0] = *reinterpret_cast<const uint32_t*>(qr);
+      qa[h][1] = *reinterpret_cast<const uint32_t*>(qr + 8);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = 32 * warp + 8 * j + (lane & 7);
+      const int s = 4 * kp2 + (lane >> 3);
+      uint32_t bb[4];
+      ldsm_x4(bb, smem_u32(Ks + r * ROWB + ((s ^ (r & 7)) << 4)));
+      mma16816<T>(acc[j], qa[0][0], 0u, qa[0][1], 0u, bb[0], bb[1]);
+      mma16816<T>(acc[j], qa[1][0], 0u, qa[1][1], 0u, bb[2], bb[3]);
     }
   }
+  // ---- softmax of this warp's 32 keys for head g (each thread holds 8 of them)
+  float mx = -INFINITY;
 #pragma unroll
-  for (int g = 0; g < G; ++g)
+  for (int j = 0; j < 4; ++j)
 #pragma unroll
-    for (int e = 0; e < PL; ++e) so[warp][g][lane * PL + e] = o[g][e];
+    for (int e = 0; e < 2; ++e) {
+      const int kl = 32 * warp + 8 * j + c2 + e;
+      const bool ok = k0 + kl < total;
+      acc[j][e] = ok ? acc[j][e] * sm_scale + bias[kl] : -INFINITY;
+      mx = fmaxf(mx, acc[j][e]);
+    }
+  mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+  const float ref = (mx == -INFINITY) ? 0.f : mx;
+  float l = 0.f;
+  uint32_t pa[4];  // P of n-tile j as bf16x2 / f16x2 (keys c2, c2+1), cast to V's dtype
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float p0 = acc[j][0] == -INFINITY ? 0.f : expf(acc[j][0] - ref);
+    const float p1 = acc[j][1] == -INFINITY ? 0.f : expf(acc[j][1] - ref);
+    l += p0 + p1;
+    pa[j] = pack_t2<T>(p0, p1);
+  }
+  l += __shfl_xor_sync(0xFFFFFFFFu, l, 1);
+  l += __shfl_xor_sync(0xFFFFFFFFu, l, 2);
+  if ((lane & 3) == 0 && g < G) { swm[warp * 8 + g] = mx; swl[warp * 8 + g] = l; }
+  // ---- O = P . V over this warp's 32 keys (two k-steps of 16 keys, D/8 n-tiles)
+  float o[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 2; ++kk) {
+    const int mi = lane >> 3;
+    const int r = 32 * warp + 16 * kk + (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+    for (int np = 0; np < D / 16; ++np) {
+      const int s = 2 * np + (mi >> 1);
+      uint32_t bb[4];
+      ldsm_x4_t(bb, smem_u32(Vs + r * ROWB + ((s ^ (r & 7)) << 4)));
+      mma16816<T>(o[2 * np], pa[2 * kk], 0u, pa[2 * kk + 1], 0u, bb[0], bb[1]);
+      mma16816<T>(o[2 * np + 1], pa[2 * kk], 0u, pa[2 * kk + 1], 0u, bb[2], bb[3]);
+    }
+  }
+  __syncthreads();  // every warp is done reading K / V: the K rows' space takes the partial O
+  if (g < G) {
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      float* dst = so + (warp * G + g) * D + 8 * n + c2;
+      dst[0] = o[n][0];
+      dst[1] = o[n][1];
+    }
+  }
   __syncthreads();
   // merge the warps: reference = the chunk maximum, each warp's partial scaled to it
-  for (int i = tid; i < G * D; i += DEC_VKC) {
-    const int g = i / D, d = i % D;
-    float M = swm[0][g];
+  for (int i = tid; i < G * D; i += 128) {
+    const int h = i / D, d = i % D;
+    float M = swm[h];
 #pragma unroll
-    for (int w = 1; w < NW; ++w) M = fmaxf(M, swm[w][g]);
-    float acc = 0.f;
+    for (int w = 1; w < 4; ++w) M = fmaxf(M, swm[w * 8 + h]);
+    float a = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < NW; ++w)
-        if (swm[w][g] != -INFINITY) acc = fmaf(so[w][g][d], expf(swm[w][g] - M), acc);
+      for (int w = 0; w < 4; ++w)
+        if (swm[w * 8 + h] != -INFINITY) a = fmaf(so[(w * G + h) * D + d], expf(swm[w * 8 + h] - M), a);
     }
-    pout[g * (D + 2) + 2 + d] = acc;
+    pout[h * (D + 2) + 2 + d] = a;
   }
   if (tid < G) {
-    float M = swm[0][tid];
+    float M = swm[tid];
 #pragma unroll
-    for (int w = 1; w < NW; ++w) M = fmaxf(M, swm[w][tid]);
-    float l = 0.f;
+    for (int w = 1; w < 4; ++w) M = fmaxf(M, swm[w * 8 + tid]);
+    float lt = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < NW; ++w)
-        if (swm[w][tid] != -INFINITY) l = fmaf(swl[w][tid], expf(swm[w][tid] - M), l);
+      for (int w = 0; w < 4; ++w)
+        if (swm[w * 8 + tid] != -INFINITY) lt = fmaf(swl[w * 8 + tid], expf(swm[w * 8 + tid] - M), lt);
     }
     pout[tid * (D + 2)] = M;
-    pout[tid * (D + 2) + 1] = l;
+    pout[tid * (D + 2) + 1] = lt;
   }
-  (void)mw;
 }
 
 size_t decode_attn_workspace(int64_t B, int64_t Hq, int64_t capacity, int64_t exact_len, int64_t head_dim) {
@@ -478,33 +585,45 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
   if (B * Hkv == 0) return cudaSuccess;
   if (G < 1 || G > DEC_GMAX) return cudaErrorInvalidValue;
   {
-    // vectorised path: 16-bit types, head_dim 64 / 128, unit head-dim strides, 16-byte rows
+    // tensor-core path: 16-bit types, head_dim 64 / 128, unit head-dim strides, 16-byte rows
     auto a16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
-    const bool shape_ok = (dtype == BF16 || dtype == F16) && (head_dim == 64 || head_dim == 128) &&
-                          (G == 1 || G == 2 || G == 4 || G == 8);
+    const bool shape_ok = (dtype == BF16 || dtype == F16) && (head_dim == 64 || head_dim == 128);
     const bool layout_ok = qs[2] == 1 && kps[3] == 1 && vps[3] == 1 && kes[3] == 1 && ves[3] == 1 && a16(kp) &&
                            a16(vp) && a16(ke) && a16(ve) && (kps[0] % 8 | kps[1] % 8 | kps[2] % 8) == 0 &&
                            (vps[0] % 8 | vps[1] % 8 | vps[2] % 8) == 0 && (kes[0] % 8 | kes[1] % 8 | kes[2] % 8) == 0 &&
-                           (ves[0] % 8 | ves[1] % 8 | ves[2] % 8) == 0 && (reinterpret_cast<uintptr_t>(vp) & 7) == 0;
+                           (ves[0] % 8 | ves[1] % 8 | ves[2] % 8) == 0;
     if (shape_ok && layout_ok) {
       int64_t nc = (capacity + exact_len + DEC_VKC - 1) / DEC_VKC;
       if (nc < 1) nc = 1;
       dim3 g2(static_cast<unsigned>(nc), static_cast<unsigned>(B * Hkv));
-#define DAB_DECV(TY, DD, GG)                                                                                       decode_attn_vec_kernel<TY, DD, GG><<<g2, DEC_VKC, 0, st>>>(                                                             static_cast<const TY*>(q), qs[0], qs[1], static_cast<const TY*>(kp), kps[0], kps[1], kps[2],                    static_cast<const TY*>(vp), vps[0], vps[1], vps[2], counts, cs[0], cs[1], cs[2], lengths, ls[0], ls[1],         static_cast<const TY*>(ke), kes[0], kes[1], kes[2], static_cast<const TY*>(ve), ves[0], ves[1], ves[2],         sm_scale, exact_len, Hkv, nc, part);                                                                         decode_combine_kernel<TY, DD><<<static_cast<unsigned>(B * Hkv * GG), 128, 0, st>>>(                                part, static_cast<TY*>(out), os[0], os[1], os[2], GG, Hkv, nc, head_dim);                                    return cudaGetLastError();
-#define DAB_DECV_G(TY, DD) \
-  switch (G) {             \
-    case 1: DAB_DECV(TY, DD, 1) \
-    case 2: DAB_DECV(TY, DD, 2) \
-    case 4: DAB_DECV(TY, DD, 4) \
-    default: DAB_DECV(TY, DD, 8) \
-  }
-#define DAB_DECV_D(TY)                         \
-  if (head_dim == 64) { DAB_DECV_G(TY, 64) } \
-  else { DAB_DECV_G(TY, 128) }
-      if (dtype == BF16) { DAB_DECV_D(__nv_bfloat16) } else { DAB_DECV_D(__half) }
-#undef DAB_DECV_D
-#undef DAB_DECV_G
-#undef DAB_DECV
+      auto run = [&](auto tag, auto dd) -> cudaError_t {
+        using TY = decltype(tag);
+        constexpr int DD = decltype(dd)::value;
+        constexpr int SM = decode_mma_smem<DD>();
+        // the dynamic shared-memory limit is raised once per instantiation and device
+        static std::atomic<uint64_t> attr_set{0};
+        int dev = 0;
+        cudaError_t ea = cudaGetDevice(&dev);
+        if (ea != cudaSuccess) return ea;
+        const uint64_t bit = 1ull << (dev & 63);
+        if (!(attr_set.load() & bit)) {
+          ea = cudaFuncSetAttribute(decode_attn_mma_kernel<TY, DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM);
+          if (ea != cudaSuccess) return ea;
+          attr_set.fetch_or(bit);
+        }
+        decode_attn_mma_kernel<TY, DD><<<g2, 128, SM, st>>>(
+            static_cast<const TY*>(q), qs[0], qs[1], static_cast<const TY*>(kp), kps[0], kps[1], kps[2],
+            static_cast<const TY*>(vp), vps[0], vps[1], vps[2], counts, cs[0], cs[1], cs[2], lengths, ls[0], ls[1],
+            static_cast<const TY*>(ke), kes[0], kes[1], kes[2], static_cast<const TY*>(ve), ves[0], ves[1], ves[2],
+            sm_scale, exact_len, static_cast<int>(G), Hkv, nc, part);
+        decode_combine_kernel<TY, DD><<<static_cast<unsigned>(B * Hkv * G), 128, 0, st>>>(
+            part, static_cast<TY*>(out), os[0], os[1], os[2], G, Hkv, nc, head_dim);
+        return cudaGetLastError();
+      };
+      using I64 = std::integral_constant<int, 64>;
+      using I128 = std::integral_constant<int, 128>;
+      if (dtype == BF16) return head_dim == 64 ? run(__nv_bfloat16{}, I64{}) : run(__nv_bfloat16{}, I128{});
+      return head_dim == 64 ? run(__half{}, I64{}) : run(__half{}, I128{});
     }
   }
   int bd = 16;

@@ -419,6 +419,38 @@ def test_decode_replay_matches_reference(golden, name, dt, use_cos):
     _cmp(torch.stack(outs), torch.from_numpy(g["outputs"]), dt, name)
 
 
+@pytest.mark.parametrize("dt,D,G,B,Hkv", [(torch.bfloat16, 128, 4, 3, 2), (torch.float16, 64, 8, 2, 1),
+                                          (torch.bfloat16, 128, 1, 2, 2), (torch.bfloat16, 64, 2, 1, 3)])
+def test_decode_attention_16bit_matches_oracle(dt, D, G, B, Hkv):
+    """The 16-bit decode path (tensor-core split-K chunks of 128 keys, then the combine) on
+    ragged packed lengths (0, short, not multiples of 128, several chunks) plus an exact
+    window, against the oracle's fused_hybrid_decode_kernel restatement."""
+    import deltaDecoding as dd
+    g = torch.Generator().manual_seed(40 + D + G)
+    cap, W = 700, 24
+    Hq = Hkv * G
+    kp = (torch.randn((B, Hkv, cap, D), generator=g) * 0.5).to(dt)
+    vp = torch.randn((B, Hkv, cap, D), generator=g).to(dt)
+    cnt = torch.randint(1, 9, (B, Hkv, cap), generator=g, dtype=torch.int32)
+    lens_all = [0, 5, 127, 128, 129, 300, 650, 700]
+    lens = torch.tensor([lens_all[(i * 3 + 1) % len(lens_all)] for i in range(B * Hkv)], dtype=torch.int32)
+    lens = lens.view(B, Hkv)
+    ke = (torch.randn((B, Hkv, W, D), generator=g) * 0.5).to(dt)
+    ve = torch.randn((B, Hkv, W, D), generator=g).to(dt)
+    q = (torch.randn((B, Hq, D), generator=g) * 0.5).to(dt)
+    for exact_len in (W, 7):
+        ref = O.decode_attention(q, kp, vp, cnt, lens, ke, ve, D ** -0.5, exact_len, G)
+        c = lambda t: t.cuda()  # noqa: E731
+        qc, kpc, vpc, cc, lc, kec, vec = c(q), c(kp), c(vp), c(cnt), c(lens), c(ke), c(ve)
+        out = torch.empty_like(qc)
+        dd.fused_hybrid_decode_kernel[(B, Hq)](
+            qc, kpc, vpc, cc, lc, kec, vec, out, *qc.stride(), *kpc.stride(), *vpc.stride(), *cc.stride(),
+            *lc.stride(), *kec.stride(), *vec.stride(), *out.stride(), D ** -0.5, exact_len, G, head_dim=D,
+            BLOCK_M=16, BLOCK_N=128, BLOCK_D=D)
+        _cmp(out, ref, dt, f"decode16/{D}/{G}/{exact_len}")
+    _check_ws_clean()
+
+
 def test_hybrid_cache_end_to_end():
     """HybridCompressedCache: prefill hand-off then decode steps, against the oracle."""
     import types
