@@ -63,34 +63,47 @@ __global__ void __launch_bounds__(256) schedule_kernel(const int32_t* __restrict
   const int bh = blockIdx.x;
   const int b = bh / Hts, h = bh % Hts;
   const int32_t* tsr = ts + b * tsb + h * tsh;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int j = warp; j < nblk; j += blockDim.x >> 5) {
+  // four threads per packed block, 32 consecutive keys each: every thread requests all of its
+  // timestamps and counts before using any (one memory round trip per 64 blocks)
+  const int tid = threadIdx.x;
+  for (int j0 = 0; j0 < nblk; j0 += 64) {
+    const int j = j0 + (tid >> 2);
+    const int k0 = j * TC_BN + (tid & 3) * 32;
     int tmax = INT32_MIN, tmin = INT32_MAX;
     float cmin = INFINITY, cmax = -INFINITY;
-    for (int e = lane; e < TC_BN; e += 32) {
-      const int key = j * TC_BN + e;
-      int t;
-      if (key < num_packed) {
-        t = tsr[static_cast<int64_t>(key) * tsn];
-        const int64_t off = b * cb + h * ch + static_cast<int64_t>(key) * cn;
-        const float c = counts_is_int ? static_cast<float>(static_cast<const int32_t*>(counts)[off])
-                                      : static_cast<const float*>(counts)[off];
-        if (c > 0.f) tmin = min(tmin, t);
-        cmin = fminf(cmin, c);
-        cmax = fmaxf(cmax, c);
-      } else {
-        t = seq_k + 1;
+    if (j < nblk) {
+      int tv[32];
+      float cv[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int key = k0 + e;
+        tv[e] = seq_k + 1;  // masked lanes of a partial block
+        cv[e] = 0.f;
+        if (key < num_packed) {
+          tv[e] = tsr[static_cast<int64_t>(key) * tsn];
+          const int64_t off = b * cb + h * ch + static_cast<int64_t>(key) * cn;
+          cv[e] = counts_is_int ? static_cast<float>(static_cast<const int32_t*>(counts)[off])
+                                : static_cast<const float*>(counts)[off];
+        }
       }
-      tmax = max(tmax, t);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        if (k0 + e < num_packed) {
+          if (cv[e] > 0.f) tmin = min(tmin, tv[e]);
+          cmin = fminf(cmin, cv[e]);
+          cmax = fmaxf(cmax, cv[e]);
+        }
+        tmax = max(tmax, tv[e]);
+      }
     }
 #pragma unroll
-    for (int o = 16; o; o >>= 1) {
+    for (int o = 1; o <= 2; o <<= 1) {
       tmax = max(tmax, __shfl_xor_sync(0xFFFFFFFFu, tmax, o));
       tmin = min(tmin, __shfl_xor_sync(0xFFFFFFFFu, tmin, o));
       cmin = fminf(cmin, __shfl_xor_sync(0xFFFFFFFFu, cmin, o));
       cmax = fmaxf(cmax, __shfl_xor_sync(0xFFFFFFFFu, cmax, o));
     }
-    if (lane == 0) {
+    if ((tid & 3) == 0 && j < nblk) {
       sT[j] = tmax;
       if (want_blkmin) blkmin[static_cast<int64_t>(bh) * nblk + j] = tmin;
       // a block whose valid keys share one count c is weighted by adding log2(c) to the
