@@ -326,18 +326,19 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
 }
 
 // Tensor-core split-K decode for 16-bit types with unit head-dim strides and 16-byte rows.
-// A CTA (4 warps) takes 128 keys of one (batch, kv-head) for all G (<= 8) q-heads:
+// A CTA (DEC_NW = 8 warps) takes 128 keys of one (batch, kv-head) for all G (<= 8) q-heads:
 //   * every thread copies 16-byte row segments of the block's K and V rows into shared memory
 //     with cp.async (one memory round trip per CTA; rows past the end are zero-filled), with
 //     the segment index XOR-swizzled by the row so that ldmatrix reads are conflict-free;
-//   * each warp scores its 32 keys with mma.sync m16n8k16 (A = the q-heads padded to 16 rows,
-//     B = K rows via ldmatrix), runs the softmax of its 32 keys per head on the accumulator
-//     fragments (P cast to V's dtype, as the reference does before its PV product), and
-//     multiplies P by its V rows (ldmatrix.trans) with the P fragments reused in place as the
-//     A operand;
-//   * the four warps' (max, sum, O) are merged in shared memory into one partial per chunk.
-// The instruction count per key drops ~6x against scoring one key per lane on CUDA cores,
-// which left the kernel issue-bound at ~0.3 of HBM bandwidth.
+//   * warp w scores keys 16w..16w+15 with mma.sync m16n8k16 (A = the q-heads padded to 16 rows,
+//     B = K rows via ldmatrix);
+//   * the chunk's row maximum per head goes through shared memory, and P = exp(s - max), cast
+//     to V's dtype as the reference does before its PV product, is written to shared memory;
+//   * warp w multiplies P by V for head-dim columns D/8*w.. over all 128 keys (V by
+//     ldmatrix.trans), so the warps' outputs need no merge; (max, sum, O) form the chunk's
+//     partial for the combine kernel.
+// Against scoring one key per lane on CUDA cores (68 M instructions per launch, issue-bound at
+// ~0.3 of HBM bandwidth) this issues a fraction of the instructions.
 constexpr int DEC_VKC = 128;
 
 __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool valid) {
@@ -352,6 +353,9 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t* r, uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t* r, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
 }
 // C (f32, 16x8) += A (16x16) * B (16x8), A row-major / B column-major, 16-bit inputs
 template <typename T>
@@ -376,13 +380,15 @@ __device__ __forceinline__ uint32_t pack_t2(float lo, float hi) {
   return pack2(lo, hi, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
 }
 
+constexpr int DEC_NW = 8;  // warps per CTA: 16 keys each
+constexpr int DEC_PROW = DEC_VKC + 8;  // padded P row (elements): conflict-free A-fragment loads
 template <int D>
 constexpr int decode_mma_smem() {
-  return 256 * D * 2 + 8 * D * 2 + 128 * 4 + 2 * 4 * 8 * 4;
+  return 256 * D * 2 + 8 * D * 2 + 128 * 4 + 2 * DEC_NW * 8 * 4 + 8 * DEC_PROW * 2;
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(128) decode_attn_mma_kernel(
+__global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
     const T* __restrict__ q, int64_t qs_b, int64_t qs_h, const T* __restrict__ kp, int64_t kps_b, int64_t kps_h,
     int64_t kps_n, const T* __restrict__ vp, int64_t vps_b, int64_t vps_h, int64_t vps_n,
     const int32_t* __restrict__ counts, int64_t cs_b, int64_t cs_h, int64_t cs_n, const int32_t* __restrict__ lengths,
@@ -391,14 +397,18 @@ __global__ void __launch_bounds__(128) decode_attn_mma_kernel(
     int G, int64_t Hkv, int64_t nchunk, float* __restrict__ part) {
   constexpr int ROWB = D * 2;   // bytes per K / V row
   constexpr int SEGS = D / 8;   // 16-byte segments per row
+  constexpr int NT = DEC_NW * 32;        // threads
+  constexpr int KPW = DEC_VKC / DEC_NW;  // keys per warp
+  constexpr int NTW = KPW / 8;           // QK n-tiles per warp
   extern __shared__ __align__(128) uint8_t dsm[];
   uint8_t* Ks = dsm;                                          // [128][D], swizzled segments
   uint8_t* Vs = dsm + DEC_VKC * ROWB;                         // [128][D], swizzled segments
   T* qsm = reinterpret_cast<T*>(dsm + 2 * DEC_VKC * ROWB);    // [8][D], rows >= G zero
   float* bias = reinterpret_cast<float*>(qsm + 8 * D);        // [128] log(count) of packed keys
-  float* swm = bias + DEC_VKC;                                // [4][8] per-warp max
-  float* swl = swm + 32;                                      // [4][8] per-warp sum
-  float* so = reinterpret_cast<float*>(Ks);                   // [4][G][D] per-warp O (after QK)
+  float* swm = bias + DEC_VKC;                                // [NW][8] per-warp max
+  float* swl = swm + DEC_NW * 8;                              // [NW][8] per-warp sum
+  T* Ps = reinterpret_cast<T*>(swl + DEC_NW * 8);             // [8][PROW] P of the chunk
+  constexpr int PROW = DEC_PROW;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t chunk = blockIdx.x;
   const int64_t bk = blockIdx.y;
@@ -415,7 +425,7 @@ __global__ void __launch_bounds__(128) decode_attn_mma_kernel(
   // Thread t always copies 16-byte segment t % SEGS of rows t / SEGS + RPP*i; RPP is a multiple
   // of 8, so the swizzled segment (s ^ (row & 7)) is the same for all of this thread's rows.
   {
-    constexpr int RPP = 128 / SEGS;
+    constexpr int RPP = NT / SEGS;
     const int s = tid % SEGS, r0 = tid / SEGS;
     const uint32_t soff = static_cast<uint32_t>(r0 * ROWB + ((s ^ (r0 & 7)) << 4));
     const uint32_t kd = smem_u32(Ks) + soff, vd = smem_u32(Vs) + soff;
@@ -447,11 +457,11 @@ __global__ void __launch_bounds__(128) decode_attn_mma_kernel(
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
   // q rows 0..G-1 (A-fragment rows 0..7; rows 8..15 are never read, their fragments are 0)
-  for (int i = tid; i < 8 * D; i += 128) {
+  for (int i = tid; i < 8 * D; i += NT) {
     const int g = i / D, d = i % D;
     qsm[i] = g < G ? q[b * qs_b + (hk * G + g) * qs_h + d] : from_f32<T>(0.f);
   }
-  {
+  if (tid < DEC_VKC) {
     const int64_t key = k0 + tid;
     bias[tid] = (key < plen) ? logf(static_cast<float>(counts[b * cs_b + hk * cs_h + key * cs_n])) : 0.f;
   }
@@ -460,10 +470,10 @@ __global__ void __launch_bounds__(128) decode_attn_mma_kernel(
 
   const int g = lane >> 2;        // head row of this thread's accumulator fragments (rows g+8 are padding)
   const int c2 = (lane & 3) * 2;  // first of the two key / head-dim columns this thread holds
-  // ---- S^T = q . K^T for this warp's 32 keys: four n-tiles of 8 keys
-  float acc[4][4];
+  // ---- S^T = q . K^T for this warp's KPW keys: n-tiles of 8 keys
+  float acc[NTW][4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
+  for (int j = 0; j < NTW; ++j)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
 #pragma unroll
@@ -476,8 +486,8 @@ __global__ void __launch_bounds__(128) decode_attn_mma_kernel(
       qa[h][1] = *reinterpret_cast<const uint32_t*>(qr + 8);
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = 32 * warp + 8 * j + (lane & 7);
+    for (int j = 0; j < NTW; ++j) {
+      const int r = KPW * warp + 8 * j + (lane & 7);
       const int s = 4 * kp2 + (lane >> 3);
       uint32_t bb[4];
       ldsm_x4(bb, smem_u32(Ks + r * ROWB + ((s ^ (r & 7)) << 4)));
@@ -485,87 +495,78 @@ __global__ void __launch_bounds__(128) decode_attn_mma_kernel(
       mma16816<T>(acc[j], qa[1][0], 0u, qa[1][1], 0u, bb[2], bb[3]);
     }
   }
-  // ---- softmax of this warp's 32 keys for head g (each thread holds 8 of them)
+  // ---- softmax over the chunk's 128 keys for head g: each warp's maximum through shared
+  // memory, one chunk maximum, P = exp(s - max) cast to V's dtype into shared memory
   float mx = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
+  for (int j = 0; j < NTW; ++j)
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const int kl = 32 * warp + 8 * j + c2 + e;
+      const int kl = KPW * warp + 8 * j + c2 + e;
       const bool ok = k0 + kl < total;
       acc[j][e] = ok ? acc[j][e] * sm_scale + bias[kl] : -INFINITY;
       mx = fmaxf(mx, acc[j][e]);
     }
   mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
   mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
-  const float ref = (mx == -INFINITY) ? 0.f : mx;
-  float l = 0.f;
-  uint32_t pa[4];  // P of n-tile j as bf16x2 / f16x2 (keys c2, c2+1), cast to V's dtype
+  if ((lane & 3) == 0) swm[warp * 8 + g] = mx;
+  __syncthreads();
+  float M = swm[g];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int w = 1; w < DEC_NW; ++w) M = fmaxf(M, swm[w * 8 + g]);
+  const float ref = (M == -INFINITY) ? 0.f : M;
+  float l = 0.f;
+#pragma unroll
+  for (int j = 0; j < NTW; ++j) {
     const float p0 = acc[j][0] == -INFINITY ? 0.f : expf(acc[j][0] - ref);
     const float p1 = acc[j][1] == -INFINITY ? 0.f : expf(acc[j][1] - ref);
     l += p0 + p1;
-    pa[j] = pack_t2<T>(p0, p1);
+    *reinterpret_cast<uint32_t*>(Ps + g * PROW + KPW * warp + 8 * j + c2) = pack_t2<T>(p0, p1);
   }
   l += __shfl_xor_sync(0xFFFFFFFFu, l, 1);
   l += __shfl_xor_sync(0xFFFFFFFFu, l, 2);
-  if ((lane & 3) == 0 && g < G) { swm[warp * 8 + g] = mx; swl[warp * 8 + g] = l; }
-  // ---- O = P . V over this warp's 32 keys (two k-steps of 16 keys, D/8 n-tiles)
-  float o[D / 8][4];
+  if ((lane & 3) == 0) swl[warp * 8 + g] = l;
+  __syncthreads();
+  // ---- O = P . V: warp w owns head-dim columns (D / NW) * w .. over all 128 keys, so the
+  // warps' outputs need no merge
+  constexpr int NTD = D / 8 / DEC_NW;  // n-tiles of 8 columns per warp (2 for d = 128, 1 for 64)
+  float o[NTD][4];
 #pragma unroll
-  for (int n = 0; n < D / 8; ++n)
+  for (int n = 0; n < NTD; ++n)
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
+  const int mi = lane >> 3;
 #pragma unroll
-  for (int kk = 0; kk < 2; ++kk) {
-    const int mi = lane >> 3;
-    const int r = 32 * warp + 16 * kk + (mi & 1) * 8 + (lane & 7);
-#pragma unroll
-    for (int np = 0; np < D / 16; ++np) {
-      const int s = 2 * np + (mi >> 1);
+  for (int kk = 0; kk < DEC_VKC / 16; ++kk) {
+    const uint32_t a0 = *reinterpret_cast<const uint32_t*>(Ps + g * PROW + 16 * kk + c2);
+    const uint32_t a2 = *reinterpret_cast<const uint32_t*>(Ps + g * PROW + 16 * kk + 8 + c2);
+    const int r = 16 * kk + (mi & 1) * 8 + (lane & 7);
+    if constexpr (NTD == 2) {
+      const int s = 2 * warp + (mi >> 1);
       uint32_t bb[4];
       ldsm_x4_t(bb, smem_u32(Vs + r * ROWB + ((s ^ (r & 7)) << 4)));
-      mma16816<T>(o[2 * np], pa[2 * kk], 0u, pa[2 * kk + 1], 0u, bb[0], bb[1]);
-      mma16816<T>(o[2 * np + 1], pa[2 * kk], 0u, pa[2 * kk + 1], 0u, bb[2], bb[3]);
+      mma16816<T>(o[0], a0, 0u, a2, 0u, bb[0], bb[1]);
+      mma16816<T>(o[1], a0, 0u, a2, 0u, bb[2], bb[3]);
+    } else {
+      uint32_t bb[2];
+      ldsm_x2_t(bb, smem_u32(Vs + r * ROWB + ((warp ^ (r & 7)) << 4)));
+      mma16816<T>(o[0], a0, 0u, a2, 0u, bb[0], bb[1]);
     }
   }
-  __syncthreads();  // every warp is done reading K / V: the K rows' space takes the partial O
   if (g < G) {
 #pragma unroll
-    for (int n = 0; n < D / 8; ++n) {
-      float* dst = so + (warp * G + g) * D + 8 * n + c2;
+    for (int n = 0; n < NTD; ++n) {
+      float* dst = pout + g * (D + 2) + 2 + (D / DEC_NW) * warp + 8 * n + c2;
       dst[0] = o[n][0];
       dst[1] = o[n][1];
     }
-  }
-  __syncthreads();
-  // merge the warps: reference = the chunk maximum, each warp's partial scaled to it
-  for (int i = tid; i < G * D; i += 128) {
-    const int h = i / D, d = i % D;
-    float M = swm[h];
+    if (warp == 0 && (lane & 3) == 0) {
+      float lt = 0.f;
 #pragma unroll
-    for (int w = 1; w < 4; ++w) M = fmaxf(M, swm[w * 8 + h]);
-    float a = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < 4; ++w)
-        if (swm[w * 8 + h] != -INFINITY) a = fmaf(so[(w * G + h) * D + d], expf(swm[w * 8 + h] - M), a);
+      for (int w = 0; w < DEC_NW; ++w) lt += swl[w * 8 + g];
+      pout[g * (D + 2)] = M;
+      pout[g * (D + 2) + 1] = lt;
     }
-    pout[h * (D + 2) + 2 + d] = a;
-  }
-  if (tid < G) {
-    float M = swm[tid];
-#pragma unroll
-    for (int w = 1; w < 4; ++w) M = fmaxf(M, swm[w * 8 + tid]);
-    float lt = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < 4; ++w)
-        if (swm[w * 8 + tid] != -INFINITY) lt = fmaf(swl[w * 8 + tid], expf(swm[w * 8 + tid] - M), lt);
-    }
-    pout[tid * (D + 2)] = M;
-    pout[tid * (D + 2) + 1] = lt;
   }
 }
 
@@ -611,7 +612,7 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
           if (ea != cudaSuccess) return ea;
           attr_set.fetch_or(bit);
         }
-        decode_attn_mma_kernel<TY, DD><<<g2, 128, SM, st>>>(
+        decode_attn_mma_kernel<TY, DD><<<g2, DEC_NW * 32, SM, st>>>(
             static_cast<const TY*>(q), qs[0], qs[1], static_cast<const TY*>(kp), kps[0], kps[1], kps[2],
             static_cast<const TY*>(vp), vps[0], vps[1], vps[2], counts, cs[0], cs[1], cs[2], lengths, ls[0], ls[1],
             static_cast<const TY*>(ke), kes[0], kes[1], kes[2], static_cast<const TY*>(ve), ves[0], ves[1], ves[2],

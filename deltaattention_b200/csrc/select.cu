@@ -382,15 +382,18 @@ __global__ void __launch_bounds__(256) rope_kernel(const T* __restrict__ x, int6
   yr[(i + half) * yd] = from_f32<T>(o2);
 }
 
-// Contiguous-row RoPE (unit stride along d in x, y and the tables): one thread loads 16 bytes
-// of the first half of a row and the matching 16 bytes of the second half, with the same
-// per-element rounding sequence as rope_kernel. Grid: (rows of one head / rows per block,
-// heads, batch), so no index division by runtime sizes.
+// Contiguous-row RoPE (unit stride along d in x, y and the tables): one thread takes 16 bytes
+// of the first half of a row and the matching 16 bytes of the second half, for the same
+// position in ROPE_HB heads, with the same per-element rounding sequence as rope_kernel. Its
+// cos / sin vectors are loaded once for all those heads, and every head's inputs are
+// requested before any is used. Grid: (rows of one head / rows per block, head groups,
+// batch), so no index division by runtime sizes.
+constexpr int ROPE_HB = 8;  // heads per thread: one cos / sin load serves ROPE_HB rows
 template <typename T, int D>
 __global__ void __launch_bounds__(256) rope_rows_kernel(const T* __restrict__ x, int64_t xb, int64_t xh, int64_t xs,
                                                         T* __restrict__ y, int64_t yb, int64_t yh, int64_t ys,
                                                         const T* __restrict__ cs, const T* __restrict__ sn,
-                                                        int64_t cb, int64_t cs_s, int N) {
+                                                        int64_t cb, int64_t cs_s, int N, int H) {
   constexpr int V = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte vector
   constexpr int HALF = D / 2;
   constexpr int TPR = HALF / V;                          // threads per row
@@ -398,28 +401,42 @@ __global__ void __launch_bounds__(256) rope_rows_kernel(const T* __restrict__ x,
   const int s = blockIdx.x * RPB + static_cast<int>(threadIdx.x) / TPR;
   if (s >= N) return;
   const int i = (static_cast<int>(threadIdx.x) % TPR) * V;
-  const int64_t b = blockIdx.z, h = blockIdx.y;
-  const T* xr = x + b * xb + h * xh + s * xs;
-  T* yr = y + b * yb + h * yh + s * ys;
+  const int64_t b = blockIdx.z;
+  const int h0 = blockIdx.y * ROPE_HB;
+  const int nh = (H - h0) < ROPE_HB ? (H - h0) : ROPE_HB;
   const int64_t c0 = b * cb + s * cs_s;
   union Vec { uint4 u; T e[V]; };
-  Vec x1, x2, c1, c2, s1, s2, o1, o2;
-  x1.u = *reinterpret_cast<const uint4*>(xr + i);
-  x2.u = *reinterpret_cast<const uint4*>(xr + i + HALF);
+  Vec c1, c2, s1, s2;
   c1.u = __ldg(reinterpret_cast<const uint4*>(cs + c0 + i));
   c2.u = __ldg(reinterpret_cast<const uint4*>(cs + c0 + i + HALF));
   s1.u = __ldg(reinterpret_cast<const uint4*>(sn + c0 + i));
   s2.u = __ldg(reinterpret_cast<const uint4*>(sn + c0 + i + HALF));
+  // every head's two input vectors are requested before any is used
+  Vec x1[ROPE_HB], x2[ROPE_HB];
 #pragma unroll
-  for (int e = 0; e < V; ++e) {
-    const float a1 = to_f32(x1.e[e]), a2 = to_f32(x2.e[e]);
-    o1.e[e] = from_f32<T>(__fadd_rn(round_as<T>(__fmul_rn(a1, to_f32(c1.e[e]))),
-                                    round_as<T>(__fmul_rn(-a2, to_f32(s1.e[e])))));
-    o2.e[e] = from_f32<T>(__fadd_rn(round_as<T>(__fmul_rn(a2, to_f32(c2.e[e]))),
-                                    round_as<T>(__fmul_rn(a1, to_f32(s2.e[e])))));
+  for (int hh = 0; hh < ROPE_HB; ++hh) {
+    if (hh < nh) {
+      const T* xr = x + b * xb + (h0 + hh) * xh + s * xs;
+      x1[hh].u = *reinterpret_cast<const uint4*>(xr + i);
+      x2[hh].u = *reinterpret_cast<const uint4*>(xr + i + HALF);
+    }
   }
-  *reinterpret_cast<uint4*>(yr + i) = o1.u;
-  *reinterpret_cast<uint4*>(yr + i + HALF) = o2.u;
+#pragma unroll
+  for (int hh = 0; hh < ROPE_HB; ++hh) {
+    if (hh >= nh) continue;
+    Vec o1, o2;
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const float a1 = to_f32(x1[hh].e[e]), a2 = to_f32(x2[hh].e[e]);
+      o1.e[e] = from_f32<T>(__fadd_rn(round_as<T>(__fmul_rn(a1, to_f32(c1.e[e]))),
+                                      round_as<T>(__fmul_rn(-a2, to_f32(s1.e[e])))));
+      o2.e[e] = from_f32<T>(__fadd_rn(round_as<T>(__fmul_rn(a2, to_f32(c2.e[e]))),
+                                      round_as<T>(__fmul_rn(a1, to_f32(s2.e[e])))));
+    }
+    T* yr = y + b * yb + (h0 + hh) * yh + s * ys;
+    *reinterpret_cast<uint4*>(yr + i) = o1.u;
+    *reinterpret_cast<uint4*>(yr + i + HALF) = o2.u;
+  }
 }
 
 template <typename T, int D>
@@ -433,10 +450,11 @@ static bool try_rope_rows(const void* x, const int64_t* xs, void* y, const int64
   for (int64_t v : {xs[0], xs[1], xs[2], ys[0], ys[1], ys[2], css[0], css[1]})
     if (v % V != 0) return false;
   if (B > 65535 || H > 65535 || N > (int64_t{1} << 30)) return false;
-  const dim3 grid(static_cast<unsigned>((N + RPB - 1) / RPB), static_cast<unsigned>(H), static_cast<unsigned>(B));
+  const dim3 grid(static_cast<unsigned>((N + RPB - 1) / RPB), static_cast<unsigned>((H + ROPE_HB - 1) / ROPE_HB),
+                  static_cast<unsigned>(B));
   rope_rows_kernel<T, D><<<grid, 256, 0, st>>>(static_cast<const T*>(x), xs[0], xs[1], xs[2], static_cast<T*>(y), ys[0],
                                                ys[1], ys[2], static_cast<const T*>(cs), static_cast<const T*>(sn),
-                                               css[0], css[1], static_cast<int>(N));
+                                               css[0], css[1], static_cast<int>(N), static_cast<int>(H));
   *err = cudaGetLastError();
   return true;
 }
@@ -563,7 +581,7 @@ __global__ void __launch_bounds__(PACK_TILE) keep_pack_kernel(
     int64_t xh, int64_t xs, const T* __restrict__ v, int64_t vb, int64_t vh, int64_t vs, T* __restrict__ kp,
     T* __restrict__ vp, int64_t pb, int64_t ph, int64_t ps, int32_t* __restrict__ ts, int32_t* __restrict__ counts,
     int64_t mb, int64_t mh, int32_t* __restrict__ index_map, const int32_t* tile_off, const int32_t* next_first,
-    int64_t H, int64_t N, int64_t D, int64_t ntile, int64_t capacity) {
+    int64_t H, int64_t N, int64_t D, int64_t ntile, int64_t capacity, int vec16) {
   __shared__ int32_t warp_off[PACK_TILE / 32];
   __shared__ int32_t pos_of[PACK_TILE];
   __shared__ int32_t total;
@@ -600,6 +618,41 @@ __global__ void __launch_bounds__(PACK_TILE) keep_pack_kernel(
     ts[b * mb + h * mh + j] = static_cast<int32_t>(s);
     counts[b * mb + h * mh + j] = nxt - static_cast<int32_t>(s);
   }
+  if (vec16) {
+    // 16-byte rows: the warp's kept rows are flattened into (row, 16-byte piece) work items,
+    // lane i takes items i, i+32, ...; four items' loads are issued before their stores
+    const int nv = static_cast<int>(D * static_cast<int64_t>(sizeof(T)) / 16);
+    const int nrows = __popc(bal);
+    const int items = nrows * nv;
+    const int lbase = warp_off[warp];
+    for (int i0 = lane; i0 < items; i0 += 4 * 32) {
+      uint4 kr4[4], vr4[4];
+      int64_t dst[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = i0 + u * 32;
+        dst[u] = -1;
+        if (idx < items) {
+          const int r = idx / nv, c = idx % nv;
+          const int loc = lbase + r;
+          const int32_t jj = base + loc;
+          if (jj < capacity) {
+            const int64_t ss = pos_of[loc];
+            kr4[u] = *(reinterpret_cast<const uint4*>(k + b * xb + h * xh + ss * xs) + c);
+            vr4[u] = *(reinterpret_cast<const uint4*>(v + b * vb + h * vh + ss * vs) + c);
+            dst[u] = (b * pb + h * ph + static_cast<int64_t>(jj) * ps) * static_cast<int64_t>(sizeof(T)) + c * 16;
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (dst[u] < 0) continue;
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(kp) + dst[u]) = kr4[u];
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(vp) + dst[u]) = vr4[u];
+      }
+    }
+    return;
+  }
   // each warp copies the K/V rows of its kept lanes
   for (unsigned m = bal; m; m &= m - 1) {
     const int src = __ffs(m) - 1;
@@ -613,6 +666,40 @@ __global__ void __launch_bounds__(PACK_TILE) keep_pack_kernel(
     for (int64_t d = lane; d < D; d += 32) {
       kd[d] = kr[d];
       vd[d] = vr[d];
+    }
+  }
+}
+
+// slots [anchors[bh], capacity) of every head: zero K / V rows, timestamps and counts (the
+// reference packs into zero-initialised tensors; writing the padding here spares the caller a
+// memset of the whole packed history)
+template <typename T>
+__global__ void __launch_bounds__(256) pack_pad_kernel(T* __restrict__ kp, T* __restrict__ vp, int64_t pb, int64_t ph,
+                                                       int64_t ps, int32_t* __restrict__ ts,
+                                                       int32_t* __restrict__ counts, int64_t mb, int64_t mh,
+                                                       const int32_t* __restrict__ anchors, int64_t H, int64_t D,
+                                                       int64_t capacity, int vec16) {
+  const int64_t bh = blockIdx.y;
+  const int64_t b = bh / H, h = bh % H;
+  const int64_t j0 = anchors[bh] + static_cast<int64_t>(blockIdx.x) * 32;
+  if (j0 >= capacity) return;
+  const int64_t rows = (capacity - j0) < 32 ? (capacity - j0) : 32;
+  if (threadIdx.x < rows) {
+    ts[b * mb + h * mh + j0 + threadIdx.x] = 0;
+    counts[b * mb + h * mh + j0 + threadIdx.x] = 0;
+  }
+  if (vec16) {
+    const int nv = static_cast<int>(D * static_cast<int64_t>(sizeof(T)) / 16);
+    for (int64_t i = threadIdx.x; i < rows * nv; i += blockDim.x) {
+      const int64_t off = (b * pb + h * ph + (j0 + i / nv) * ps) * static_cast<int64_t>(sizeof(T)) + (i % nv) * 16;
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(kp) + off) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(vp) + off) = make_uint4(0, 0, 0, 0);
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < rows * D; i += blockDim.x) {
+      const int64_t off = b * pb + h * ph + (j0 + i / D) * ps + i % D;
+      kp[off] = from_f32<T>(0.f);
+      vp[off] = from_f32<T>(0.f);
     }
   }
 }
@@ -635,11 +722,20 @@ cudaError_t launch_pack_from_keep(int dtype, const int32_t* keep, const int64_t*
       keep, kms[0], kms[1], kms[2], H, N, tile_cnt, tile_first, ntile);
   keep_tile_scan_kernel<<<static_cast<unsigned>(BH), 32, 0, st>>>(tile_cnt, tile_first, tile_off, next_first,
                                                                   anchors, max_anchors, ntile, N);
-#define DAB_KP(TY)                                                                                           \
-  keep_pack_kernel<TY><<<dim3(static_cast<unsigned>(ntile), static_cast<unsigned>(BH)), PACK_TILE, 0, st>>>( \
-      keep, kms[0], kms[1], kms[2], static_cast<const TY*>(k), xs[0], xs[1], xs[2],                         \
-      static_cast<const TY*>(v), vs[0], vs[1], vs[2], static_cast<TY*>(kp), static_cast<TY*>(vp), ps[0],     \
-      ps[1], ps[2], ts, counts, ms[0], ms[1], index_map, tile_off, next_first, H, N, D, ntile, capacity);    \
+  const size_t es = dtype == F32 ? 4 : 2;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const int vec16 = al16(k) && al16(v) && al16(kp) && al16(vp) && (D * es) % 16 == 0 &&
+                    ((xs[0] | xs[1] | xs[2] | vs[0] | vs[1] | vs[2] | ps[0] | ps[1] | ps[2]) * es) % 16 == 0;
+  const unsigned pad_blocks = static_cast<unsigned>((capacity + 31) / 32);
+#define DAB_KP(TY)                                                                                               \
+  keep_pack_kernel<TY><<<dim3(static_cast<unsigned>(ntile), static_cast<unsigned>(BH)), PACK_TILE, 0, st>>>(     \
+      keep, kms[0], kms[1], kms[2], static_cast<const TY*>(k), xs[0], xs[1], xs[2],                             \
+      static_cast<const TY*>(v), vs[0], vs[1], vs[2], static_cast<TY*>(kp), static_cast<TY*>(vp), ps[0],         \
+      ps[1], ps[2], ts, counts, ms[0], ms[1], index_map, tile_off, next_first, H, N, D, ntile, capacity, vec16); \
+  if (capacity > 0)                                                                                              \
+    pack_pad_kernel<TY><<<dim3(pad_blocks, static_cast<unsigned>(BH)), 256, 0, st>>>(                           \
+        static_cast<TY*>(kp), static_cast<TY*>(vp), ps[0], ps[1], ps[2], ts, counts, ms[0], ms[1], anchors, H, D, \
+        capacity, vec16);                                                                                        \
   return cudaGetLastError();
   switch (dtype) {
     case F32: DAB_KP(float)

@@ -89,8 +89,9 @@ def delta_keep_mask(k_rot: torch.Tensor, threshold: float, similarity: str = "eu
     nch = max(1, -(-N // cs))
     use_cos = similarity == "cosine"
     thr = threshold if use_cos else threshold ** 2
-    keep = torch.zeros((B, H, N), dtype=torch.int32, device=k_rot.device)
-    cc = torch.zeros((B, H, nch), dtype=torch.int32, device=k_rot.device)
+    # the scan writes every position and every chunk count
+    keep = torch.empty((B, H, N), dtype=torch.int32, device=k_rot.device)
+    cc = torch.empty((B, H, nch), dtype=torch.int32, device=k_rot.device)
     bd = 1 << max(4, (D - 1).bit_length())
     chunked_eval_kernel[(B * H, nch)](
         k_rot, keep, cc, thr, *k_rot.stride(), *keep.stride(), *cc.stride(), N, D, cs, num_heads=H,
@@ -107,12 +108,13 @@ def pack_from_keep(k_rot: torch.Tensor, v: torch.Tensor, keep: torch.Tensor, num
         num_packed = int(keep.sum(-1).max().item())  # the reference's packed length (modeling_llama.py:656)
     M = int(num_packed)
     dev = k_rot.device
-    kp = torch.zeros((B, H, M, D), dtype=k_rot.dtype, device=dev)
-    vp = torch.zeros_like(kp)
-    ts = torch.zeros((B, H, M), dtype=torch.int32, device=dev)
-    cnt = torch.zeros_like(ts)
-    anchors = torch.zeros((B * H,), dtype=torch.int32, device=dev)
-    mx = torch.zeros((1,), dtype=torch.int32, device=dev)
+    # every slot is written by the library (padding past a head's anchors with zeros)
+    kp = torch.empty((B, H, M, D), dtype=k_rot.dtype, device=dev)
+    vp = torch.empty_like(kp)
+    ts = torch.empty((B, H, M), dtype=torch.int32, device=dev)
+    cnt = torch.empty_like(ts)
+    anchors = torch.empty((B * H,), dtype=torch.int32, device=dev)
+    mx = torch.empty((1,), dtype=torch.int32, device=dev)
     im = torch.empty((B, H, N), dtype=torch.int32, device=dev) if want_index_map else None
     lib = L.load()
     st = L.stream_of(k_rot)

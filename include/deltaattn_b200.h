@@ -177,9 +177,10 @@ size_t dab_pack_from_keep_workspace_size(int64_t batch, int64_t heads, int64_t s
 
 /* Device-side packing from a keep mask (modeling_llama.py:655-685 without the host sync at
  * :656): index_map = cumsum(keep) - 1 (optional, [B][H][N] contiguous), packed K/V rows,
- * timestamps and run-length counts into buffers of `capacity` rows (rows beyond a head's
- * anchors are left untouched: zero-initialise them for the reference's padding
- * semantics), anchors per head and their maximum (the reference's M). */
+ * timestamps and run-length counts into buffers of `capacity` rows, anchors per head and
+ * their maximum (the reference's M). Rows beyond a head's anchors are written with zero
+ * K / V, timestamp 0 and count 0: the reference's zero-initialised padding, so the caller
+ * need not clear the buffers. */
 int dab_pack_from_keep(const int32_t* keep_mask, const int64_t* km_strides, const void* k, const int64_t* k_strides,
                        const void* v, const int64_t* v_strides, void* k_packed, void* v_packed,
                        const int64_t* pack_strides, int32_t* packed_ts, int32_t* packed_counts,
