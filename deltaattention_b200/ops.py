@@ -229,7 +229,7 @@ def _streams_for(dev: torch.device):
     return _side_streams[key]
 
 
-def delta_prefill_host(q, k, v, cos, sin, *, out, kv_heads_per_group=1, **kw):
+def delta_prefill_host(q, k, v, cos, sin, *, out, kv_heads_per_group=1, q_heads_per_group=None, **kw):
     """delta_prefill on host-resident inputs, writing a host-resident output.
 
     q [B, Hq, N, d], k / v [B, Hkv, N, d] and out [B, Hq, N, d] are CPU tensors in head-major
@@ -239,7 +239,9 @@ def delta_prefill_host(q, k, v, cos, sin, *, out, kv_heads_per_group=1, **kw):
     Every kv-head (with its group of query heads) is independent in this layer-op with periodic
     selection: packing and attention of kv-head h read only k / v head h and q heads
     h*G .. h*G+G-1. The
-    heads are therefore processed in groups of ``kv_heads_per_group`` kv-heads, and group g's
+    heads are therefore processed in groups of ``kv_heads_per_group`` kv-heads (or, with
+    ``q_heads_per_group`` below a kv-head's query-head count, groups of that many query heads
+    of one kv-head, whose K / V are copied with its first group), and group g's
     host->device copies, group g-1's compute and group g-2's device->host copy run at the same
     time on three streams. Results equal one ``delta_prefill`` call on the whole tensors.
 
@@ -273,27 +275,35 @@ def delta_prefill_host(q, k, v, cos, sin, *, out, kv_heads_per_group=1, **kw):
     # the device buffers come from the current stream's pool: the copy streams start after it
     h2d.wait_stream(cur)
     d2h.wait_stream(cur)
-    step = max(1, int(kv_heads_per_group))
-    groups = [(a, min(Hkv, a + step)) for a in range(0, Hkv, step)]
+    # groups: (kv-heads [a, b), query heads [qa, qb), copy K / V of [a, b) with this group)
+    qg = G if q_heads_per_group is None else int(q_heads_per_group)
+    if 1 <= qg < G:
+        if G % qg:
+            raise ValueError("delta_prefill_host: q_heads_per_group must divide the query heads per kv-head")
+        groups = [(a, a + 1, a * G + s, a * G + s + qg, s == 0) for a in range(Hkv) for s in range(0, G, qg)]
+    else:
+        step = max(1, int(kv_heads_per_group))
+        groups = [(a, min(Hkv, a + step), a * G, min(Hkv, a + step) * G, True) for a in range(0, Hkv, step)]
     ev_in = []
     with torch.cuda.stream(h2d):
-        for a, b in groups:
+        for a, b, qa, qb, with_kv in groups:
             for bi in range(B):
-                dk[bi, a:b].copy_(k[bi, a:b], non_blocking=True)
-                dv[bi, a:b].copy_(v[bi, a:b], non_blocking=True)
-                dq[bi, a * G:b * G].copy_(q[bi, a * G:b * G], non_blocking=True)
+                if with_kv:
+                    dk[bi, a:b].copy_(k[bi, a:b], non_blocking=True)
+                    dv[bi, a:b].copy_(v[bi, a:b], non_blocking=True)
+                dq[bi, qa:qb].copy_(q[bi, qa:qb], non_blocking=True)
             e = torch.cuda.Event()
             e.record(h2d)
             ev_in.append(e)
-    for (a, b), e in zip(groups, ev_in):
+    for (a, b, qa, qb, _), e in zip(groups, ev_in):
         cur.wait_event(e)
-        delta_prefill(dq[:, a * G:b * G], dk[:, a:b], dv[:, a:b], cos, sin, out=do[:, a * G:b * G], **kw)
+        delta_prefill(dq[:, qa:qb], dk[:, a:b], dv[:, a:b], cos, sin, out=do[:, qa:qb], **kw)
         done = torch.cuda.Event()
         done.record(cur)
         d2h.wait_event(done)
         with torch.cuda.stream(d2h):
             for bi in range(B):
-                out[bi, a * G:b * G].copy_(do[bi, a * G:b * G], non_blocking=True)
+                out[bi, qa:qb].copy_(do[bi, qa:qb], non_blocking=True)
     cur.wait_stream(d2h)
     return out
 

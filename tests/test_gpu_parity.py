@@ -313,8 +313,8 @@ def test_native_gqa_prefill_matches_oracle(mode):
     _check_ws_clean()
 
 
-@pytest.mark.parametrize("B,group", [(2, 1), (1, 2), (1, 3)])
-def test_host_pipelined_prefill_equals_device_call(B, group):
+@pytest.mark.parametrize("B,group,qgroup", [(2, 1, None), (1, 2, None), (1, 3, None), (2, 1, 1), (1, 1, 2)])
+def test_host_pipelined_prefill_equals_device_call(B, group, qgroup):
     """ops.delta_prefill_host (kv-head groups, copies overlapped with compute on three streams)
     writes exactly what one ops.delta_prefill call on the device tensors returns."""
     from deltaattention_b200 import ops, synth
@@ -326,7 +326,8 @@ def test_host_pipelined_prefill_equals_device_call(B, group):
     hq, hk, hv = (t.contiguous().cpu().pin_memory() for t in (q, k, v))
     ho = torch.full((B, Hq, N, D), float("nan"), dtype=torch.bfloat16).pin_memory()
     for _ in range(2):  # a second call reuses the cached copy streams
-        ops.delta_prefill_host(hq, hk, hv, cos, sin, out=ho, kv_heads_per_group=group, **kw)
+        ops.delta_prefill_host(hq, hk, hv, cos, sin, out=ho, kv_heads_per_group=group, q_heads_per_group=qgroup,
+                               **kw)
         torch.cuda.current_stream().synchronize()
         assert torch.equal(ho.view(torch.int16), want.view(torch.int16))
     _check_ws_clean()
