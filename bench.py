@@ -143,6 +143,69 @@ def hbm_kernels(dev, seed):
     return out
 
 
+def decode_step(dev, seed, layers=32, steps=20):
+    """One decode token over every layer of a Llama-3.1-8B-shaped model with the device-length
+    cache (cache.DeviceDecodeCache): 16 sequences, Hq=32 / Hkv=8, d=128, packed lengths
+    uniform in [1024, 8192] per (sequence, kv-head), exact window 100. Timed as eager
+    launches (update, advance, attention + combine per layer) and as one replayed CUDA graph.
+    HBM bytes per step: packed K / V rows, counts and the window read once per layer
+    (516 B per key), as in hbm_kernels."""
+    from deltaattention_b200.cache import DeviceDecodeCache
+    from deltaattention_b200 import _lib as L
+    B, Hq, Hkv, D, W, cap = 16, 32, 8, 128, 100, 8192 + 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    c = DeviceDecodeCache(layers, B, Hkv, D, cap, W, torch.bfloat16, device=dev, threshold=8.0)
+    c.k_packed.normal_(generator=g)
+    c.v_packed.normal_(generator=g)
+    c.packed_counts.fill_(4)
+    c.k_exact.normal_(generator=g)
+    c.v_exact.normal_(generator=g)
+    lens = torch.randint(1024, 8193, (B * Hkv,), generator=g, device=dev, dtype=torch.int32)
+    c.packed_lengths.copy_(lens.expand(layers, -1))
+    c.seq_state[:, 0] = W
+    c.seq_state[:, 1] = 65536
+    q = torch.randn((layers, B, Hq, D), generator=g, device=dev).bfloat16()
+    kn = torch.randn((layers, B, Hkv, 1, D), generator=g, device=dev).bfloat16()
+    vn = torch.randn((layers, B, Hkv, 1, D), generator=g, device=dev).bfloat16()
+    out = torch.empty_like(q)
+
+    def eager():
+        for layer in range(layers):
+            c.step(layer, q[layer], kn[layer], vn[layer], out[layer])
+
+    for _ in range(3):
+        eager()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        eager()
+    e1.record()
+    torch.cuda.synchronize()
+    eager_ms = e0.elapsed_time(e1) / steps
+    graph = c.capture_step(q, kn, vn, out)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    graph_ms = e0.elapsed_time(e1) / steps
+    keys = int(c.packed_lengths.sum().item()) + layers * B * Hkv * W
+    nbytes = keys * 516
+    err = int(c.err.item())
+    del graph
+    codes = L.workspace_errors()
+    peak, _ = hbm_peak()
+    return {"layers": layers, "shape": f"B={B} Hq={Hq} Hkv={Hkv} d={D} packed U[1024,8192] window {W}",
+            "eager_ms": eager_ms, "graph_ms": graph_ms, "tokens_per_s": B / (graph_ms / 1000.0),
+            "hbm_gbs": nbytes / (graph_ms / 1000.0) / 1e9, "frac": nbytes / (graph_ms / 1000.0) / 1e9 / peak,
+            "launches_per_step": layers * 4, "err": err, "ws_errors": codes}
+
+
 def sweep(dev, seed, reps=3):
     """cfg3: the same layer-op at N in {8k .. 128k} and r in {2, 4, 8}, each against the same
     kernel family run dense (r = 1). Attention only, CUDA events, median of `reps` launches
@@ -463,6 +526,8 @@ def run_ours(args, world, rank, local):
         line["sweep"] = sweep(dev, 3000 + rank)
     hk = hbm_kernels(dev, 2000 + rank)
     line["hbm_kernels"] = {"peak_gbs": hbm_peak()[0], "peak_kind": hbm_peak()[1], **hk}
+    if not args.no_sweep:
+        line["decode_step"] = decode_step(dev, 4000 + rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
         dt, tk = cpu_sample(tuple(range(8)))
@@ -497,7 +562,9 @@ def main():
         return
     world, rank, local = dist_setup()
     if args.only_hbm:
-        print(json.dumps(hbm_kernels(torch.device("cuda", local), 2000 + rank)), flush=True)
+        dev = torch.device("cuda", local)
+        print(json.dumps({**hbm_kernels(dev, 2000 + rank), "decode_step": decode_step(dev, 4000 + rank)}),
+              flush=True)
         return
     try:
         run_ours(args, world, rank, local)

@@ -32,13 +32,15 @@ cudaError_t launch_attn_tc(int, bool, const TcParams&, int, cudaStream_t);
 cudaError_t launch_schedule(const int32_t*, const int64_t*, const void*, const int64_t*, int, int, int, int, int,
                             int, int, int, int2*, int32_t*, int, float*, cudaStream_t);
 cudaError_t launch_decode_update(int, int, bool, const void*, const void*, void*, void*, void*, void*, int32_t*,
-                                 int32_t*, int32_t*, int64_t, int64_t, float, int64_t, const int64_t*,
+                                 int32_t*, int32_t*, int64_t, int64_t, const int64_t*, float, int64_t, const int64_t*,
                                  const int64_t*, const int64_t*, const int64_t*, int64_t, int64_t, int64_t, int64_t,
                                  int*, cudaStream_t);
 cudaError_t launch_decode_attn(int, const void*, const int64_t*, const void*, const int64_t*, const void*,
                                const int64_t*, const int32_t*, const int64_t*, const int32_t*, const int64_t*,
                                const void*, const int64_t*, const void*, const int64_t*, void*, const int64_t*,
-                               float, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float*, cudaStream_t);
+                               float, int64_t, const int64_t*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                               float*, cudaStream_t);
+cudaError_t launch_decode_advance(int64_t*, int64_t, cudaStream_t);
 size_t decode_attn_workspace(int64_t, int64_t, int64_t, int64_t, int64_t);
 cudaError_t launch_nm_select(int, const void*, const int64_t*, int32_t*, const int64_t*, int64_t, int64_t, int64_t,
                              int64_t, int, int, int64_t, cudaStream_t);
@@ -385,7 +387,7 @@ int dab_decode_update(const void* new_k, const void* new_v, void* k_exact, void*
   const int bd = block_d < 16 ? 16 : static_cast<int>(block_d);
   return cuda_status(launch_decode_update(dtype, bd, use_cosine != 0, new_k, new_v, k_exact, v_exact, k_packed,
                                           v_packed, packed_counts, packed_ts, packed_lengths, exact_seq_len,
-                                          total_seq_len, threshold, exact_window, new_strides, exact_strides,
+                                          total_seq_len, nullptr, threshold, exact_window, new_strides, exact_strides,
                                           pack_strides, pc_strides, num_heads, head_dim, programs, capacity,
                                           err_word, static_cast<cudaStream_t>(stream)),
                      "decode_update");
@@ -413,10 +415,65 @@ int dab_decode_attention(const void* q, const void* k_packed, const void* v_pack
   const int64_t* s = strides;
   return cuda_status(launch_decode_attn(dtype, q, s + 0, k_packed, s + 3, v_packed, s + 7, packed_counts, s + 11,
                                         packed_lengths, s + 14, k_exact, s + 16, v_exact, s + 20, out, s + 24,
-                                        sm_scale, exact_len, num_kv_groups, batch, num_q_heads / num_kv_groups,
-                                        head_dim, capacity, static_cast<float*>(workspace),
-                                        static_cast<cudaStream_t>(stream)),
+                                        sm_scale, exact_len, nullptr, exact_len, num_kv_groups, batch,
+                                        num_q_heads / num_kv_groups, head_dim, capacity,
+                                        static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)),
                      "decode_attention");
+}
+
+// ---------------------------------------------------- decode with device-resident lengths
+// Same kernels as dab_decode_update / dab_decode_attention; the (exact, total) sequence
+// lengths are read from device memory instead of host arguments, and dab_decode_advance
+// steps them on the device, so a decode step issues no host-side length bookkeeping.
+int dab_decode_update_dev(const void* new_k, const void* new_v, void* k_exact, void* v_exact, void* k_packed,
+                          void* v_packed, int32_t* packed_counts, int32_t* packed_ts, int32_t* packed_lengths,
+                          const int64_t* seq_state, float threshold, int64_t exact_window, int dtype,
+                          const int64_t* new_strides, const int64_t* exact_strides, const int64_t* pack_strides,
+                          const int64_t* pc_strides, int64_t num_heads, int64_t head_dim, int64_t block_d,
+                          int use_cosine, int64_t programs, int64_t capacity, int* err_word, void* stream) {
+  if (!seq_state) return fail(1, "dab_decode_update_dev: null seq_state");
+  if (!new_k || !new_v || !k_exact || !v_exact || !k_packed || !v_packed || !packed_counts || !packed_ts ||
+      !packed_lengths)
+    return fail(1, "dab_decode_update_dev: null pointer");
+  if (block_d < head_dim || block_d > 256 || (block_d & (block_d - 1)))
+    return fail(1, "dab_decode_update_dev: BLOCK_D must be a power of two in [head_dim, 256]");
+  const int bd = block_d < 16 ? 16 : static_cast<int>(block_d);
+  return cuda_status(launch_decode_update(dtype, bd, use_cosine != 0, new_k, new_v, k_exact, v_exact, k_packed,
+                                          v_packed, packed_counts, packed_ts, packed_lengths, 0, 0, seq_state,
+                                          threshold, exact_window, new_strides, exact_strides, pack_strides,
+                                          pc_strides, num_heads, head_dim, programs, capacity, err_word,
+                                          static_cast<cudaStream_t>(stream)),
+                     "decode_update_dev");
+}
+
+int dab_decode_attention_dev(const void* q, const void* k_packed, const void* v_packed,
+                             const int32_t* packed_counts, const int32_t* packed_lengths, const void* k_exact,
+                             const void* v_exact, void* out, int dtype, const int64_t* strides, float sm_scale,
+                             const int64_t* seq_state, int64_t exact_window, int64_t num_kv_groups, int64_t batch,
+                             int64_t num_q_heads, int64_t head_dim, int64_t capacity, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (!seq_state) return fail(1, "dab_decode_attention_dev: null seq_state");
+  if (!q || !k_packed || !v_packed || !packed_counts || !packed_lengths || !k_exact || !v_exact || !out)
+    return fail(1, "dab_decode_attention_dev: null pointer");
+  if (!strides) return fail(1, "dab_decode_attention_dev: null strides");
+  if (exact_window <= 0) return fail(1, "dab_decode_attention_dev: exact_window must be positive");
+  if (num_kv_groups <= 0 || num_q_heads % num_kv_groups) return fail(1, "dab_decode_attention_dev: bad kv groups");
+  if (num_kv_groups > 8) return fail(1, "dab_decode_attention_dev: more than 8 q-heads per kv-head");
+  if (head_dim > 256) return fail(1, "dab_decode_attention_dev: head_dim > 256");
+  const size_t need = decode_attn_workspace(batch, num_q_heads, capacity, exact_window, head_dim);
+  if (!workspace || workspace_bytes < need) return fail(1, "dab_decode_attention_dev: workspace too small");
+  const int64_t* s = strides;
+  return cuda_status(launch_decode_attn(dtype, q, s + 0, k_packed, s + 3, v_packed, s + 7, packed_counts, s + 11,
+                                        packed_lengths, s + 14, k_exact, s + 16, v_exact, s + 20, out, s + 24,
+                                        sm_scale, exact_window, seq_state, exact_window, num_kv_groups, batch,
+                                        num_q_heads / num_kv_groups, head_dim, capacity,
+                                        static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)),
+                     "decode_attention_dev");
+}
+
+int dab_decode_advance(int64_t* seq_state, int64_t count, void* stream) {
+  if (!seq_state && count > 0) return fail(1, "dab_decode_advance: null seq_state");
+  return cuda_status(launch_decode_advance(seq_state, count, static_cast<cudaStream_t>(stream)), "decode_advance");
 }
 
 // ------------------------------------------------------------------------- native pieces

@@ -20,10 +20,14 @@ template <typename T, int BD, bool COS>
 __global__ void __launch_bounds__(128) decode_update_kernel(
     const T* __restrict__ nk, const T* __restrict__ nv, T* __restrict__ ke, T* __restrict__ ve,
     T* __restrict__ kp, T* __restrict__ vp, int32_t* __restrict__ counts, int32_t* __restrict__ ts,
-    int32_t* __restrict__ lengths, int64_t exact_seq_len, int64_t total_seq_len, float thr, int64_t W,
-    int64_t ns_b, int64_t ns_h, int64_t ns_s, int64_t ns_d, int64_t es_b, int64_t es_h, int64_t es_s, int64_t es_d,
-    int64_t ps_b, int64_t ps_h, int64_t ps_s, int64_t ps_d, int64_t cs_b, int64_t cs_h, int64_t cs_s,
-    int64_t num_heads, int64_t head_dim, int64_t programs, int64_t capacity, int* err) {
+    int32_t* __restrict__ lengths, int64_t exact_seq_len, int64_t total_seq_len, const int64_t* __restrict__ st,
+    float thr, int64_t W, int64_t ns_b, int64_t ns_h, int64_t ns_s, int64_t ns_d, int64_t es_b, int64_t es_h,
+    int64_t es_s, int64_t es_d, int64_t ps_b, int64_t ps_h, int64_t ps_s, int64_t ps_d, int64_t cs_b, int64_t cs_h,
+    int64_t cs_s, int64_t num_heads, int64_t head_dim, int64_t programs, int64_t capacity, int* err) {
+  if (st) {  // device-resident (exact, total) sequence state
+    exact_seq_len = st[0];
+    total_seq_len = st[1];
+  }
   constexpr int NH = BD > 128 ? 2 : 1;
   constexpr int PER = BD / 8 / NH;
   const int lane = threadIdx.x & 31;
@@ -126,7 +130,8 @@ __global__ void __launch_bounds__(128) decode_update_kernel(
 
 cudaError_t launch_decode_update(int dtype, int bd, bool cosine, const void* nk, const void* nv, void* ke,
                                  void* ve, void* kp, void* vp, int32_t* counts, int32_t* ts, int32_t* lengths,
-                                 int64_t exact_seq_len, int64_t total_seq_len, float thr, int64_t W,
+                                 int64_t exact_seq_len, int64_t total_seq_len, const int64_t* seq_state, float thr,
+                                 int64_t W,
                                  const int64_t* ns, const int64_t* es, const int64_t* ps, const int64_t* cs,
                                  int64_t num_heads, int64_t head_dim, int64_t programs, int64_t capacity, int* err,
                                  cudaStream_t st) {
@@ -136,7 +141,8 @@ cudaError_t launch_decode_update(int dtype, int bd, bool cosine, const void* nk,
 #define DAB_UPD(TY, N, C)                                                                                     \
   decode_update_kernel<TY, N, C><<<blocks, 128, 0, st>>>(                                                     \
       static_cast<const TY*>(nk), static_cast<const TY*>(nv), static_cast<TY*>(ke), static_cast<TY*>(ve),      \
-      static_cast<TY*>(kp), static_cast<TY*>(vp), counts, ts, lengths, exact_seq_len, total_seq_len, thr, W,   \
+      static_cast<TY*>(kp), static_cast<TY*>(vp), counts, ts, lengths, exact_seq_len, total_seq_len, seq_state, \
+      thr, W,                                                                                                 \
       ns[0], ns[1], ns[2], ns[3], es[0], es[1], es[2], es[3], ps[0], ps[1], ps[2], ps[3], cs[0], cs[1], cs[2], \
       num_heads, head_dim, programs, capacity, err);                                                          \
   return cudaGetLastError();
@@ -173,8 +179,9 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(
     int64_t vps_n, int64_t vps_d, const int32_t* __restrict__ counts, int64_t cs_b, int64_t cs_h, int64_t cs_n,
     const int32_t* __restrict__ lengths, int64_t ls_b, int64_t ls_h, const T* __restrict__ ke, int64_t kes_b,
     int64_t kes_h, int64_t kes_n, int64_t kes_d, const T* __restrict__ ve, int64_t ves_b, int64_t ves_h,
-    int64_t ves_n, int64_t ves_d, float sm_scale, int64_t exact_len, int64_t G, int64_t Hkv, int64_t head_dim,
-    int64_t nchunk, float* __restrict__ part) {
+    int64_t ves_n, int64_t ves_d, float sm_scale, int64_t exact_len, const int64_t* __restrict__ st, int64_t W,
+    int64_t G, int64_t Hkv, int64_t head_dim, int64_t nchunk, float* __restrict__ part) {
+  if (st) exact_len = st[0] < W ? st[0] : W;  // device-resident sequence state
   __shared__ float sq[DEC_GMAX][BD];
   __shared__ float sp[DEC_GMAX][DEC_KC];
   __shared__ float swm[4][DEC_GMAX];
@@ -394,7 +401,8 @@ __global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
     const int32_t* __restrict__ counts, int64_t cs_b, int64_t cs_h, int64_t cs_n, const int32_t* __restrict__ lengths,
     int64_t ls_b, int64_t ls_h, const T* __restrict__ ke, int64_t kes_b, int64_t kes_h, int64_t kes_n,
     const T* __restrict__ ve, int64_t ves_b, int64_t ves_h, int64_t ves_n, float sm_scale, int64_t exact_len,
-    int G, int64_t Hkv, int64_t nchunk, float* __restrict__ part) {
+    const int64_t* __restrict__ st, int64_t W, int G, int64_t Hkv, int64_t nchunk, float* __restrict__ part) {
+  if (st) exact_len = st[0] < W ? st[0] : W;  // device-resident sequence state
   constexpr int ROWB = D * 2;   // bytes per K / V row
   constexpr int SEGS = D / 8;   // 16-byte segments per row
   constexpr int NT = DEC_NW * 32;        // threads
@@ -570,6 +578,21 @@ __global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
   }
 }
 
+// One decode step of device-resident sequence states: (exact, total) += 1 for `count` pairs.
+__global__ void decode_advance_kernel(int64_t* st, int64_t count) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < count) {
+    st[2 * i] += 1;
+    st[2 * i + 1] += 1;
+  }
+}
+
+cudaError_t launch_decode_advance(int64_t* st, int64_t count, cudaStream_t s) {
+  if (count <= 0) return cudaSuccess;
+  decode_advance_kernel<<<static_cast<unsigned>((count + 127) / 128), 128, 0, s>>>(st, count);
+  return cudaGetLastError();
+}
+
 size_t decode_attn_workspace(int64_t B, int64_t Hq, int64_t capacity, int64_t exact_len, int64_t head_dim) {
   int bd = 16;
   while (bd < head_dim) bd <<= 1;
@@ -581,8 +604,10 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
                                const void* vp, const int64_t* vps, const int32_t* counts, const int64_t* cs,
                                const int32_t* lengths, const int64_t* ls, const void* ke, const int64_t* kes,
                                const void* ve, const int64_t* ves, void* out, const int64_t* os, float sm_scale,
-                               int64_t exact_len, int64_t G, int64_t B, int64_t Hkv, int64_t head_dim,
-                               int64_t capacity, float* part, cudaStream_t st) {
+                               int64_t exact_len, const int64_t* seq_state, int64_t W, int64_t G, int64_t B,
+                               int64_t Hkv, int64_t head_dim, int64_t capacity, float* part, cudaStream_t st) {
+  // with a device-resident state the window length is read on the device; `exact_len` is then
+  // its bound (the window size) and sizes the split-K grid
   if (B * Hkv == 0) return cudaSuccess;
   if (G < 1 || G > DEC_GMAX) return cudaErrorInvalidValue;
   {
@@ -616,7 +641,7 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
             static_cast<const TY*>(q), qs[0], qs[1], static_cast<const TY*>(kp), kps[0], kps[1], kps[2],
             static_cast<const TY*>(vp), vps[0], vps[1], vps[2], counts, cs[0], cs[1], cs[2], lengths, ls[0], ls[1],
             static_cast<const TY*>(ke), kes[0], kes[1], kes[2], static_cast<const TY*>(ve), ves[0], ves[1], ves[2],
-            sm_scale, exact_len, static_cast<int>(G), Hkv, nc, part);
+            sm_scale, exact_len, seq_state, W, static_cast<int>(G), Hkv, nc, part);
         decode_combine_kernel<TY, DD><<<static_cast<unsigned>(B * Hkv * G), 128, 0, st>>>(
             part, static_cast<TY*>(out), os[0], os[1], os[2], G, Hkv, nc, head_dim);
         return cudaGetLastError();
@@ -638,7 +663,7 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
       static_cast<const TY*>(q), qs[0], qs[1], qs[2], static_cast<const TY*>(kp), kps[0], kps[1], kps[2], kps[3], \
       static_cast<const TY*>(vp), vps[0], vps[1], vps[2], vps[3], counts, cs[0], cs[1], cs[2], lengths, ls[0],  \
       ls[1], static_cast<const TY*>(ke), kes[0], kes[1], kes[2], kes[3], static_cast<const TY*>(ve), ves[0],    \
-      ves[1], ves[2], ves[3], sm_scale, exact_len, G, Hkv, head_dim, nchunk, part);                             \
+      ves[1], ves[2], ves[3], sm_scale, exact_len, seq_state, W, G, Hkv, head_dim, nchunk, part);               \
   decode_combine_kernel<TY, N><<<static_cast<unsigned>(B * Hkv * G), 128, 0, st>>>(                             \
       part, static_cast<TY*>(out), os[0], os[1], os[2], G, Hkv, nchunk, head_dim);                              \
   return cudaGetLastError();

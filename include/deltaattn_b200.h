@@ -155,6 +155,28 @@ int dab_decode_attention(const void* q, const void* k_packed, const void* v_pack
                          int64_t num_kv_groups, int64_t batch, int64_t num_q_heads, int64_t head_dim,
                          int64_t capacity, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode with device-resident sequence lengths (native; the reference keeps them on the host,
+ * deltaDecoding.py:216-221). seq_state points to int64 {exact_seq_len, total_seq_len} in
+ * device memory, the values dab_decode_update / dab_decode_attention take as host arguments.
+ * dab_decode_update_dev is dab_decode_update reading them there; dab_decode_attention_dev is
+ * dab_decode_attention with exact_len = min(seq_state[0], exact_window) read on the device
+ * (the workspace is sized with exact_len = exact_window); dab_decode_advance adds 1 to both
+ * lengths of `count` consecutive states. One decode step is update, advance, attention, the
+ * order of modeling_llama.py's update, length increment and attention. */
+int dab_decode_update_dev(const void* new_k, const void* new_v, void* k_exact, void* v_exact, void* k_packed,
+                          void* v_packed, int32_t* packed_counts, int32_t* packed_ts, int32_t* packed_lengths,
+                          const int64_t* seq_state, float threshold, int64_t exact_window, int dtype,
+                          const int64_t* new_strides, const int64_t* exact_strides, const int64_t* pack_strides,
+                          const int64_t* pc_strides, int64_t num_heads, int64_t head_dim, int64_t block_d,
+                          int use_cosine, int64_t programs, int64_t capacity, int* err_word, void* stream);
+int dab_decode_attention_dev(const void* q, const void* k_packed, const void* v_packed,
+                             const int32_t* packed_counts, const int32_t* packed_lengths, const void* k_exact,
+                             const void* v_exact, void* out, int dtype, const int64_t* strides, float sm_scale,
+                             const int64_t* seq_state, int64_t exact_window, int64_t num_kv_groups, int64_t batch,
+                             int64_t num_q_heads, int64_t head_dim, int64_t capacity, void* workspace,
+                             size_t workspace_bytes, void* stream);
+int dab_decode_advance(int64_t* seq_state, int64_t count, void* stream);
+
 /* apply_rotary_pos_emb for one tensor (modeling_llama.py:180-204): y = x*cos +
  * rotate_half(x)*sin with eager rounding to the tensor dtype after each op. x/y strides
  * (b, h, s, d); cos/sin strides (b, s, d) (b-stride 0 broadcasts). */

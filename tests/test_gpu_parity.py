@@ -452,6 +452,100 @@ def test_decode_attention_16bit_matches_oracle(dt, D, G, B, Hkv):
     _check_ws_clean()
 
 
+def _device_cache_setup(layers, seed):
+    """A prefilled DeviceDecodeCache plus the same state as plain tensors for the host-length
+    launches of the reference API."""
+    from deltaattention_b200.cache import DeviceDecodeCache
+    g = torch.Generator().manual_seed(seed)
+    B, Hkv, G, D, W, N0, cap, thr = 2, 2, 4, 128, 16, 240, 160, 8.0
+    c = DeviceDecodeCache(layers, B, Hkv, D, cap, W, torch.bfloat16, threshold=thr)
+    for layer in range(layers):
+        keys = torch.from_numpy(I.ar1_keys(B, Hkv, N0, D, seed=seed + layer)).bfloat16()
+        vals = (torch.randn((B, Hkv, N0, D), generator=g) * 0.5).bfloat16()
+        keep = O.periodic_keep_mask(B, Hkv, N0 - W, 0.25)
+        _, kp, vp, ts, counts = O.pack_from_keep(keys[:, :, :N0 - W], vals[:, :, :N0 - W], keep)
+        c.load_prefill(layer, kp.cuda(), vp.cuda(), counts.cuda(), ts.cuda(), keys[:, :, N0 - W:].cuda(),
+                       vals[:, :, N0 - W:].cuda(), N0)
+    host = dict(k_packed=c.k_packed.clone(), v_packed=c.v_packed.clone(), counts=c.packed_counts.clone(),
+                ts=c.packed_timestamps.clone(), lens=c.packed_lengths.clone(), k_exact=c.k_exact.clone(),
+                v_exact=c.v_exact.clone(), exact=[W] * layers, total=[N0] * layers)
+    steps = []
+    for _ in range(24):
+        steps.append(((torch.randn((layers, B, Hkv * G, D), generator=g) * 0.5).bfloat16().cuda(),
+                      (torch.randn((layers, B, Hkv, 1, D), generator=g) * 0.5).bfloat16().cuda(),
+                      (torch.randn((layers, B, Hkv, 1, D), generator=g) * 0.5).bfloat16().cuda()))
+    return c, host, steps, dict(B=B, Hkv=Hkv, G=G, D=D, W=W, thr=thr)
+
+
+def _host_length_step(host, layer, q, k_new, v_new, p):
+    """One decode step through the reference-API kernels with host lengths (deltaDecoding.py)."""
+    import deltaDecoding as dd
+    B, Hkv, G, D, W = p["B"], p["Hkv"], p["G"], p["D"], p["W"]
+    ke, ve, kp, vp = host["k_exact"][layer], host["v_exact"][layer], host["k_packed"][layer], host["v_packed"][layer]
+    cnt, tss, lens = host["counts"][layer], host["ts"][layer], host["lens"][layer]
+    dd.fused_hybrid_decode_update_kernel[(B * Hkv,)](
+        k_new, v_new, ke, ve, kp, vp, cnt, tss, lens, host["exact"][layer], host["total"][layer], p["thr"] ** 2, W,
+        *k_new.stride(), *ke.stride(), *kp.stride(), *cnt.stride(), Hkv, D, BLOCK_D=D, USE_COSINE=False)
+    host["exact"][layer] += 1
+    host["total"][layer] += 1
+    out = torch.empty_like(q)
+    lv = lens.view(B, Hkv)
+    dd.fused_hybrid_decode_kernel[(B, Hkv * G)](
+        q, kp, vp, cnt, lv, ke, ve, out, *q.stride(), *kp.stride(), *vp.stride(), *cnt.stride(), *lv.stride(),
+        *ke.stride(), *ve.stride(), *out.stride(), D ** -0.5, min(host["exact"][layer], W), G, head_dim=D,
+        BLOCK_M=16, BLOCK_N=128, BLOCK_D=D)
+    return out
+
+
+def test_device_decode_cache_matches_host_lengths():
+    """DeviceDecodeCache (lengths on the device, advanced by a kernel) gives bit-identical
+    outputs and cache contents to the reference-API launches with host lengths, over steps
+    that both merge into and append to the packed history."""
+    layers = 2
+    c, host, steps, p = _device_cache_setup(layers, seed=61)
+    for q, kn, vn in steps:
+        for layer in range(layers):
+            got = c.step(layer, q[layer], kn[layer], vn[layer])
+            want = _host_length_step(host, layer, q[layer], kn[layer], vn[layer], p)
+            assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    torch.cuda.synchronize()
+    assert c.lengths() == [(host["exact"][i], host["total"][i]) for i in range(layers)]
+    assert torch.equal(c.packed_lengths, host["lens"])
+    assert torch.equal(c.packed_counts, host["counts"]) and torch.equal(c.packed_timestamps, host["ts"])
+    assert torch.equal(c.k_packed.view(torch.int16), host["k_packed"].view(torch.int16))
+    assert torch.equal(c.k_exact.view(torch.int16), host["k_exact"].view(torch.int16))
+    grew = c.packed_lengths.max().item() > 40 and c.packed_counts.max().item() > 4
+    assert grew, "the steps should both append anchors and merge into them"
+    assert int(c.err.item()) == 0
+    _check_ws_clean()
+
+
+def test_device_decode_cache_graph_replay():
+    """A decode step over every layer captured once in a CUDA graph and replayed per token
+    equals the eager steps token by token."""
+    layers = 2
+    eager, _, steps, _ = _device_cache_setup(layers, seed=62)
+    graphed, _, _, _ = _device_cache_setup(layers, seed=62)
+    q0, k0, v0 = steps[0]
+    for layer in range(layers):  # one eager step on both (kernel attributes are set outside capture)
+        eager.step(layer, q0[layer], k0[layer], v0[layer])
+        graphed.step(layer, q0[layer], k0[layer], v0[layer])
+    sq, sk, sv = torch.empty_like(q0), torch.empty_like(k0), torch.empty_like(v0)
+    sout = torch.empty_like(q0)
+    graph = graphed.capture_step(sq, sk, sv, sout)
+    for q, kn, vn in steps[1:]:
+        want = torch.stack([eager.step(layer, q[layer], kn[layer], vn[layer]) for layer in range(layers)])
+        sq.copy_(q)
+        sk.copy_(kn)
+        sv.copy_(vn)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(sout.view(torch.int16), want.view(torch.int16))
+    assert eager.lengths() == graphed.lengths()
+    del graph
+    _check_ws_clean()
+
+
 def test_hybrid_cache_end_to_end():
     """HybridCompressedCache: prefill hand-off then decode steps, against the oracle."""
     import types

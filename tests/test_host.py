@@ -55,6 +55,19 @@ def test_host_only_entry_points(lib_path):
     assert lib.dab_pack_from_keep_workspace_size(2, 3, 5000) == 4 * 2 * 3 * 5 * 4
 
 
+def test_device_length_entries_reject_null_state(lib_path):
+    """The device-length decode entries check their state pointer before touching the GPU."""
+    lib = L.load()
+    z = (ctypes.c_int64 * 4)(0, 0, 0, 0)
+    assert lib.dab_decode_advance(None, 1, None) != 0
+    assert b"seq_state" in lib.dab_last_error()
+    assert lib.dab_decode_advance(None, 0, None) == 0  # nothing to advance
+    rc = lib.dab_decode_update_dev(*([None] * 9), None, 0.0, 16, 2, z, z, z, z, 2, 128, 128, 0, 2, 64, None, None)
+    assert rc != 0 and b"seq_state" in lib.dab_last_error()
+    rc = lib.dab_decode_attention_dev(*([None] * 8), 2, z, 1.0, None, 16, 4, 1, 8, 128, 64, None, 0, None)
+    assert rc != 0 and b"seq_state" in lib.dab_last_error()
+
+
 @pytest.mark.parametrize("n,m,r,N", [(2, 4, 4, 2000), (2, 4, 2, 777), (1, 4, 4, 1024), (3, 8, 8, 1500)])
 def test_nm_packed_length_matches_oracle(lib_path, n, m, r, N):
     """dab_nm_num_packed (host arithmetic) equals the oracle's kept count per head."""
