@@ -63,7 +63,8 @@ def hbm_kernels(dev, seed):
     """HBM-bound kernels of the path, each launch timed alone with L2 flushed before it.
 
     Returns {name: {"us": t, "bytes": algorithmic bytes, "gbs": bytes / t, "frac": gbs / peak}}:
-    delta selection (chunked_eval, cfg2 keys), device packing from a keep mask (cfg2 K/V),
+    delta selection (chunked_eval, cfg2 keys), device packing from a keep mask (cfg2 K/V), 2:4 N:M
+    selection (cfg2 keys),
     decode attention (16 sequences, packed lengths U[1024, 8192], window 100, 32 q-heads) and
     the decode cache update (one token per sequence)."""
     from deltaattention_b200 import ops, synth
@@ -100,6 +101,11 @@ def hbm_kernels(dev, seed):
     nbytes = Hkv * N * 4 + kept * D * 2 * 2 * 2 + Hkv * M * 8
     out["pack_from_keep"] = {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / peak,
                              "kept_fraction": kept / (Hkv * N)}
+    # 2:4 N:M selection at r = 4: candidates every 2nd key, so half of K is read; keep mask written
+    from deltaattention_b200.dropin.nmDeltaFlashAttention import nm_keep_mask
+    us = timed(lambda: nm_keep_mask(k_rot, 2, 4, 4))
+    nbytes = Hkv * (N // 2) * D * 2 + Hkv * N * 4
+    out["nm_select"] = {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / peak}
     del k, v, k_rot, keep
     # decode: cfg5-like cache state
     g = torch.Generator(device=dev).manual_seed(seed)
@@ -204,6 +210,110 @@ def decode_step(dev, seed, layers=32, steps=20):
             "eager_ms": eager_ms, "graph_ms": graph_ms, "tokens_per_s": B / (graph_ms / 1000.0),
             "hbm_gbs": nbytes / (graph_ms / 1000.0) / 1e9, "frac": nbytes / (graph_ms / 1000.0) / 1e9 / peak,
             "launches_per_step": layers * 4, "err": err, "ws_errors": codes}
+
+
+def serving(dev, seed, steps=256):
+    """cfg5: batched varlen serving with Llama-3.1-8B layer shapes (one attention layer).
+
+    16 sequences with lengths U[4096, 32768] packed back to back (cu_seqlens) in one
+    projection-layout buffer; q / v ~ N(0, 1), keys AR(1) (config-1 distributions), RoPE
+    theta 5e5, bf16. Prefill, per sequence: RoPE(q, k), 2:4 N:M selection at r = 4, device
+    packing, two-phase attention (dense window 128), hand-off of the packed history and the
+    last 100 keys into a DeviceDecodeCache. Then `steps` decode steps for all 16 sequences
+    (cache update with raw Euclidean threshold 15, length advance, decode attention), new
+    keys continuing each sequence's AR(1) process; the steps are captured in one CUDA graph
+    and replayed. HBM bytes per decode step: every packed K / V row with its count and the
+    window read once (516 B per key)."""
+    from deltaattention_b200 import ops, synth
+    from deltaattention_b200.cache import DeviceDecodeCache
+    from deltaattention_b200.dropin.nmDeltaFlashAttention import nm_delta_flash_attention, nm_num_packed
+    B, Hq, Hkv, D, W, Wd, thr = 16, CFG["Hq"], CFG["Hkv"], CFG["D"], CFG["W"], 100, 15.0
+    gen = torch.Generator().manual_seed(seed)
+    lens = torch.randint(4096, 32769, (B,), generator=gen).tolist()
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    T = cu[-1]
+    q, k, v = synth.layer_inputs(1, Hq, Hkv, T, D, torch.bfloat16, seed=seed, device=dev, qv_scale=1.0,
+                                 key_offset=False)
+    cos, sin = synth.rope_tables(max(lens), D, CFG["theta"], torch.bfloat16, device=dev)
+    o = torch.empty((1, T, Hq, D), dtype=torch.bfloat16, device=dev).transpose(1, 2)
+    cap = max(nm_num_packed(n) for n in lens) + steps + 64
+    cache = DeviceDecodeCache(1, B, Hkv, D, cap, Wd, torch.bfloat16, device=dev, threshold=thr)
+    stream = torch.cuda.current_stream(dev)
+
+    def prefill():
+        for i in range(B):
+            s0, s1 = cu[i], cu[i + 1]
+            qr = ops.rope(q[:, :, s0:s1], cos, sin)
+            kr = ops.rope(k[:, :, s0:s1], cos, sin)
+            vi = v[:, :, s0:s1]
+            _, pk = nm_delta_flash_attention(qr, kr, vi, 2, 4, 4, dense_window=W, out=o[:, :, s0:s1],
+                                             return_packed=True)
+            cache.load_prefill(0, pk.k, pk.v, pk.counts, pk.timestamps, kr[:, :, -Wd:], vi[:, :, -Wd:], s1 - s0,
+                               batch_index=i)
+
+    prefill()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    prefill()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    packed0 = int(cache.packed_lengths.sum().item())
+
+    # decode inputs: q ~ N(0, 1); keys continue each sequence's AR(1) from its last key
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed + 1)
+    qs = torch.randn((steps, B, Hq, D), generator=g, device=dev).to(torch.bfloat16)
+    vs = torch.randn((steps, B, Hkv, 1, D), generator=g, device=dev).to(torch.bfloat16)
+    last = torch.stack([k[0, :, cu[i + 1] - 1].float() for i in range(B)])  # [B, Hkv, D]
+    ks = torch.empty((steps, B, Hkv, 1, D), dtype=torch.bfloat16, device=dev)
+    for t in range(steps):
+        last = 0.95 * last + 0.31 * torch.randn(last.shape, generator=g, device=dev)
+        ks[t, :, :, 0] = last.to(torch.bfloat16)
+    outs = torch.empty_like(qs)
+    names = ("seq_state", "packed_lengths", "packed_counts", "k_exact", "v_exact")
+    snap = {n: getattr(cache, n).clone() for n in names}
+
+    def restore():
+        for n in names:
+            getattr(cache, n).copy_(snap[n])
+
+    for t in range(3):  # eager warm-up (kernel attributes are set outside capture)
+        cache.step(0, qs[t], ks[t], vs[t], outs[t])
+    restore()
+    cache._workspace(Hq)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for t in range(steps):
+            cache.step(0, qs[t], ks[t], vs[t], outs[t])
+    stream.wait_stream(side)
+    graph.replay()
+    torch.cuda.synchronize()
+    restore()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    decode_ms = e0.elapsed_time(e1)
+    err = int(cache.err.item())
+    packed1 = int(cache.packed_lengths.sum().item())
+    del graph
+    keys = steps * (packed0 + packed1) // 2 + steps * B * Hkv * Wd  # mean packed length over the steps
+    nbytes = keys * 516
+    peak, _ = hbm_peak()
+    return {"sequences": B, "lengths": "U[4096, 32768]", "prefill_tokens": T, "prefill_ms": prefill_ms,
+            "prefill_tokens_per_s": T / (prefill_ms / 1000.0), "selection": "2:4 N:M, r=4 (nmDeltaFlashAttention)",
+            "decode_steps": steps, "decode_ms_per_step": decode_ms / steps,
+            "decode_tokens_per_s": B * steps / (decode_ms / 1000.0),
+            "decode_hbm_gbs": nbytes / (decode_ms / 1000.0) / 1e9,
+            "decode_frac": nbytes / (decode_ms / 1000.0) / 1e9 / peak,
+            "anchors_appended": packed1 - packed0, "anchor_slots_updated": steps * B * Hkv, "err": err}
 
 
 def sweep(dev, seed, reps=3):
@@ -528,6 +638,7 @@ def run_ours(args, world, rank, local):
     line["hbm_kernels"] = {"peak_gbs": hbm_peak()[0], "peak_kind": hbm_peak()[1], **hk}
     if not args.no_sweep:
         line["decode_step"] = decode_step(dev, 4000 + rank)
+        line["serving_cfg5"] = serving(dev, 5000 + rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
         dt, tk = cpu_sample(tuple(range(8)))
@@ -563,8 +674,8 @@ def main():
     world, rank, local = dist_setup()
     if args.only_hbm:
         dev = torch.device("cuda", local)
-        print(json.dumps({**hbm_kernels(dev, 2000 + rank), "decode_step": decode_step(dev, 4000 + rank)}),
-              flush=True)
+        print(json.dumps({**hbm_kernels(dev, 2000 + rank), "decode_step": decode_step(dev, 4000 + rank),
+                          "serving_cfg5": serving(dev, 5000 + rank)}), flush=True)
         return
     try:
         run_ours(args, world, rank, local)

@@ -52,19 +52,26 @@ class DeviceDecodeCache:
         self._ws = None
         self._ws_heads = 0
 
-    def load_prefill(self, layer, k_packed, v_packed, counts, timestamps, k_exact, v_exact, total_len):
-        """The prefill hand-off of ``HybridCompressedCache.initialize_from_prefill``."""
+    def load_prefill(self, layer, k_packed, v_packed, counts, timestamps, k_exact, v_exact, total_len,
+                     batch_index=None):
+        """The prefill hand-off of ``HybridCompressedCache.initialize_from_prefill``.
+
+        With ``batch_index`` the tensors hold one sequence ([1, Hkv, ...]) and fill that row of
+        the batch, so sequences of different lengths (a varlen prefill) are loaded one by one.
+        The batch shares the layer's (exact, total) pair, as the reference's cache does; the
+        total only stamps the timestamps of anchors appended during decode."""
         p_len = k_packed.shape[2]
         if p_len > self.capacity:
             raise ValueError(f"DeviceDecodeCache: {p_len} packed anchors exceed the capacity {self.capacity}")
-        self.k_packed[layer, :, :, :p_len] = k_packed
-        self.v_packed[layer, :, :, :p_len] = v_packed
-        self.packed_counts[layer, :, :, :p_len] = counts
-        self.packed_timestamps[layer, :, :, :p_len] = timestamps
-        self.packed_lengths[layer, :] = p_len
+        b = slice(None) if batch_index is None else slice(int(batch_index), int(batch_index) + 1)
+        self.k_packed[layer, b, :, :p_len] = k_packed
+        self.v_packed[layer, b, :, :p_len] = v_packed
+        self.packed_counts[layer, b, :, :p_len] = counts
+        self.packed_timestamps[layer, b, :, :p_len] = timestamps
+        self.packed_lengths[layer].view(self.bsz, self.n_kv_heads)[b] = p_len
         e_len = k_exact.shape[2]
-        self.k_exact[layer, :, :, :e_len] = k_exact
-        self.v_exact[layer, :, :, :e_len] = v_exact
+        self.k_exact[layer, b, :, :e_len] = k_exact
+        self.v_exact[layer, b, :, :e_len] = v_exact
         self.seq_state[layer, 0] = e_len
         self.seq_state[layer, 1] = int(total_len)
 

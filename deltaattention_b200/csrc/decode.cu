@@ -284,10 +284,14 @@ template <typename T, int BD>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __restrict__ part, T* __restrict__ out,
                                                              int64_t os_b, int64_t os_h, int64_t os_d, int64_t G,
                                                              int64_t Hkv, int64_t nchunk, int64_t head_dim) {
-  // four warps take every fourth chunk, so the partials stream in parallel; a shared-memory
-  // step merges the four running sums
-  __shared__ float sm[4], sl[4];
-  __shared__ float sacc[4][BD];
+  // pass 1: every chunk's (max, sum) in parallel, the block maximum, and each chunk's scale
+  // factor in shared memory (0 for chunks past the sequence, whose O was never written);
+  // pass 2: one thread per head-dim column sums the scaled partial O over the chunks, eight
+  // chunks' loads in flight at a time
+  extern __shared__ float cmb[];  // f[nchunk], then l[nchunk]
+  float* sf = cmb;
+  float* sl = cmb + nchunk;
+  __shared__ float red[4];
   const int64_t bh = blockIdx.x;  // (b, q-head)
   const int64_t Hq = Hkv * G;
   const int64_t b = bh / Hq, h = bh % Hq;
@@ -297,38 +301,46 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
   const float* base = part + (bk * nchunk * G + g) * (BD + 2);
   const int64_t cstride = G * (BD + 2);
   float m = -INFINITY;
-  for (int64_t c = warp; c < nchunk; c += 4) m = fmaxf(m, base[c * cstride]);
-  if (lane == 0) sm[warp] = m;
+  for (int64_t c = threadIdx.x; c < nchunk; c += blockDim.x) {
+    const float mc = base[c * cstride];
+    sf[c] = mc;
+    sl[c] = base[c * cstride + 1];
+    m = fmaxf(m, mc);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  if (lane == 0) red[warp] = m;
   __syncthreads();
-  m = fmaxf(fmaxf(sm[0], sm[1]), fmaxf(sm[2], sm[3]));
+  m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
   const float ref = (m == -INFINITY) ? 0.f : m;
   float l = 0.f;
-  float acc[BD / 32 > 0 ? BD / 32 : 1];
-#pragma unroll
-  for (int j = 0; j < (BD / 32 > 0 ? BD / 32 : 1); ++j) acc[j] = 0.f;
-  for (int64_t c = warp; c < nchunk; c += 4) {
-    const float* pc = base + c * cstride;
-    const float mc = pc[0];
-    if (mc == -INFINITY) continue;
-    const float f = expf(mc - ref);
-    l = fmaf(pc[1], f, l);
-#pragma unroll
-    for (int j = 0; j < (BD / 32 > 0 ? BD / 32 : 1); ++j) {
-      const int d = j * 32 + lane;
-      if (d < head_dim) acc[j] = fmaf(pc[2 + d], f, acc[j]);
-    }
+  for (int64_t c = threadIdx.x; c < nchunk; c += blockDim.x) {
+    const float mc = sf[c];
+    const float f = (mc == -INFINITY) ? 0.f : expf(mc - ref);
+    sf[c] = f;
+    l = fmaf(sl[c], f, l);
   }
-  if (lane == 0) sl[warp] = l;
 #pragma unroll
-  for (int j = 0; j < (BD / 32 > 0 ? BD / 32 : 1); ++j) {
-    const int d = j * 32 + lane;
-    if (d < BD) sacc[warp][d] = acc[j];
-  }
+  for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+  __syncthreads();  // every f is in place; red[] is free again
+  if (lane == 0) red[warp] = l;
   __syncthreads();
-  const float lt = (sl[0] + sl[1]) + (sl[2] + sl[3]);
+  const float lt = (red[0] + red[1]) + (red[2] + red[3]);
   for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
-    const float a = (sacc[0][d] + sacc[1][d]) + (sacc[2][d] + sacc[3][d]);
-    out[b * os_b + h * os_h + d * os_d] = from_f32<T>(a / lt);
+    const float* col = base + 2 + d;
+    float acc = 0.f;
+    for (int64_t c0 = 0; c0 < nchunk; c0 += 8) {
+      float v[8], f[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t c = c0 + u;
+        f[u] = c < nchunk ? sf[c] : 0.f;
+        v[u] = f[u] != 0.f ? col[c * cstride] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = fmaf(v[u], f[u], acc);
+    }
+    out[b * os_b + h * os_h + d * os_d] = from_f32<T>(acc / lt);
   }
 }
 
@@ -429,7 +441,8 @@ __global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
     if (tid < G) { pout[tid * (D + 2)] = -INFINITY; pout[tid * (D + 2) + 1] = 0.f; }
     return;
   }
-  // ---- the block's K and V rows into shared memory (one round trip), q and the count biases.
+  // ---- the block's K rows, then its V rows, into shared memory (two commit groups, so QK^T and
+  // the softmax run while V lands), q and the count biases.
   // Thread t always copies 16-byte segment t % SEGS of rows t / SEGS + RPP*i; RPP is a multiple
   // of 8, so the swizzled segment (s ^ (row & 7)) is the same for all of this thread's rows.
   {
@@ -444,10 +457,11 @@ __global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
       const T* ks = kb + (k0 + r0) * kps_n;
       const T* vs = vb + (k0 + r0) * vps_n;
 #pragma unroll 8
-      for (int i = 0; i < DEC_VKC / RPP; ++i) {
-        cp_async16_zfill(kd + i * RPP * ROWB, ks + i * RPP * kps_n, true);
-        cp_async16_zfill(vd + i * RPP * ROWB, vs + i * RPP * vps_n, true);
-      }
+      for (int i = 0; i < DEC_VKC / RPP; ++i) cp_async16_zfill(kd + i * RPP * ROWB, ks + i * RPP * kps_n, true);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+#pragma unroll 8
+      for (int i = 0; i < DEC_VKC / RPP; ++i) cp_async16_zfill(vd + i * RPP * ROWB, vs + i * RPP * vps_n, true);
+      asm volatile("cp.async.commit_group;" ::: "memory");
     } else {
       // packed tail, exact window, or past the end (zero-filled)
       const T* keb = ke + b * kes_b + hk * kes_h + s * 8;
@@ -455,14 +469,18 @@ __global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
       for (int i = 0; i < DEC_VKC / RPP; ++i) {
         const int64_t key = k0 + r0 + i * RPP;
         const bool ok = key < total;
-        const bool pk = key < plen;
-        const T* ks = !ok ? kb : (pk ? kb + key * kps_n : keb + (key - plen) * kes_n);
-        const T* vs = !ok ? vb : (pk ? vb + key * vps_n : veb + (key - plen) * ves_n);
+        const T* ks = !ok ? kb : (key < plen ? kb + key * kps_n : keb + (key - plen) * kes_n);
         cp_async16_zfill(kd + i * RPP * ROWB, ks, ok);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      for (int i = 0; i < DEC_VKC / RPP; ++i) {
+        const int64_t key = k0 + r0 + i * RPP;
+        const bool ok = key < total;
+        const T* vs = !ok ? vb : (key < plen ? vb + key * vps_n : veb + (key - plen) * ves_n);
         cp_async16_zfill(vd + i * RPP * ROWB, vs, ok);
       }
+      asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
   }
   // q rows 0..G-1 (A-fragment rows 0..7; rows 8..15 are never read, their fragments are 0)
   for (int i = tid; i < 8 * D; i += NT) {
@@ -473,7 +491,7 @@ __global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
     const int64_t key = k0 + tid;
     bias[tid] = (key < plen) ? logf(static_cast<float>(counts[b * cs_b + hk * cs_h + key * cs_n])) : 0.f;
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  asm volatile("cp.async.wait_group 1;" ::: "memory");  // K has landed; V is still in flight
   __syncthreads();
 
   const int g = lane >> 2;        // head row of this thread's accumulator fragments (rows g+8 are padding)
@@ -534,6 +552,7 @@ __global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
   l += __shfl_xor_sync(0xFFFFFFFFu, l, 1);
   l += __shfl_xor_sync(0xFFFFFFFFu, l, 2);
   if ((lane & 3) == 0) swl[warp * 8 + g] = l;
+  asm volatile("cp.async.wait_group 0;" ::: "memory");  // V
   __syncthreads();
   // ---- O = P . V: warp w owns head-dim columns (D / NW) * w .. over all 128 keys, so the
   // warps' outputs need no merge
@@ -642,7 +661,13 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
             static_cast<const TY*>(vp), vps[0], vps[1], vps[2], counts, cs[0], cs[1], cs[2], lengths, ls[0], ls[1],
             static_cast<const TY*>(ke), kes[0], kes[1], kes[2], static_cast<const TY*>(ve), ves[0], ves[1], ves[2],
             sm_scale, exact_len, seq_state, W, static_cast<int>(G), Hkv, nc, part);
-        decode_combine_kernel<TY, DD><<<static_cast<unsigned>(B * Hkv * G), 128, 0, st>>>(
+        const size_t csm = static_cast<size_t>(2 * nc) * sizeof(float);
+        if (csm > 48 * 1024) {
+          ea = cudaFuncSetAttribute(decode_combine_kernel<TY, DD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(csm));
+          if (ea != cudaSuccess) return ea;
+        }
+        decode_combine_kernel<TY, DD><<<static_cast<unsigned>(B * Hkv * G), 128, csm, st>>>(
             part, static_cast<TY*>(out), os[0], os[1], os[2], G, Hkv, nc, head_dim);
         return cudaGetLastError();
       };
@@ -658,13 +683,19 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
   int64_t nchunk = (capacity + exact_len + DEC_KC - 1) / DEC_KC;
   if (nchunk < 1) nchunk = 1;
   dim3 grid(static_cast<unsigned>(nchunk), static_cast<unsigned>(B * Hkv));
+  const size_t csm = static_cast<size_t>(2 * nchunk) * sizeof(float);
 #define DAB_DEC(TY, N)                                                                                          \
+  if (csm > 48 * 1024) {                                                                                        \
+    cudaError_t ea = cudaFuncSetAttribute(decode_combine_kernel<TY, N>,                                         \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(csm));  \
+    if (ea != cudaSuccess) return ea;                                                                           \
+  }                                                                                                             \
   decode_attn_kernel<TY, N><<<grid, 128, 0, st>>>(                                                              \
       static_cast<const TY*>(q), qs[0], qs[1], qs[2], static_cast<const TY*>(kp), kps[0], kps[1], kps[2], kps[3], \
       static_cast<const TY*>(vp), vps[0], vps[1], vps[2], vps[3], counts, cs[0], cs[1], cs[2], lengths, ls[0],  \
       ls[1], static_cast<const TY*>(ke), kes[0], kes[1], kes[2], kes[3], static_cast<const TY*>(ve), ves[0],    \
       ves[1], ves[2], ves[3], sm_scale, exact_len, seq_state, W, G, Hkv, head_dim, nchunk, part);               \
-  decode_combine_kernel<TY, N><<<static_cast<unsigned>(B * Hkv * G), 128, 0, st>>>(                             \
+  decode_combine_kernel<TY, N><<<static_cast<unsigned>(B * Hkv * G), 128, csm, st>>>(                           \
       part, static_cast<TY*>(out), os[0], os[1], os[2], G, Hkv, nchunk, head_dim);                              \
   return cudaGetLastError();
 #define DAB_DEC_BD(TY)           \

@@ -9,6 +9,8 @@
 //  * rope: apply_rotary_pos_emb (modeling_llama.py:200-204) with eager rounding.
 //  * periodic_meta / keep-mask packing for the native path (modeling_llama.py:626-685
 //    without the host sync and without repeat_kv).
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace dab {
@@ -134,13 +136,26 @@ __global__ void __launch_bounds__(256) chunked_eval_kernel(
   if (g == 0) ccount[b * cc_b + h * cc_h + chunk * cc_c] = local;
 }
 
-// The same scan with rows staged through shared memory: each 8-lane group keeps a ring of
-// ROWS rows filled by 16-byte cp.async copies (one commit group per row), so the row a step
-// needs was requested ROWS steps earlier and the serial chain is no longer one memory latency
-// per token. Used when the head dimension is the power of two BD with unit stride and rows
-// start on 16-byte boundaries.
-constexpr int CE_ROWS = 16;   // rows in flight per chain
-constexpr int CE_GROUPS = 4;  // chains per block (one warp)
+// The scan with speculative rounds. While no key is kept the anchor stays fixed, so the
+// decisions for the next SPEC_W tokens against it are independent of one another: each
+// round decides SPEC_W candidates at once and the first kept one (found by ballot) becomes
+// the new anchor; the decisions past it are discarded. The serial chain then advances one
+// anchor (or SPEC_W rejected tokens) per round instead of one token per step.
+//
+// One warp owns one chunk (spec_warps chunks per CTA). Lane 4c + q scores candidate c with accumulators 2q and 2q + 1
+// of the reference order (elements g, g + 8, ... for accumulator g): their sum is the first
+// level of the pairwise tree and two shuffles finish it, so every decision is the one
+// delta_decide makes. Rows are staged in a per-warp ring of SPEC_RING rows by 16-byte
+// cp.async copies, one commit group per batch of 8 rows, SPEC_LA batches beyond the last
+// row a round reads; the anchor is held in registers, so rows behind the scan position are
+// free to be overwritten.
+constexpr int SPEC_W = 8;       // candidates per round (4 lanes each)
+constexpr int SPEC_RING = 64;   // rows in the ring
+constexpr int SPEC_LA = 5;      // batches requested beyond the one a round reads (<= ring batches - 2)
+// chains per CTA, one per warp (one per SM sub-partition); two when rows are wider than 512 B so
+// that the rings fit in shared memory
+template <typename T, int BD>
+constexpr int spec_warps() { return BD * static_cast<int>(sizeof(T)) <= 512 ? 4 : 2; }
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
@@ -149,80 +164,203 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// elements e and e + 1 of a staged row (e even), one shared-memory load
+template <typename T>
+__device__ __forceinline__ float2 load_pair(const uint8_t* row, int e) {
+  if constexpr (sizeof(T) == 4) {
+    return *reinterpret_cast<const float2*>(row + e * 4);
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(row + e * 2);
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+  } else {
+    return __half22float2(*reinterpret_cast<const __half2*>(row + e * 2));
+  }
+}
+
+__device__ __forceinline__ float2 fneg2(float2 v) { return make_float2(-v.x, -v.y); }
+
+// levels 2 and 3 of the pairwise tree across the four lanes of a candidate (level 1 is the
+// lane's own pair sum)
+__device__ __forceinline__ float spec_tree(float v) {
+  v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+  v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
+  return v;
+}
+
+// One candidate row against the anchor. Euclid: `aw` holds the anchor's 16-bit pairs as raw
+// words, or (fp32) `an` the NEGATED anchor pairs. Cosine: `an` holds the anchor and `rr` its
+// finished squared norm, which depends on the anchor alone.
+// 16-bit Euclid: round(x - a) and round(d * d) as one packed 16-bit sub / mul. Both equal
+// the fp32 operation followed by rounding to T: d * d is exact in fp32, and x - a is either
+// exact in fp32 or (exponents more than 15 / 12 apart for bf16 / fp16) so close to x that
+// neither rounding moves it off x's nearest value.
+template <typename T>
+struct Packed16;
+template <>
+struct Packed16<__nv_bfloat16> {
+  using T2 = __nv_bfloat162;
+  static __device__ __forceinline__ float2 sq_diff(uint32_t x, uint32_t a) {
+    const T2 d = __hsub2(*reinterpret_cast<const T2*>(&x), *reinterpret_cast<const T2*>(&a));
+    return __bfloat1622float2(__hmul2(d, d));
+  }
+};
+template <>
+struct Packed16<__half> {
+  using T2 = __half2;
+  static __device__ __forceinline__ float2 sq_diff(uint32_t x, uint32_t a) {
+    const T2 d = __hsub2(*reinterpret_cast<const T2*>(&x), *reinterpret_cast<const T2*>(&a));
+    return __half22float2(__hmul2(d, d));
+  }
+};
+
 template <typename T, int BD, bool COS>
-__global__ void __launch_bounds__(CE_GROUPS * 8) chunked_eval_staged_kernel(
+__device__ __forceinline__ bool spec_decide(const uint8_t* row, const float2 (&an)[BD > 128 ? 2 : 1][BD / 8 / (BD > 128 ? 2 : 1)],
+                                            const uint32_t (&aw)[BD > 128 ? 2 : 1][BD / 8 / (BD > 128 ? 2 : 1)],
+                                            float rr, int q, float thr) {
+  constexpr int NH = BD > 128 ? 2 : 1;
+  constexpr int PER = BD / 8 / NH;
+  if constexpr (COS) {
+    float dot = 0.f, cc = 0.f;
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh) {
+      float2 d = make_float2(0.f, 0.f), c = d;
+#pragma unroll
+      for (int m = 0; m < PER; ++m) {
+        const float2 x = load_pair<T>(row, hh * 128 + 2 * q + 8 * m);
+        const float2 pd = fmul2(x, an[hh][m]), pc = fmul2(x, x);
+        d = m ? fadd2(d, pd) : pd;
+        c = m ? fadd2(c, pc) : pc;
+      }
+      const float vd = spec_tree(__fadd_rn(d.x, d.y));
+      const float vc = spec_tree(__fadd_rn(c.x, c.y));
+      dot = hh ? __fadd_rn(dot, vd) : vd;
+      cc = hh ? __fadd_rn(cc, vc) : vc;
+    }
+    const float nc = __fsqrt_rn(__fadd_rn(cc, 1e-8f));
+    const float nr = __fsqrt_rn(__fadd_rn(rr, 1e-8f));
+    return __fdiv_rn(dot, __fmul_rn(nc, nr)) < thr;
+  } else {
+    float tot = 0.f;
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh) {
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int m = 0; m < PER; ++m) {
+        const int e = hh * 128 + 2 * q + 8 * m;
+        float2 sq;
+        if constexpr (sizeof(T) == 2) {
+          sq = Packed16<T>::sq_diff(*reinterpret_cast<const uint32_t*>(row + e * 2), aw[hh][m]);
+        } else {  // fp32: x + (-a) is x - a exactly
+          const float2 d = fadd2(load_pair<T>(row, e), an[hh][m]);
+          sq = fmul2(d, d);
+        }
+        acc = m ? fadd2(acc, sq) : sq;
+      }
+      const float v = spec_tree(__fadd_rn(acc.x, acc.y));
+      tot = hh ? __fadd_rn(tot, v) : v;
+    }
+    return round_as<T>(tot) > thr;
+  }
+}
+
+template <typename T, int BD, bool COS>
+__global__ void __launch_bounds__(spec_warps<T, BD>() * 32) delta_scan_spec_kernel(
     const T* __restrict__ x, int64_t xs_b, int64_t xs_h, int64_t xs_s,
     int32_t* __restrict__ keep, int64_t km_b, int64_t km_h, int64_t km_s,
     int32_t* __restrict__ ccount, int64_t cc_b, int64_t cc_h, int64_t cc_c,
-    float thr, int64_t seq_len, int64_t chunk_size, int64_t num_heads, int64_t grid_bh, int64_t grid_chunks) {
+    float thr, int64_t seq_len, int64_t chunk_size, int64_t num_heads, int64_t num_chunks) {
   constexpr int NH = BD > 128 ? 2 : 1;
   constexpr int PER = BD / 8 / NH;
   constexpr int ROWB = BD * static_cast<int>(sizeof(T));  // bytes per row
   constexpr int NCP = ROWB / 16;                           // 16-byte copies per row
-  constexpr int PITCH = ROWB + 16;                         // padded row pitch (bank spread)
-  extern __shared__ __align__(16) uint8_t ce_smem[];
+  constexpr int PITCH = ROWB + 16;                         // padded pitch: rows 4 banks apart
+  extern __shared__ __align__(16) uint8_t spec_smem[];
   const int lane = threadIdx.x & 31;
-  const int g = lane & 7;
-  const int grp = threadIdx.x >> 3;
-  const unsigned gmask = 0xFFu << (lane & 24);
-  uint8_t* ring = ce_smem + grp * (CE_ROWS * PITCH + 16);
-  const int64_t chunk = static_cast<int64_t>(blockIdx.x) * CE_GROUPS + grp;
+  uint8_t* ring = spec_smem + (threadIdx.x >> 5) * (SPEC_RING * PITCH);
+  const int c = lane >> 2;  // candidate of this lane
+  const int q = lane & 3;   // its accumulators: 2q and 2q + 1
+  const int64_t chunk = static_cast<int64_t>(blockIdx.x) * spec_warps<T, BD>() + (threadIdx.x >> 5);
   const int64_t bh = blockIdx.y;
-  if (chunk >= grid_chunks || bh >= grid_bh) return;
   const int64_t b = bh / num_heads, h = bh % num_heads;
   const int64_t start = chunk * chunk_size;
-  if (start >= seq_len) return;
-  const int64_t end = min(start + chunk_size, seq_len);
-  const uint8_t* row0 = reinterpret_cast<const uint8_t*>(x + b * xs_b + h * xs_h);
+  if (chunk >= num_chunks || start >= seq_len) return;  // whole warps leave; no CTA-wide barrier follows
+  const int n = static_cast<int>(min(chunk_size, seq_len - start));
   const int64_t rstride = xs_s * static_cast<int64_t>(sizeof(T));
-  int32_t* krow = keep + b * km_b + h * km_h;
+  const uint8_t* src0 = reinterpret_cast<const uint8_t*>(x + b * xs_b + h * xs_h) + start * rstride;
+  int32_t* krow = keep + b * km_b + h * km_h + start * km_s;
+  const int nbatch = (n + 7) >> 3;
 
-  // request row pos into its ring slot (lane g copies 16-byte pieces g, g + 8, ...); one
-  // commit group per call, empty past the end, so the group count stays uniform
-  auto request = [&](int64_t pos) {
-    if (pos < end) {
-      const uint8_t* src = row0 + pos * rstride;
-      uint8_t* dst = ring + (pos % CE_ROWS) * PITCH;
-#pragma unroll
-      for (int c = g; c < NCP; c += 8) cp_async16(dst + c * 16, src + c * 16);
+  int req = 0;  // next batch to request
+  auto top_up = [&](int need) {  // request through batch need + SPEC_LA (empty groups past the end)
+    for (; req <= need + SPEC_LA; ++req) {
+      if (req < nbatch) {
+        for (int k = lane; k < 8 * NCP; k += 32) {
+          const int r = 8 * req + k / NCP;
+          if (r < n) cp_async16(ring + (r % SPEC_RING) * PITCH + (k % NCP) * 16, src0 + r * rstride + (k % NCP) * 16);
+        }
+      }
+      cp_async_commit();
     }
-    cp_async_commit();
   };
-  auto read = [&](int64_t pos, float (&dst)[NH][PER]) {
-    const T* r = reinterpret_cast<const T*>(ring + (pos % CE_ROWS) * PITCH);
+  float2 an[NH][PER];
+  uint32_t aw[NH][PER];
+  float rr = 0.f;  // cosine: the anchor's squared norm in the reference order
+  auto load_anchor = [&](int r) {
+    const uint8_t* row = ring + (r % SPEC_RING) * PITCH;
 #pragma unroll
-    for (int hh = 0; hh < NH; ++hh)
+    for (int hh = 0; hh < NH; ++hh) {
+      float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int m = 0; m < PER; ++m) dst[hh][m] = to_f32(r[hh * 128 + g + 8 * m]);
+      for (int m = 0; m < PER; ++m) {
+        if constexpr (!COS && sizeof(T) == 2) {
+          aw[hh][m] = *reinterpret_cast<const uint32_t*>(row + (hh * 128 + 2 * q + 8 * m) * 2);
+          continue;
+        }
+        const float2 y = load_pair<T>(row, hh * 128 + 2 * q + 8 * m);
+        if constexpr (COS) {
+          an[hh][m] = y;
+          const float2 pr = fmul2(y, y);
+          acc = m ? fadd2(acc, pr) : pr;
+        } else {
+          an[hh][m] = make_float2(-y.x, -y.y);
+        }
+      }
+      if constexpr (COS) {
+        const float v = spec_tree(__fadd_rn(acc.x, acc.y));
+        rr = hh ? __fadd_rn(rr, v) : v;
+      }
+    }
   };
 
-  for (int k = 0; k < CE_ROWS; ++k) request(start + k);
-  float ref[NH][PER], cur[NH][PER];
-  cp_async_wait<CE_ROWS - 1>();
-  __syncwarp(gmask);
-  read(start, ref);
-  __syncwarp(gmask);
-  request(start + CE_ROWS);
-  if (g == 0) krow[start * km_s] = 1;
-  int local = 1;
-  for (int64_t i = start + 1; i < end; ++i) {
-    cp_async_wait<CE_ROWS - 1>();  // row i has landed (its group is the oldest pending)
-    __syncwarp(gmask);
-    read(i, cur);
-    __syncwarp(gmask);             // every lane has read slot i before it is refilled
-    request(i + CE_ROWS);
-    const bool kp = delta_decide<T, BD, COS>(cur, ref, gmask, thr);
-    if (g == 0) krow[i * km_s] = kp ? 1 : 0;
-    if (kp) {
-#pragma unroll
-      for (int hh = 0; hh < NH; ++hh)
-#pragma unroll
-        for (int m = 0; m < PER; ++m) ref[hh][m] = cur[hh][m];
-      ++local;
+  top_up(0);
+  cp_async_wait<SPEC_LA>();
+  __syncwarp();
+  load_anchor(0);
+  if (lane == 0) krow[0] = 1;
+  int count = 1;
+  int p = 1;  // first undecided row
+  while (p < n) {
+    const int hi = min(p + SPEC_W - 1, n - 1);
+    top_up(hi >> 3);
+    cp_async_wait<SPEC_LA>();  // every batch through hi's has landed
+    __syncwarp();
+    const bool valid = p + c < n;
+    const int r = valid ? p + c : n - 1;
+    const bool kp = spec_decide<T, BD, COS>(ring + (r % SPEC_RING) * PITCH, an, aw, rr, q, thr);
+    const unsigned kb = __ballot_sync(0xFFFFFFFFu, kp && valid) & 0x11111111u;
+    const int first = kb ? (__ffs(kb) - 1) >> 2 : SPEC_W;
+    if (q == 0 && valid && c <= first) krow[static_cast<int64_t>(p + c) * km_s] = c == first ? 1 : 0;
+    if (first < SPEC_W) {
+      ++count;
+      load_anchor(p + first);
+      p += first + 1;
+    } else {
+      p += SPEC_W;
     }
+    __syncwarp();  // every lane is done with the ring before the next top-up refills it
   }
   cp_async_wait<0>();
-  if (g == 0) ccount[b * cc_b + h * cc_h + chunk * cc_c] = local;
+  if (lane == 0) ccount[b * cc_b + h * cc_h + chunk * cc_c] = count;
 }
 
 template <typename T, int BD, bool COS>
@@ -235,16 +373,17 @@ static cudaError_t launch_chunked_eval_t(const void* x, const int64_t* xs, int32
                       (xs[1] * static_cast<int64_t>(sizeof(T))) % 16 == 0 &&
                       (xs[2] * static_cast<int64_t>(sizeof(T))) % 16 == 0 && BD * sizeof(T) >= 128;
   if (staged) {
-    const int smem = CE_GROUPS * (CE_ROWS * (BD * static_cast<int>(sizeof(T)) + 16) + 16);
-    auto kfn = chunked_eval_staged_kernel<T, BD, COS>;
+    constexpr int WPC = spec_warps<T, BD>();
+    const int smem = WPC * SPEC_RING * (BD * static_cast<int>(sizeof(T)) + 16);
+    auto kfn = delta_scan_spec_kernel<T, BD, COS>;
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return e;
     }
-    dim3 g2(static_cast<unsigned>((grid_chunks + CE_GROUPS - 1) / CE_GROUPS), static_cast<unsigned>(grid_bh));
-    kfn<<<g2, CE_GROUPS * 8, smem, st>>>(static_cast<const T*>(x), xs[0], xs[1], xs[2], keep, km[0], km[1], km[2], cc,
-                                         ccs[0], ccs[1], ccs[2], thr, seq_len, chunk_size, num_heads, grid_bh,
-                                         grid_chunks);
+    dim3 g2(static_cast<unsigned>((grid_chunks + WPC - 1) / WPC), static_cast<unsigned>(grid_bh));
+    kfn<<<g2, WPC * 32, smem, st>>>(static_cast<const T*>(x), xs[0], xs[1], xs[2], keep, km[0], km[1], km[2],
+                                           cc, ccs[0], ccs[1], ccs[2], thr, seq_len, chunk_size, num_heads,
+                                           grid_chunks);
     return cudaGetLastError();
   }
   const int groups_per_block = 8;  // 64 threads
@@ -806,6 +945,95 @@ __global__ void __launch_bounds__(128) nm_select_kernel(const T* __restrict__ x,
   }
 }
 
+// The same selection with candidate rows staged in shared memory. A CTA scores the candidates
+// of NM_CAND_MAX / m whole groups of one (batch, head): their rows and the row of the candidate
+// before them arrive by coalesced 16-byte cp.async copies, four lanes score each candidate (lane q holds
+// accumulators 2q and 2q + 1 of the eight strided fp32 accumulators; their sum is the first
+// level of the pairwise tree, two shuffles finish it), then one thread per group ranks it and
+// the keep mask of every position the groups cover is written by consecutive threads. Used
+// when the head dimension is the power of two BD with unit stride and rows start on 16-byte
+// boundaries; the scores are the ones nm_select_kernel computes.
+constexpr int NM_CAND_MAX = 64;  // candidates per CTA (whole groups)
+
+template <typename T, int BD>
+__global__ void __launch_bounds__(128) nm_select_staged_kernel(const T* __restrict__ x, int64_t xb, int64_t xh,
+                                                               int64_t xs, int32_t* __restrict__ keep, int64_t kb,
+                                                               int64_t kh, int64_t ks, int64_t H, int64_t N,
+                                                               int n_keep, int m_group, int64_t c, int64_t groups) {
+  constexpr int NH = BD > 128 ? 2 : 1;
+  constexpr int PER = BD / 8 / NH;
+  constexpr int ROWB = BD * static_cast<int>(sizeof(T));
+  constexpr int NCP = ROWB / 16;
+  constexpr int PITCH = ROWB + 16;
+  extern __shared__ __align__(16) uint8_t nm_smem[];
+  float* sc = reinterpret_cast<float*>(nm_smem);                 // scores of this CTA's candidates
+  uint8_t* rows = nm_smem + NM_CAND_MAX * sizeof(float);         // row r holds candidate i0 - 1 + r
+  const int gpc = NM_CAND_MAX / m_group;                         // groups per CTA
+  const int64_t g0 = static_cast<int64_t>(blockIdx.x) * gpc;
+  const int64_t bh = blockIdx.y;
+  if (g0 >= groups) return;
+  const int64_t b = bh / H, h = bh % H;
+  const int64_t G = (N + c - 1) / c;  // candidates of the head
+  const int64_t i0 = g0 * m_group;
+  const int cn = static_cast<int>(min(static_cast<int64_t>(gpc) * m_group, G - i0));  // candidates here
+  const uint8_t* base = reinterpret_cast<const uint8_t*>(x + b * xb + h * xh);
+  const int64_t cstride = c * xs * static_cast<int64_t>(sizeof(T));  // bytes between candidates
+  // stage candidates i0 - 1 .. i0 + cn - 1 (row 0 stays unused when i0 == 0); every copy in
+  // flight at once
+  for (int j = threadIdx.x; j < (cn + 1) * NCP; j += blockDim.x) {
+    const int r = j / NCP, k = j % NCP;
+    const int64_t i = i0 - 1 + r;
+    if (i >= 0) cp_async16(rows + r * PITCH + k * 16, base + i * cstride + k * 16);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  const int q = threadIdx.x & 3;
+  for (int a = threadIdx.x >> 2; a < ((cn + 7) & ~7); a += blockDim.x >> 2) {  // whole warps iterate together
+    const int ra = a < cn ? a : cn - 1;
+    const uint8_t* r1 = rows + (ra + 1) * PITCH;
+    const uint8_t* r0 = rows + ra * PITCH;
+    float tot = 0.f;
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh) {
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int m = 0; m < PER; ++m) {
+        const int e = hh * 128 + 2 * q + 8 * m;
+        const float2 d = fadd2(load_pair<T>(r1, e), fneg2(load_pair<T>(r0, e)));
+        const float2 sq = fmul2(d, d);
+        acc = m ? fadd2(acc, sq) : sq;
+      }
+      const float t = spec_tree(__fadd_rn(acc.x, acc.y));
+      tot = hh ? __fadd_rn(tot, t) : t;
+    }
+    if (q == 0 && a < cn) sc[a] = (i0 + a == 0) ? INFINITY : tot;
+  }
+  __syncthreads();
+  // rank each group (one thread per group); the keep bits go to the row area, no longer read
+  int32_t* kept = reinterpret_cast<int32_t*>(rows);
+  const int ng = (cn + m_group - 1) / m_group;
+  for (int gi = threadIdx.x; gi < ng; gi += blockDim.x) {
+    const int a0 = gi * m_group;
+    const int size = min(m_group, cn - a0);
+    const int nk = min(n_keep, size);
+    for (int a = 0; a < size; ++a) {
+      int rank = 0;
+      for (int o = 0; o < size; ++o)
+        rank += (sc[a0 + o] > sc[a0 + a]) || (sc[a0 + o] == sc[a0 + a] && o < a);
+      kept[a0 + a] = rank < nk ? 1 : 0;
+    }
+  }
+  __syncthreads();
+  int32_t* kr = keep + b * kb + h * kh;
+  const int64_t p0 = i0 * c;
+  const int64_t p1 = min((i0 + cn) * c, N);
+  for (int64_t p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+    const int64_t off = p - p0;
+    kr[p * ks] = (off % c == 0) ? kept[off / c] : 0;
+  }
+}
+
 cudaError_t launch_nm_select(int dtype, const void* x, const int64_t* xs, int32_t* keep, const int64_t* kms,
                              int64_t B, int64_t H, int64_t N, int64_t D, int n_keep, int m_group, int64_t c,
                              cudaStream_t st) {
@@ -816,8 +1044,25 @@ cudaError_t launch_nm_select(int dtype, const void* x, const int64_t* xs, int32_
   if (bd > 256) return cudaErrorInvalidValue;
   const int64_t G = (N + c - 1) / c;
   const int64_t groups = (G + m_group - 1) / m_group;
+  if (B * H > 65535) return cudaErrorInvalidValue;
+  const int esz = dtype == F32 ? 4 : 2;
+  const bool staged = D == bd && xs[3] == 1 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                      (xs[0] * esz) % 16 == 0 && (xs[1] * esz) % 16 == 0 && (xs[2] * esz) % 16 == 0;
   dim3 grid(static_cast<unsigned>((groups + 127) / 128), static_cast<unsigned>(B * H));
+  const int gpc = NM_CAND_MAX / m_group;
+  dim3 sgrid(static_cast<unsigned>((groups + gpc - 1) / gpc), static_cast<unsigned>(B * H));
+  const int smem = NM_CAND_MAX * 4 + (NM_CAND_MAX + 1) * (bd * esz + 16);
 #define DAB_NM(TY, BDV)                                                                                      \
+  if (staged) {                                                                                              \
+    auto kfn = nm_select_staged_kernel<TY, BDV>;                                                             \
+    if (smem > 48 * 1024) {                                                                                  \
+      cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);          \
+      if (e != cudaSuccess) return e;                                                                        \
+    }                                                                                                        \
+    kfn<<<sgrid, 128, smem, st>>>(static_cast<const TY*>(x), xs[0], xs[1], xs[2], keep, kms[0], kms[1],     \
+                                  kms[2], H, N, n_keep, m_group, c, groups);                                 \
+    return cudaGetLastError();                                                                               \
+  }                                                                                                          \
   nm_select_kernel<TY, BDV><<<grid, 128, 0, st>>>(static_cast<const TY*>(x), xs[0], xs[1], xs[2], xs[3], keep, \
                                                   kms[0], kms[1], kms[2], H, N, D, n_keep, m_group, c, groups); \
   return cudaGetLastError();

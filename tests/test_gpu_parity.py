@@ -112,6 +112,59 @@ def test_chunked_eval_euclid_matches_oracle(dt):
     np.testing.assert_array_equal(cc.cpu().numpy(), ref_cc.numpy())
 
 
+SCAN = [  # dtype, head_dim, chunk, cosine: row widths 128 B to 1 KiB, ragged and tiny chunks
+    (torch.bfloat16, 256, 300, False), (torch.bfloat16, 64, 512, False), (torch.float16, 128, 13, False),
+    (torch.float32, 32, 77, True), (torch.bfloat16, 128, 512, True), (torch.float32, 256, 100, False),
+]
+
+
+@pytest.mark.parametrize("level", range(4))
+@pytest.mark.parametrize("dt,D,chunk,use_cos", SCAN)
+def test_delta_scan_keep_rates_match_oracle(dt, D, chunk, use_cos, level):
+    """The delta scan from almost every key kept (level 0) to almost none (level 3), on ragged
+    chunks and row widths from 128 to 1024 bytes: keep mask and chunk counts equal the oracle's."""
+    import tritonModules as tm
+    B, H, N = 1, 3, 1000
+    k = I.post_rope_keys(B, H, N, D, 5e5, dt, seed=91, offset=True)
+    kk = k.float().numpy()
+    a, b = kk[:, :, 1:], kk[:, :, :-1]
+    if use_cos:
+        c = (a * b).sum(-1) / (np.linalg.norm(a, axis=-1) * np.linalg.norm(b, axis=-1) + 1e-8)
+        lo = float(np.quantile(c, 0.03))
+        thr = [float(np.quantile(c, 0.97)), lo, lo - 0.3, lo - 0.8][level]
+    else:
+        d = ((a - b) ** 2).sum(-1)
+        hi = float(np.quantile(d, 0.97))
+        thr = [float(np.quantile(d, 0.03)), hi, 4 * hi, 16 * hi][level]
+    nch = -(-N // chunk)
+    ref_keep, ref_cc = O.delta_keep_mask(k, thr, use_cos, chunk, nch)
+    kc = k.cuda()
+    keep = torch.zeros((B, H, N), dtype=torch.int32, device="cuda")
+    cc = torch.zeros((B, H, nch), dtype=torch.int32, device="cuda")
+    tm.chunked_eval_kernel[(B * H, nch)](kc, keep, cc, thr, *kc.stride(), *keep.stride(), *cc.stride(), N, D, chunk,
+                                         num_heads=H, BLOCK_D=D, USE_COSINE=use_cos)
+    np.testing.assert_array_equal(keep.cpu().numpy(), ref_keep.numpy())
+    np.testing.assert_array_equal(cc.cpu().numpy(), ref_cc.numpy())
+
+
+@pytest.mark.parametrize("similarity,threshold", [("euclidean", 11.0), ("cosine", 0.9)])
+def test_delta_scan_full_size_matches_oracle(similarity, threshold):
+    """cfg2 keys at full size (8 kv-heads x 32k tokens in the projection layout, chunk 512,
+    bf16; the bench's keys and Euclidean threshold, which keep about 1 key in 4): keep mask
+    and chunk counts equal the oracle's on the same post-RoPE keys, token for token."""
+    from deltaattention_b200 import ops, synth
+    dev = torch.device("cuda")
+    _, k, _ = synth.layer_inputs(1, 8, 8, 32768, 128, torch.bfloat16, seed=2000, device=dev)
+    cos, sin = synth.rope_tables(32768, 128, 5e5, torch.bfloat16, device=dev)
+    k_rot = ops.rope(k, cos, sin)
+    keep, cc = ops.delta_keep_mask(k_rot, threshold, similarity, 512)
+    use_cos = similarity == "cosine"
+    ref_keep, ref_cc = O.delta_keep_mask(k_rot.cpu(), threshold if use_cos else threshold ** 2, use_cos, 512, 64)
+    bad = (keep.cpu() != ref_keep).nonzero().tolist()
+    assert not bad, f"{len(bad)} decisions differ, first at (b, h, t) = {bad[:4]}"
+    np.testing.assert_array_equal(cc.cpu().numpy(), ref_cc.numpy())
+
+
 def test_scatter_pack_matches_reference(golden):
     import tritonModules as tm
     g = golden("pack_fp32")
@@ -183,6 +236,27 @@ def test_nm_select_matches_oracle():
         got = nm.nm_keep_mask(k.cuda(), n, m, r)
         np.testing.assert_array_equal(got.cpu().numpy(), ref.numpy())
         assert int(got[0, 0].sum()) == nm.nm_num_packed(N, n, m, r)
+
+
+NM_CASES = [  # dtype, head_dim, n, m, ratio, N, layout
+    (torch.float32, 64, 2, 4, 4, 1999, "bhsd"), (torch.float16, 256, 2, 4, 4, 1500, "bhsd"),
+    (torch.bfloat16, 128, 2, 4, 4, 3001, "bshd"), (torch.bfloat16, 96, 2, 4, 4, 1000, "bhsd"),
+    (torch.bfloat16, 128, 1, 3, 3, 2000, "bhsd"), (torch.float16, 64, 8, 16, 4, 4099, "bshd"),
+    (torch.bfloat16, 16, 2, 4, 8, 777, "bhsd"),
+]
+
+
+@pytest.mark.parametrize("dt,D,n,m,r,N,layout", NM_CASES)
+def test_nm_select_layouts_match_oracle(dt, D, n, m, r, N, layout):
+    """N:M selection over dtypes, head dims 16-256 (96 takes the unstaged kernel), group sizes
+    that do not divide a CTA's candidate count, ragged tails and the projection layout."""
+    from deltaattention_b200.dropin import nmDeltaFlashAttention as nm
+    k = I.post_rope_keys(2, 3, N, D, 5e5, dt, seed=N + D)
+    ref = O.nm_keep_mask(k, n, m, r)
+    kc = k.cuda() if layout == "bhsd" else k.transpose(1, 2).contiguous().cuda().transpose(1, 2)
+    got = nm.nm_keep_mask(kc, n, m, r)
+    np.testing.assert_array_equal(got.cpu().numpy(), ref.numpy())
+    assert (got.sum(-1) == nm.nm_num_packed(N, n, m, r)).all()
 
 
 # ------------------------------------------------------------------ attention
