@@ -346,9 +346,11 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
 
 // Tensor-core split-K decode for 16-bit types with unit head-dim strides and 16-byte rows.
 // A CTA (DEC_NW = 8 warps) takes 128 keys of one (batch, kv-head) for all G (<= 8) q-heads:
-//   * every thread copies 16-byte row segments of the block's K and V rows into shared memory
-//     with cp.async (one memory round trip per CTA; rows past the end are zero-filled), with
-//     the segment index XOR-swizzled by the row so that ldmatrix reads are conflict-free;
+//   * every thread copies 16-byte row segments of the block's K rows into shared memory with
+//     cp.async (rows past the end are zero-filled), with the segment index XOR-swizzled by the
+//     row so that ldmatrix reads are conflict-free; the V rows follow into the same buffer as
+//     soon as every warp has read K, and land while the softmax runs (one 32 KB buffer instead
+//     of two, so five CTAs share an SM);
 //   * warp w scores keys 16w..16w+15 with mma.sync m16n8k16 (A = the q-heads padded to 16 rows,
 //     B = K rows via ldmatrix);
 //   * the chunk's row maximum per head goes through shared memory, and P = exp(s - max), cast
@@ -401,13 +403,15 @@ __device__ __forceinline__ uint32_t pack_t2(float lo, float hi) {
 
 constexpr int DEC_NW = 8;  // warps per CTA: 16 keys each
 constexpr int DEC_PROW = DEC_VKC + 8;  // padded P row (elements): conflict-free A-fragment loads
+// K and V share one row buffer (V is copied in once every warp has read K), so five CTAs fit
+// on an SM
 template <int D>
 constexpr int decode_mma_smem() {
-  return 256 * D * 2 + 8 * D * 2 + 128 * 4 + 2 * DEC_NW * 8 * 4 + 8 * DEC_PROW * 2;
+  return 128 * D * 2 + 8 * D * 2 + 128 * 4 + 2 * DEC_NW * 8 * 4 + 8 * DEC_PROW * 2;
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
+__global__ void __launch_bounds__(DEC_NW * 32, 5) decode_attn_mma_kernel(
     const T* __restrict__ q, int64_t qs_b, int64_t qs_h, const T* __restrict__ kp, int64_t kps_b, int64_t kps_h,
     int64_t kps_n, const T* __restrict__ vp, int64_t vps_b, int64_t vps_h, int64_t vps_n,
     const int32_t* __restrict__ counts, int64_t cs_b, int64_t cs_h, int64_t cs_n, const int32_t* __restrict__ lengths,
@@ -422,8 +426,8 @@ __global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
   constexpr int NTW = KPW / 8;           // QK n-tiles per warp
   extern __shared__ __align__(128) uint8_t dsm[];
   uint8_t* Ks = dsm;                                          // [128][D], swizzled segments
-  uint8_t* Vs = dsm + DEC_VKC * ROWB;                         // [128][D], swizzled segments
-  T* qsm = reinterpret_cast<T*>(dsm + 2 * DEC_VKC * ROWB);    // [8][D], rows >= G zero
+  uint8_t* Vs = dsm;                                          // V over K once K has been read
+  T* qsm = reinterpret_cast<T*>(dsm + DEC_VKC * ROWB);        // [8][D], rows >= G zero
   float* bias = reinterpret_cast<float*>(qsm + 8 * D);        // [128] log(count) of packed keys
   float* swm = bias + DEC_VKC;                                // [NW][8] per-warp max
   float* swl = swm + DEC_NW * 8;                              // [NW][8] per-warp sum
@@ -441,47 +445,30 @@ __global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
     if (tid < G) { pout[tid * (D + 2)] = -INFINITY; pout[tid * (D + 2) + 1] = 0.f; }
     return;
   }
-  // ---- the block's K rows, then its V rows, into shared memory (two commit groups, so QK^T and
-  // the softmax run while V lands), q and the count biases.
+  // ---- the block's K rows into shared memory (V follows into the same buffer once every warp
+  // has read K), q and the count biases.
   // Thread t always copies 16-byte segment t % SEGS of rows t / SEGS + RPP*i; RPP is a multiple
   // of 8, so the swizzled segment (s ^ (row & 7)) is the same for all of this thread's rows.
-  {
-    constexpr int RPP = NT / SEGS;
-    const int s = tid % SEGS, r0 = tid / SEGS;
-    const uint32_t soff = static_cast<uint32_t>(r0 * ROWB + ((s ^ (r0 & 7)) << 4));
-    const uint32_t kd = smem_u32(Ks) + soff, vd = smem_u32(Vs) + soff;
-    const T* kb = kp + b * kps_b + hk * kps_h + s * 8;
-    const T* vb = vp + b * vps_b + hk * vps_h + s * 8;
+  constexpr int RPP = NT / SEGS;
+  const int cs_seg = tid % SEGS, r0 = tid / SEGS;
+  const uint32_t rows_dst = smem_u32(Ks) + static_cast<uint32_t>(r0 * ROWB + ((cs_seg ^ (r0 & 7)) << 4));
+  // rows k0 + r0 + RPP*i of the packed history (stride pn) continued by the exact window (stride en)
+  auto issue_rows = [&](const T* pb, int64_t pn, const T* eb, int64_t en) {
     if (k0 + DEC_VKC <= plen) {
-      // whole block in the packed history: fixed strides
-      const T* ks = kb + (k0 + r0) * kps_n;
-      const T* vs = vb + (k0 + r0) * vps_n;
+      const T* src = pb + (k0 + r0) * pn;
 #pragma unroll 8
-      for (int i = 0; i < DEC_VKC / RPP; ++i) cp_async16_zfill(kd + i * RPP * ROWB, ks + i * RPP * kps_n, true);
-      asm volatile("cp.async.commit_group;" ::: "memory");
-#pragma unroll 8
-      for (int i = 0; i < DEC_VKC / RPP; ++i) cp_async16_zfill(vd + i * RPP * ROWB, vs + i * RPP * vps_n, true);
-      asm volatile("cp.async.commit_group;" ::: "memory");
+      for (int i = 0; i < DEC_VKC / RPP; ++i) cp_async16_zfill(rows_dst + i * RPP * ROWB, src + i * RPP * pn, true);
     } else {
-      // packed tail, exact window, or past the end (zero-filled)
-      const T* keb = ke + b * kes_b + hk * kes_h + s * 8;
-      const T* veb = ve + b * ves_b + hk * ves_h + s * 8;
       for (int i = 0; i < DEC_VKC / RPP; ++i) {
         const int64_t key = k0 + r0 + i * RPP;
         const bool ok = key < total;
-        const T* ks = !ok ? kb : (key < plen ? kb + key * kps_n : keb + (key - plen) * kes_n);
-        cp_async16_zfill(kd + i * RPP * ROWB, ks, ok);
+        const T* src = !ok ? pb : (key < plen ? pb + key * pn : eb + (key - plen) * en);
+        cp_async16_zfill(rows_dst + i * RPP * ROWB, src, ok);
       }
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      for (int i = 0; i < DEC_VKC / RPP; ++i) {
-        const int64_t key = k0 + r0 + i * RPP;
-        const bool ok = key < total;
-        const T* vs = !ok ? vb : (key < plen ? vb + key * vps_n : veb + (key - plen) * ves_n);
-        cp_async16_zfill(vd + i * RPP * ROWB, vs, ok);
-      }
-      asm volatile("cp.async.commit_group;" ::: "memory");
     }
-  }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  issue_rows(kp + b * kps_b + hk * kps_h + cs_seg * 8, kps_n, ke + b * kes_b + hk * kes_h + cs_seg * 8, kes_n);
   // q rows 0..G-1 (A-fragment rows 0..7; rows 8..15 are never read, their fragments are 0)
   for (int i = tid; i < 8 * D; i += NT) {
     const int g = i / D, d = i % D;
@@ -491,7 +478,7 @@ __global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
     const int64_t key = k0 + tid;
     bias[tid] = (key < plen) ? logf(static_cast<float>(counts[b * cs_b + hk * cs_h + key * cs_n])) : 0.f;
   }
-  asm volatile("cp.async.wait_group 1;" ::: "memory");  // K has landed; V is still in flight
+  asm volatile("cp.async.wait_group 0;" ::: "memory");  // K
   __syncthreads();
 
   const int g = lane >> 2;        // head row of this thread's accumulator fragments (rows g+8 are padding)
@@ -536,7 +523,8 @@ __global__ void __launch_bounds__(DEC_NW * 32, 3) decode_attn_mma_kernel(
   mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
   mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
   if ((lane & 3) == 0) swm[warp * 8 + g] = mx;
-  __syncthreads();
+  __syncthreads();  // every warp is done with K: V's rows go into the same buffer
+  issue_rows(vp + b * vps_b + hk * vps_h + cs_seg * 8, vps_n, ve + b * ves_b + hk * ves_h + cs_seg * 8, ves_n);
   float M = swm[g];
 #pragma unroll
   for (int w = 1; w < DEC_NW; ++w) M = fmaxf(M, swm[w * 8 + g]);
