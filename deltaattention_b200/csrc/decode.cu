@@ -286,12 +286,14 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
                                                              int64_t Hkv, int64_t nchunk, int64_t head_dim) {
   // pass 1: every chunk's (max, sum) in parallel, the block maximum, and each chunk's scale
   // factor in shared memory (0 for chunks past the sequence, whose O was never written);
-  // pass 2: one thread per head-dim column sums the scaled partial O over the chunks, eight
-  // chunks' loads in flight at a time
+  // pass 2: warp w sums the scaled partial O of chunks w, w + 4, ..., each lane two adjacent
+  // columns per 8-byte load, four chunks' loads in flight; the four warps' sums meet in
+  // shared memory
   extern __shared__ float cmb[];  // f[nchunk], then l[nchunk]
   float* sf = cmb;
   float* sl = cmb + nchunk;
   __shared__ float red[4];
+  __shared__ float2 wsum[4][BD / 2];
   const int64_t bh = blockIdx.x;  // (b, q-head)
   const int64_t Hq = Hkv * G;
   const int64_t b = bh / Hq, h = bh % Hq;
@@ -324,23 +326,46 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
   for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
   __syncthreads();  // every f is in place; red[] is free again
   if (lane == 0) red[warp] = l;
+  constexpr int NE = BD / 2 > 32 ? BD / 2 / 32 : 1;  // column pairs per lane
+  float2 acc[NE];
+#pragma unroll
+  for (int k = 0; k < NE; ++k) acc[k] = make_float2(0.f, 0.f);
+  for (int64_t c0 = warp; c0 < nchunk; c0 += 16) {
+    float2 v[4][NE];
+    float f[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t c = c0 + 4 * u;
+      f[u] = c < nchunk ? sf[c] : 0.f;
+      const float2* row = reinterpret_cast<const float2*>(base + c * cstride + 2);  // 8-byte aligned
+#pragma unroll
+      for (int k = 0; k < NE; ++k) {
+        const int e = lane + 32 * k;
+        v[u][k] = (f[u] != 0.f && e < BD / 2 && 2 * e < head_dim) ? row[e] : make_float2(0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int k = 0; k < NE; ++k) {
+        acc[k].x = fmaf(v[u][k].x, f[u], acc[k].x);
+        acc[k].y = fmaf(v[u][k].y, f[u], acc[k].y);
+      }
+  }
+#pragma unroll
+  for (int k = 0; k < NE; ++k) {
+    const int e = lane + 32 * k;
+    if (e < BD / 2) wsum[warp][e] = acc[k];
+  }
   __syncthreads();
   const float lt = (red[0] + red[1]) + (red[2] + red[3]);
   for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
-    const float* col = base + 2 + d;
-    float acc = 0.f;
-    for (int64_t c0 = 0; c0 < nchunk; c0 += 8) {
-      float v[8], f[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int64_t c = c0 + u;
-        f[u] = c < nchunk ? sf[c] : 0.f;
-        v[u] = f[u] != 0.f ? col[c * cstride] : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) acc = fmaf(v[u], f[u], acc);
-    }
-    out[b * os_b + h * os_h + d * os_d] = from_f32<T>(acc / lt);
+    const float* w0 = reinterpret_cast<const float*>(wsum[0]);
+    const float* w1 = reinterpret_cast<const float*>(wsum[1]);
+    const float* w2 = reinterpret_cast<const float*>(wsum[2]);
+    const float* w3 = reinterpret_cast<const float*>(wsum[3]);
+    const float a = (w0[d] + w1[d]) + (w2[d] + w3[d]);
+    out[b * os_b + h * os_h + d * os_d] = from_f32<T>(a / lt);
   }
 }
 
