@@ -442,7 +442,8 @@ __global__ void __launch_bounds__(DEC_NW * 32, 5) decode_attn_mma_kernel(
     const int32_t* __restrict__ counts, int64_t cs_b, int64_t cs_h, int64_t cs_n, const int32_t* __restrict__ lengths,
     int64_t ls_b, int64_t ls_h, const T* __restrict__ ke, int64_t kes_b, int64_t kes_h, int64_t kes_n,
     const T* __restrict__ ve, int64_t ves_b, int64_t ves_h, int64_t ves_n, float sm_scale, int64_t exact_len,
-    const int64_t* __restrict__ st, int64_t W, int G, int64_t Hkv, int64_t nchunk, float* __restrict__ part) {
+    const int64_t* __restrict__ st, int64_t W, int G, int64_t Hkv, int64_t nchunk, float* __restrict__ part,
+    bool qvec) {
   if (st) exact_len = st[0] < W ? st[0] : W;  // device-resident sequence state
   constexpr int ROWB = D * 2;   // bytes per K / V row
   constexpr int SEGS = D / 8;   // 16-byte segments per row
@@ -493,12 +494,21 @@ __global__ void __launch_bounds__(DEC_NW * 32, 5) decode_attn_mma_kernel(
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  issue_rows(kp + b * kps_b + hk * kps_h + cs_seg * 8, kps_n, ke + b * kes_b + hk * kes_h + cs_seg * 8, kes_n);
-  // q rows 0..G-1 (A-fragment rows 0..7; rows 8..15 are never read, their fragments are 0)
-  for (int i = tid; i < 8 * D; i += NT) {
-    const int g = i / D, d = i % D;
-    qsm[i] = g < G ? q[b * qs_b + (hk * G + g) * qs_h + d] : from_f32<T>(0.f);
+  // q rows 0..G-1 (A-fragment rows 0..7; rows 8..15 are never read, their fragments are 0):
+  // 16-byte copies in K's commit group when q's rows allow it
+  if (qvec) {
+    if (tid < 8 * SEGS) {
+      const int g = tid / SEGS, sq = tid % SEGS;
+      cp_async16_zfill(smem_u32(qsm) + g * ROWB + sq * 16, q + b * qs_b + (hk * G + (g < G ? g : 0)) * qs_h + sq * 8,
+                       g < G);
+    }
+  } else {
+    for (int i = tid; i < 8 * D; i += NT) {
+      const int g = i / D, d = i % D;
+      qsm[i] = g < G ? q[b * qs_b + (hk * G + g) * qs_h + d] : from_f32<T>(0.f);
+    }
   }
+  issue_rows(kp + b * kps_b + hk * kps_h + cs_seg * 8, kps_n, ke + b * kes_b + hk * kes_h + cs_seg * 8, kes_n);
   if (tid < DEC_VKC) {
     const int64_t key = k0 + tid;
     bias[tid] = (key < plen) ? logf(static_cast<float>(counts[b * cs_b + hk * cs_h + key * cs_n])) : 0.f;
@@ -673,7 +683,8 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
             static_cast<const TY*>(q), qs[0], qs[1], static_cast<const TY*>(kp), kps[0], kps[1], kps[2],
             static_cast<const TY*>(vp), vps[0], vps[1], vps[2], counts, cs[0], cs[1], cs[2], lengths, ls[0], ls[1],
             static_cast<const TY*>(ke), kes[0], kes[1], kes[2], static_cast<const TY*>(ve), ves[0], ves[1], ves[2],
-            sm_scale, exact_len, seq_state, W, static_cast<int>(G), Hkv, nc, part);
+            sm_scale, exact_len, seq_state, W, static_cast<int>(G), Hkv, nc, part,
+            a16(q) && (qs[0] % 8 | qs[1] % 8) == 0);
         const size_t csm = static_cast<size_t>(2 * nc) * sizeof(float);
         if (csm > 48 * 1024) {
           ea = cudaFuncSetAttribute(decode_combine_kernel<TY, DD>, cudaFuncAttributeMaxDynamicSharedMemorySize,

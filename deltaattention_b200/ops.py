@@ -245,9 +245,13 @@ def delta_prefill_host(q, k, v, cos, sin, *, out, kv_heads_per_group=1, q_heads_
     host->device copies, group g-1's compute and group g-2's device->host copy run at the same
     time on three streams. Results equal one ``delta_prefill`` call on the whole tensors.
 
-    Ordering: the copy streams first wait for the caller's current stream, and the current
-    stream waits for the last device->host copy before this returns, so work enqueued on the
-    current stream afterwards (an event, a synchronize) covers the whole layer-op.
+    Ordering: the current stream waits for the last device->host copy before this returns, so
+    work enqueued on the current stream afterwards (an event, a synchronize) covers the whole
+    layer-op. The device buffers are kept between calls with the same shapes (one set per
+    device and shape; ``release_host_prefill_buffers`` frees them), and each group's next
+    host->device copy waits only for this call's compute of the groups that read those
+    buffers, so consecutive calls overlap: the next call's copies start while this call's
+    last groups are still computing and draining.
 
     Only ``mode="periodic"``: the delta and mask modes size the packed history by the largest
     kept count over all heads (modeling_llama.py:656), and a head's padding changes its
@@ -268,13 +272,6 @@ def delta_prefill_host(q, k, v, cos, sin, *, out, kv_heads_per_group=1, q_heads_
     dev = cos.device
     cur = torch.cuda.current_stream(dev)
     h2d, d2h = _streams_for(dev)
-    dq = torch.empty(q.shape, dtype=q.dtype, device=dev)
-    dk = torch.empty(k.shape, dtype=k.dtype, device=dev)
-    dv = torch.empty(v.shape, dtype=v.dtype, device=dev)
-    do = torch.empty(out.shape, dtype=out.dtype, device=dev)
-    # the device buffers come from the current stream's pool: the copy streams start after it
-    h2d.wait_stream(cur)
-    d2h.wait_stream(cur)
     # groups: (kv-heads [a, b), query heads [qa, qb), copy K / V of [a, b) with this group)
     qg = G if q_heads_per_group is None else int(q_heads_per_group)
     if 1 <= qg < G:
@@ -284,9 +281,28 @@ def delta_prefill_host(q, k, v, cos, sin, *, out, kv_heads_per_group=1, q_heads_
     else:
         step = max(1, int(kv_heads_per_group))
         groups = [(a, min(Hkv, a + step), a * G, min(Hkv, a + step) * G, True) for a in range(0, Hkv, step)]
+    key = (dev.index, tuple(q.shape), tuple(k.shape), q.dtype, tuple(groups))
+    ws = _host_ws.get(key)
+    if ws is None:
+        ws = {"dq": torch.empty(q.shape, dtype=q.dtype, device=dev),
+              "dk": torch.empty(k.shape, dtype=k.dtype, device=dev),
+              "dv": torch.empty(v.shape, dtype=v.dtype, device=dev),
+              "do": torch.empty(out.shape, dtype=out.dtype, device=dev),
+              "computed": [None] * len(groups), "drained": [None] * len(groups)}
+        _host_ws[key] = ws
+        # the buffers come from the current stream's pool: the copy streams start after it
+        h2d.wait_stream(cur)
+        d2h.wait_stream(cur)
+    dq, dk, dv, do = ws["dq"], ws["dk"], ws["dv"], ws["do"]
+    computed, drained = ws["computed"], ws["drained"]
     ev_in = []
     with torch.cuda.stream(h2d):
-        for a, b, qa, qb, with_kv in groups:
+        for gi, (a, b, qa, qb, with_kv) in enumerate(groups):
+            # overwrite this group's buffers once the previous call's compute has read them (K / V
+            # of [a, b) are read by every group of those kv-heads)
+            for gj, (a2, b2, _, _, _) in enumerate(groups):
+                if computed[gj] is not None and (gj == gi or (with_kv and a2 < b and a < b2)):
+                    h2d.wait_event(computed[gj])
             for bi in range(B):
                 if with_kv:
                     dk[bi, a:b].copy_(k[bi, a:b], non_blocking=True)
@@ -295,17 +311,32 @@ def delta_prefill_host(q, k, v, cos, sin, *, out, kv_heads_per_group=1, q_heads_
             e = torch.cuda.Event()
             e.record(h2d)
             ev_in.append(e)
-    for (a, b, qa, qb, _), e in zip(groups, ev_in):
+    for gi, ((a, b, qa, qb, _), e) in enumerate(zip(groups, ev_in)):
         cur.wait_event(e)
+        if drained[gi] is not None:
+            cur.wait_event(drained[gi])  # the previous call's output of this group has left
         delta_prefill(dq[:, qa:qb], dk[:, a:b], dv[:, a:b], cos, sin, out=do[:, qa:qb], **kw)
         done = torch.cuda.Event()
         done.record(cur)
+        computed[gi] = done
         d2h.wait_event(done)
         with torch.cuda.stream(d2h):
             for bi in range(B):
                 out[bi, qa:qb].copy_(do[bi, qa:qb], non_blocking=True)
+            dr = torch.cuda.Event()
+            dr.record(d2h)
+            drained[gi] = dr
     cur.wait_stream(d2h)
     return out
+
+
+_host_ws = {}
+
+
+def release_host_prefill_buffers():
+    """Free the device buffers ``delta_prefill_host`` keeps between calls (after the work that
+    uses them has finished)."""
+    _host_ws.clear()
 
 
 def tile_count_periodic(N: int, r: int, W: int = 128) -> int:

@@ -407,6 +407,32 @@ def test_host_pipelined_prefill_equals_device_call(B, group, qgroup):
     _check_ws_clean()
 
 
+@pytest.mark.parametrize("group,qgroup", [(1, None), (2, None), (1, 2)])
+def test_host_prefill_back_to_back_calls(group, qgroup):
+    """Consecutive delta_prefill_host calls with no synchronisation between them (the next
+    call's copies overwrite the kept device buffers while the previous call still computes and
+    drains): every call's output equals its own device call, bit for bit."""
+    from deltaattention_b200 import ops, synth
+    B, Hq, Hkv, N, D = 1, 8, 4, 4096, 128
+    cos, sin = synth.rope_tables(N, D, 5e5, torch.bfloat16, device="cuda")
+    kw = dict(mode="periodic", keep_rate=0.25)
+    ins, wants, outs = [], [], []
+    for seed in range(4):
+        q, k, v = synth.layer_inputs(B, Hq, Hkv, N, D, torch.bfloat16, seed=100 + seed, device="cuda")
+        wants.append(ops.delta_prefill(q, k, v, cos, sin, **kw).cpu())
+        ins.append(tuple(t.contiguous().cpu().pin_memory() for t in (q, k, v)))
+        outs.append(torch.full((B, Hq, N, D), float("nan"), dtype=torch.bfloat16).pin_memory())
+    torch.cuda.synchronize()
+    for (hq, hk, hv), ho in zip(ins, outs):
+        ops.delta_prefill_host(hq, hk, hv, cos, sin, out=ho, kv_heads_per_group=group, q_heads_per_group=qgroup,
+                               **kw)
+    torch.cuda.current_stream().synchronize()
+    for ho, want in zip(outs, wants):
+        assert torch.equal(ho.view(torch.int16), want.view(torch.int16))
+    ops.release_host_prefill_buffers()
+    _check_ws_clean()
+
+
 def test_cfg1_fp32_full_size():
     """BASELINE config 1 (fp32, B=1, H=8, N=2048, d=64, r=4) at 1e-4."""
     from deltaattention_b200 import ops, synth
