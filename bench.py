@@ -217,16 +217,17 @@ def serving(dev, seed, steps=256):
 
     16 sequences with lengths U[4096, 32768] packed back to back (cu_seqlens) in one
     projection-layout buffer; q / v ~ N(0, 1), keys AR(1) (config-1 distributions), RoPE
-    theta 5e5, bf16. Prefill, per sequence: RoPE(q, k), 2:4 N:M selection at r = 4, device
-    packing, two-phase attention (dense window 128), hand-off of the packed history and the
-    last 100 keys into a DeviceDecodeCache. Then `steps` decode steps for all 16 sequences
+    theta 5e5, bf16. Prefill (ops.delta_prefill_varlen, sequences over three streams), per
+    sequence: RoPE(q, k), 2:4 N:M selection at r = 4, device packing, two-phase attention
+    (dense window 128); then the hand-off of each packed history and its last 100 keys into
+    a DeviceDecodeCache. Then `steps` decode steps for all 16 sequences
     (cache update with raw Euclidean threshold 15, length advance, decode attention), new
     keys continuing each sequence's AR(1) process; the steps are captured in one CUDA graph
     and replayed. HBM bytes per decode step: every packed K / V row with its count and the
     window read once (516 B per key)."""
     from deltaattention_b200 import ops, synth
     from deltaattention_b200.cache import DeviceDecodeCache
-    from deltaattention_b200.dropin.nmDeltaFlashAttention import nm_delta_flash_attention, nm_num_packed
+    from deltaattention_b200.dropin.nmDeltaFlashAttention import nm_num_packed
     B, Hq, Hkv, D, W, Wd, thr = 16, CFG["Hq"], CFG["Hkv"], CFG["D"], CFG["W"], 100, 15.0
     gen = torch.Generator().manual_seed(seed)
     lens = torch.randint(4096, 32769, (B,), generator=gen).tolist()
@@ -243,14 +244,11 @@ def serving(dev, seed, steps=256):
     stream = torch.cuda.current_stream(dev)
 
     def prefill():
-        for i in range(B):
+        _, packed = ops.delta_prefill_varlen(q, k, v, cos, sin, cu, selection="nm", n=2, m=4, ratio=4,
+                                             dense_window=W, out=o, return_packed=True)
+        for i, (pk, kr) in enumerate(packed):
             s0, s1 = cu[i], cu[i + 1]
-            qr = ops.rope(q[:, :, s0:s1], cos, sin)
-            kr = ops.rope(k[:, :, s0:s1], cos, sin)
-            vi = v[:, :, s0:s1]
-            _, pk = nm_delta_flash_attention(qr, kr, vi, 2, 4, 4, dense_window=W, out=o[:, :, s0:s1],
-                                             return_packed=True)
-            cache.load_prefill(0, pk.k, pk.v, pk.counts, pk.timestamps, kr[:, :, -Wd:], vi[:, :, -Wd:], s1 - s0,
+            cache.load_prefill(0, pk.k, pk.v, pk.counts, pk.timestamps, kr[:, :, -Wd:], v[:, :, s1 - Wd:s1], s1 - s0,
                                batch_index=i)
 
     prefill()

@@ -218,6 +218,73 @@ def delta_prefill(q, k, v, cos, sin, *, mode="periodic", keep_rate=0.25, thresho
     return o
 
 
+_varlen_streams = {}
+
+
+def delta_prefill_varlen(q, k, v, cos, sin, cu_seqlens, *, selection="nm", n=2, m=4, ratio=4, keep_rate=0.25,
+                         dense_window=128, sm_scale=None, out=None, streams=3, return_packed=False):
+    """The delta-attention prefill layer-op over sequences packed back to back (cu_seqlens).
+
+    q [1, Hq, T, d] and k / v [1, Hkv, T, d] (any strides, e.g. the [T, H, d] projection
+    output viewed as [1, H, T, d]) hold the sequences at offsets ``cu_seqlens`` (a host list
+    of B + 1 increasing ints, cu_seqlens[-1] = T); cos / sin are tables of at least the
+    longest sequence (positions restart at 0 in every sequence). Every sequence runs RoPE,
+    its own selection (``selection="nm"``: n:m structured at ``ratio``, the
+    nmDeltaFlashAttention variant; ``"periodic"``: keep t % round(1 / keep_rate) == 0), packing
+    and the two-phase attention, exactly as ``delta_prefill`` on that sequence alone.
+    Sequences go round-robin to ``streams`` CUDA streams, so one sequence's RoPE / selection /
+    packing overlaps another's attention; the caller's current stream is waited on first and
+    waits for every stream before this returns.
+
+    Returns out [1, Hq, T, d] (allocated when not given), and with ``return_packed`` also the
+    list of per-sequence (Packed, post-RoPE keys) for the decode-cache hand-off.
+    """
+    from .dropin.nmDeltaFlashAttention import nm_keep_mask, nm_num_packed
+    L.require_cuda(q, k, v, cos, sin, out)
+    if q.shape[0] != 1 or k.shape[0] != 1:
+        raise ValueError("delta_prefill_varlen: sequences are packed along dim 2 of [1, H, T, d] tensors")
+    cu = [int(x) for x in cu_seqlens]
+    T = q.shape[2]
+    if len(cu) < 2 or cu[0] != 0 or cu[-1] != T or any(b <= a for a, b in zip(cu, cu[1:])):
+        raise ValueError("delta_prefill_varlen: cu_seqlens must rise strictly from 0 to the packed length")
+    if max(b - a for a, b in zip(cu, cu[1:])) > cos.shape[-2]:
+        raise ValueError("delta_prefill_varlen: cos / sin are shorter than the longest sequence")
+    if selection not in ("nm", "periodic"):
+        raise ValueError(f"delta_prefill_varlen: unknown selection {selection}")
+    dev = q.device
+    if out is None:
+        out = torch.empty((1, q.shape[1], T, q.shape[3]), dtype=q.dtype, device=dev)
+    cur = torch.cuda.current_stream(dev)
+    ns = max(1, int(streams))
+    pool = _varlen_streams.setdefault(dev.index, [])
+    while len(pool) < ns:
+        pool.append(torch.cuda.Stream(dev))
+    for s in pool[:ns]:
+        s.wait_stream(cur)
+    packed = []
+    for i, (s0, s1) in enumerate(zip(cu, cu[1:])):
+        st = pool[i % ns]
+        with torch.cuda.stream(st):
+            q_rot = rope(q[:, :, s0:s1], cos, sin)
+            k_rot = rope(k[:, :, s0:s1], cos, sin)
+            vi = v[:, :, s0:s1]
+            if selection == "nm":
+                keep = nm_keep_mask(k_rot, n, m, ratio)
+                pk = pack_from_keep(k_rot, vi, keep, num_packed=nm_num_packed(s1 - s0, n, m, ratio))
+            else:
+                pk = pack_periodic(k_rot, vi, max(1, round(1.0 / keep_rate)))
+            attention(q_rot, k_rot, vi, pk, sm_scale=sm_scale, dense_window=dense_window, out=out[:, :, s0:s1])
+            if return_packed:
+                # handed to the caller's stream: keep the allocator from reusing them early
+                for t in (pk.k, pk.v, pk.timestamps, pk.counts, pk.counts_f32, k_rot):
+                    if t is not None:
+                        t.record_stream(cur)
+                packed.append((pk, k_rot))
+    for s in pool[:ns]:
+        cur.wait_stream(s)
+    return (out, packed) if return_packed else out
+
+
 _side_streams = {}
 
 

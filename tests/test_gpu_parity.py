@@ -433,6 +433,39 @@ def test_host_prefill_back_to_back_calls(group, qgroup):
     _check_ws_clean()
 
 
+@pytest.mark.parametrize("selection", ["nm", "periodic"])
+def test_varlen_prefill_equals_per_sequence_calls(selection):
+    """ops.delta_prefill_varlen over ragged sequences packed back to back (several streams):
+    every sequence's output and packed history equal a call on that sequence alone."""
+    from deltaattention_b200 import ops, synth
+    from deltaattention_b200.dropin import nmDeltaFlashAttention as nm
+    lens = [700, 1536, 1000, 2048, 513, 129]
+    cu = [0]
+    for n_ in lens:
+        cu.append(cu[-1] + n_)
+    Hq, Hkv, D = 8, 2, 128
+    q, k, v = synth.layer_inputs(1, Hq, Hkv, cu[-1], D, torch.bfloat16, seed=41, device="cuda", qv_scale=1.0,
+                                 key_offset=False)
+    cos, sin = synth.rope_tables(max(lens), D, 5e5, torch.bfloat16, device="cuda")
+    out, packed = ops.delta_prefill_varlen(q, k, v, cos, sin, cu, selection=selection, streams=3,
+                                           return_packed=True)
+    torch.cuda.synchronize()
+    for i, (s0, s1) in enumerate(zip(cu, cu[1:])):
+        q_rot = ops.rope(q[:, :, s0:s1], cos, sin)
+        k_rot = ops.rope(k[:, :, s0:s1], cos, sin)
+        if selection == "nm":
+            want, pk = nm.nm_delta_flash_attention(q_rot, k_rot, v[:, :, s0:s1], 2, 4, 4, return_packed=True)
+        else:
+            pk = ops.pack_periodic(k_rot, v[:, :, s0:s1], 4)
+            want = ops.attention(q_rot, k_rot, v[:, :, s0:s1], pk)
+        got_pk, got_k = packed[i]
+        assert torch.equal(out[:, :, s0:s1].view(torch.int16), want.view(torch.int16)), (selection, i)
+        assert torch.equal(got_k.view(torch.int16), k_rot.view(torch.int16))
+        assert torch.equal(got_pk.k.view(torch.int16), pk.k.view(torch.int16))
+        assert torch.equal(got_pk.timestamps, pk.timestamps) and torch.equal(got_pk.counts, pk.counts)
+    _check_ws_clean()
+
+
 def test_cfg1_fp32_full_size():
     """BASELINE config 1 (fp32, B=1, H=8, N=2048, d=64, r=4) at 1e-4."""
     from deltaattention_b200 import ops, synth
