@@ -43,10 +43,29 @@ __global__ void __launch_bounds__(128) decode_update_kernel(
   int32_t* cb = counts + b * cs_b + h * cs_h;
   int32_t* tb = ts + b * cs_b + h * cs_h;
   const int32_t plen = lengths[pid];
+  // every load that does not depend on the decision is issued now: the new token and the
+  // evicted V row (its K row is loaded below with the last anchor's key and count)
+  constexpr int NV = BD / 32 > 0 ? BD / 32 : 1;  // elements per lane of a row
+  T nkr[NV], nvr[NV], evr[NV];
+  {
+    const T* sk = nk + b * ns_b + h * ns_h;
+    const T* sv = nv + b * ns_b + h * ns_h;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int64_t d = lane + 32 * j;
+      if (d < head_dim) {
+        nkr[j] = sk[d * ns_d];
+        nvr[j] = sv[d * ns_d];
+        evr[j] = ev[d * es_d];
+      }
+    }
+  }
   if (exact_seq_len >= W) {
     bool merge = false;
+    int32_t last_count = 0;
     if (plen > 0) {
       const T* lk = pk + static_cast<int64_t>(plen - 1) * ps_s;
+      if (lane == 0) last_count = cb[static_cast<int64_t>(plen - 1) * cs_s];
       float ea[NH][PER], la[NH][PER];
 #pragma unroll
       for (int hh = 0; hh < NH; ++hh)
@@ -102,13 +121,17 @@ __global__ void __launch_bounds__(128) decode_update_kernel(
       }
     }
     if (merge) {
-      if (lane == 0) cb[static_cast<int64_t>(plen - 1) * cs_s] += 1;
+      if (lane == 0) cb[static_cast<int64_t>(plen - 1) * cs_s] = last_count + 1;
     } else if (plen < capacity) {
       T* dk = pk + static_cast<int64_t>(plen) * ps_s;
       T* dv = pv + static_cast<int64_t>(plen) * ps_s;
-      for (int64_t d = lane; d < head_dim; d += 32) {
-        dk[d * ps_d] = ek[d * es_d];
-        dv[d * ps_d] = ev[d * es_d];
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int64_t d = lane + 32 * j;
+        if (d < head_dim) {
+          dk[d * ps_d] = ek[d * es_d];
+          dv[d * ps_d] = evr[j];
+        }
       }
       if (lane == 0) {
         cb[static_cast<int64_t>(plen) * cs_s] = 1;
@@ -119,12 +142,14 @@ __global__ void __launch_bounds__(128) decode_update_kernel(
       atomicCAS(err, 0, 0x201);  // packed cache full: the caller must grow it first
     }
   }
-  __syncwarp();
-  const T* sk = nk + b * ns_b + h * ns_h;
-  const T* sv = nv + b * ns_b + h * ns_h;
-  for (int64_t d = lane; d < head_dim; d += 32) {
-    ek[d * es_d] = sk[d * ns_d];
-    ev[d * es_d] = sv[d * ns_d];
+  __syncwarp();  // the evicted row has been read by every lane before it is overwritten
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int64_t d = lane + 32 * j;
+    if (d < head_dim) {
+      ek[d * es_d] = nkr[j];
+      ev[d * es_d] = nvr[j];
+    }
   }
 }
 
