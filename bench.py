@@ -153,9 +153,9 @@ def decode_step(dev, seed, layers=32, steps=20):
     """One decode token over every layer of a Llama-3.1-8B-shaped model with the device-length
     cache (cache.DeviceDecodeCache): 16 sequences, Hq=32 / Hkv=8, d=128, packed lengths
     uniform in [1024, 8192] per (sequence, kv-head), exact window 100. Timed as eager
-    launches (update, advance, attention + combine per layer) and as one replayed CUDA graph.
-    HBM bytes per step: packed K / V rows, counts and the window read once per layer
-    (516 B per key), as in hbm_kernels."""
+    launches (update, then attention + combine with the length advance, per layer) and as
+    one replayed CUDA graph. HBM bytes per step: packed K / V rows, counts and the window read
+    once per layer (516 B per key), as in hbm_kernels."""
     from deltaattention_b200.cache import DeviceDecodeCache
     from deltaattention_b200 import _lib as L
     B, Hq, Hkv, D, W, cap = 16, 32, 8, 128, 100, 8192 + 64
@@ -209,7 +209,7 @@ def decode_step(dev, seed, layers=32, steps=20):
     return {"layers": layers, "shape": f"B={B} Hq={Hq} Hkv={Hkv} d={D} packed U[1024,8192] window {W}",
             "eager_ms": eager_ms, "graph_ms": graph_ms, "tokens_per_s": B / (graph_ms / 1000.0),
             "hbm_gbs": nbytes / (graph_ms / 1000.0) / 1e9, "frac": nbytes / (graph_ms / 1000.0) / 1e9 / peak,
-            "launches_per_step": layers * 4, "err": err, "ws_errors": codes}
+            "launches_per_step": layers * 3, "err": err, "ws_errors": codes}
 
 
 def serving(dev, seed, steps=256):

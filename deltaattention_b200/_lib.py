@@ -46,8 +46,8 @@ SIGNATURES = {
                                    P]),
     "dab_decode_update_dev": (I32, [P, P, P, P, P, P, P, P, P, P, F32, I64, I32, PI64, PI64, PI64, PI64, I64,
                                     I64, I64, I32, I64, I64, P, P]),
-    "dab_decode_attention_dev": (I32, [P, P, P, P, P, P, P, P, I32, PI64, F32, P, I64, I64, I64, I64, I64, I64, P,
-                                       SZ, P]),
+    "dab_decode_attention_dev": (I32, [P, P, P, P, P, P, P, P, I32, PI64, F32, P, I32, I64, I64, I64, I64, I64, I64,
+                                       P, SZ, P]),
     "dab_decode_advance": (I32, [P, I64, P]),
     "dab_rope": (I32, [P, PI64, P, PI64, P, P, PI64, I32, I64, I64, I64, I64, P]),
     "dab_periodic_meta": (I32, [P, P, P, I64, I64, I64, I64, P]),

@@ -7,8 +7,9 @@ grows its packed buffers by copying them. ``DeviceDecodeCache`` keeps the same b
 (shapes, dtypes, layouts) and runs the same kernels, with three differences:
 
 * the ``(exact, total)`` lengths of each layer live in an int64 device tensor, read by the
-  update and attention kernels and advanced by a kernel, so a decode step issues kernel
-  launches only (no host synchronisation, no host-side length bookkeeping);
+  update and attention kernels and advanced on the device (by the attention call's last
+  kernel in ``step``), so a decode step issues kernel launches only (no host
+  synchronisation, no host-side length bookkeeping);
 * the packed capacity is fixed at construction (prefill anchors plus the decode steps
   planned: each step appends at most one anchor per head); a full cache sets the update
   kernel's error word (0x201) instead of growing;
@@ -84,9 +85,10 @@ class DeviceDecodeCache:
             self._ws_heads = hq
         return self._ws
 
-    def update(self, layer, k_new, v_new):
+    def update(self, layer, k_new, v_new, advance=True):
         """Append one token per (batch, kv-head): k_new / v_new [B, Hkv, 1, d]. Advances the
-        layer's lengths on the device."""
+        layer's lengths on the device (with ``advance=False`` the advance is left to the next
+        ``attend(..., advance=True)``)."""
         L.require_cuda(k_new, v_new)
         lib = L.load()
         st = L.stream_of(k_new)
@@ -101,10 +103,15 @@ class DeviceDecodeCache:
             L.dtype_code(k_new), L.strides(k_new.stride()), L.strides(ke.stride()), L.strides(kp.stride()),
             L.strides(pc.stride()), self.n_kv_heads, self.head_dim, bd, 1 if self.use_cosine else 0,
             self.bsz * self.n_kv_heads, self.capacity, L.ptr(self.err), st), "decode_update_dev")
-        L.check(lib.dab_decode_advance(L.ptr(self.seq_state[layer]), 1, st), "decode_advance")
+        if advance:
+            L.check(lib.dab_decode_advance(L.ptr(self.seq_state[layer]), 1, st), "decode_advance")
 
-    def attend(self, layer, q, out=None, sm_scale=None):
-        """Decode attention of q [B, Hq, d] over the layer's packed history and exact window."""
+    def attend(self, layer, q, out=None, sm_scale=None, advance=False):
+        """Decode attention of q [B, Hq, d] over the layer's packed history and exact window.
+
+        With ``advance`` the call also performs the length advance an ``update(...,
+        advance=False)`` left pending: it attends with the advanced window length and steps
+        the lengths after its last read."""
         L.require_cuda(q, out)
         B, hq, D = q.shape
         if out is None:
@@ -121,14 +128,16 @@ class DeviceDecodeCache:
         ws = self._workspace(hq)
         L.check(lib.dab_decode_attention_dev(
             L.ptr(q), L.ptr(kp), L.ptr(vp), L.ptr(pc), L.ptr(pl), L.ptr(ke), L.ptr(ve), L.ptr(out), L.dtype_code(q),
-            L.strides(strides), float(sm_scale), L.ptr(self.seq_state[layer]), self.exact_window_size,
+            L.strides(strides), float(sm_scale), L.ptr(self.seq_state[layer]), 1 if advance else 0,
+            self.exact_window_size,
             hq // self.n_kv_heads, B, hq, D, self.capacity, L.ptr(ws), ws.numel(), st), "decode_attention_dev")
         return out
 
     def step(self, layer, q, k_new, v_new, out=None):
-        """One layer's decode step: update, length advance, attention (the reference's order)."""
-        self.update(layer, k_new, v_new)
-        return self.attend(layer, q, out)
+        """One layer's decode step: update, length advance, attention (the reference's order),
+        as two launches: the advance rides with the attention call."""
+        self.update(layer, k_new, v_new, advance=False)
+        return self.attend(layer, q, out, advance=True)
 
     def lengths(self):
         """(exact, total) per layer, read back to the host (a synchronising call)."""

@@ -38,7 +38,7 @@ cudaError_t launch_decode_update(int, int, bool, const void*, const void*, void*
 cudaError_t launch_decode_attn(int, const void*, const int64_t*, const void*, const int64_t*, const void*,
                                const int64_t*, const int32_t*, const int64_t*, const int32_t*, const int64_t*,
                                const void*, const int64_t*, const void*, const int64_t*, void*, const int64_t*,
-                               float, int64_t, const int64_t*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                               float, int64_t, int64_t*, int, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
                                float*, cudaStream_t);
 cudaError_t launch_decode_advance(int64_t*, int64_t, cudaStream_t);
 size_t decode_attn_workspace(int64_t, int64_t, int64_t, int64_t, int64_t);
@@ -415,7 +415,7 @@ int dab_decode_attention(const void* q, const void* k_packed, const void* v_pack
   const int64_t* s = strides;
   return cuda_status(launch_decode_attn(dtype, q, s + 0, k_packed, s + 3, v_packed, s + 7, packed_counts, s + 11,
                                         packed_lengths, s + 14, k_exact, s + 16, v_exact, s + 20, out, s + 24,
-                                        sm_scale, exact_len, nullptr, exact_len, num_kv_groups, batch,
+                                        sm_scale, exact_len, nullptr, 0, exact_len, num_kv_groups, batch,
                                         num_q_heads / num_kv_groups, head_dim, capacity,
                                         static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)),
                      "decode_attention");
@@ -449,8 +449,8 @@ int dab_decode_update_dev(const void* new_k, const void* new_v, void* k_exact, v
 int dab_decode_attention_dev(const void* q, const void* k_packed, const void* v_packed,
                              const int32_t* packed_counts, const int32_t* packed_lengths, const void* k_exact,
                              const void* v_exact, void* out, int dtype, const int64_t* strides, float sm_scale,
-                             const int64_t* seq_state, int64_t exact_window, int64_t num_kv_groups, int64_t batch,
-                             int64_t num_q_heads, int64_t head_dim, int64_t capacity, void* workspace,
+                             int64_t* seq_state, int advance, int64_t exact_window, int64_t num_kv_groups,
+                             int64_t batch, int64_t num_q_heads, int64_t head_dim, int64_t capacity, void* workspace,
                              size_t workspace_bytes, void* stream) {
   if (!seq_state) return fail(1, "dab_decode_attention_dev: null seq_state");
   if (!q || !k_packed || !v_packed || !packed_counts || !packed_lengths || !k_exact || !v_exact || !out)
@@ -465,8 +465,8 @@ int dab_decode_attention_dev(const void* q, const void* k_packed, const void* v_
   const int64_t* s = strides;
   return cuda_status(launch_decode_attn(dtype, q, s + 0, k_packed, s + 3, v_packed, s + 7, packed_counts, s + 11,
                                         packed_lengths, s + 14, k_exact, s + 16, v_exact, s + 20, out, s + 24,
-                                        sm_scale, exact_window, seq_state, exact_window, num_kv_groups, batch,
-                                        num_q_heads / num_kv_groups, head_dim, capacity,
+                                        sm_scale, exact_window, seq_state, advance, exact_window, num_kv_groups,
+                                        batch, num_q_heads / num_kv_groups, head_dim, capacity,
                                         static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)),
                      "decode_attention_dev");
 }

@@ -205,8 +205,11 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(
     const int32_t* __restrict__ lengths, int64_t ls_b, int64_t ls_h, const T* __restrict__ ke, int64_t kes_b,
     int64_t kes_h, int64_t kes_n, int64_t kes_d, const T* __restrict__ ve, int64_t ves_b, int64_t ves_h,
     int64_t ves_n, int64_t ves_d, float sm_scale, int64_t exact_len, const int64_t* __restrict__ st, int64_t W,
-    int64_t G, int64_t Hkv, int64_t head_dim, int64_t nchunk, float* __restrict__ part) {
-  if (st) exact_len = st[0] < W ? st[0] : W;  // device-resident sequence state
+    int64_t lag, int64_t G, int64_t Hkv, int64_t head_dim, int64_t nchunk, float* __restrict__ part) {
+  if (st) {  // device-resident sequence state, `lag` steps behind when the advance follows
+    const int64_t e = st[0] + lag;
+    exact_len = e < W ? e : W;
+  }
   __shared__ float sq[DEC_GMAX][BD];
   __shared__ float sp[DEC_GMAX][DEC_KC];
   __shared__ float swm[4][DEC_GMAX];
@@ -308,7 +311,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(
 template <typename T, int BD>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __restrict__ part, T* __restrict__ out,
                                                              int64_t os_b, int64_t os_h, int64_t os_d, int64_t G,
-                                                             int64_t Hkv, int64_t nchunk, int64_t head_dim) {
+                                                             int64_t Hkv, int64_t nchunk, int64_t head_dim,
+                                                             int64_t* __restrict__ adv) {
   // pass 1: every chunk's (max, sum) in parallel, the block maximum, and each chunk's scale
   // factor in shared memory (0 for chunks past the sequence, whose O was never written);
   // pass 2: warp w sums the scaled partial O of chunks w, w + 4, ..., each lane two adjacent
@@ -392,6 +396,11 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
     const float a = (w0[d] + w1[d]) + (w2[d] + w3[d]);
     out[b * os_b + h * os_h + d * os_d] = from_f32<T>(a / lt);
   }
+  // the step's length advance, after the attention kernel (the state's last reader this step)
+  if (adv && blockIdx.x == 0 && threadIdx.x == 0) {
+    adv[0] += 1;
+    adv[1] += 1;
+  }
 }
 
 // Tensor-core split-K decode for 16-bit types with unit head-dim strides and 16-byte rows.
@@ -467,9 +476,12 @@ __global__ void __launch_bounds__(DEC_NW * 32, 5) decode_attn_mma_kernel(
     const int32_t* __restrict__ counts, int64_t cs_b, int64_t cs_h, int64_t cs_n, const int32_t* __restrict__ lengths,
     int64_t ls_b, int64_t ls_h, const T* __restrict__ ke, int64_t kes_b, int64_t kes_h, int64_t kes_n,
     const T* __restrict__ ve, int64_t ves_b, int64_t ves_h, int64_t ves_n, float sm_scale, int64_t exact_len,
-    const int64_t* __restrict__ st, int64_t W, int G, int64_t Hkv, int64_t nchunk, float* __restrict__ part,
-    bool qvec) {
-  if (st) exact_len = st[0] < W ? st[0] : W;  // device-resident sequence state
+    const int64_t* __restrict__ st, int64_t W, int64_t lag, int G, int64_t Hkv, int64_t nchunk,
+    float* __restrict__ part, bool qvec) {
+  if (st) {  // device-resident sequence state, `lag` steps behind when the advance follows
+    const int64_t e = st[0] + lag;
+    exact_len = e < W ? e : W;
+  }
   constexpr int ROWB = D * 2;   // bytes per K / V row
   constexpr int SEGS = D / 8;   // 16-byte segments per row
   constexpr int NT = DEC_NW * 32;        // threads
@@ -671,8 +683,13 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
                                const void* vp, const int64_t* vps, const int32_t* counts, const int64_t* cs,
                                const int32_t* lengths, const int64_t* ls, const void* ke, const int64_t* kes,
                                const void* ve, const int64_t* ves, void* out, const int64_t* os, float sm_scale,
-                               int64_t exact_len, const int64_t* seq_state, int64_t W, int64_t G, int64_t B,
-                               int64_t Hkv, int64_t head_dim, int64_t capacity, float* part, cudaStream_t st) {
+                               int64_t exact_len, int64_t* seq_state, int advance, int64_t W, int64_t G,
+                               int64_t B, int64_t Hkv, int64_t head_dim, int64_t capacity, float* part,
+                               cudaStream_t st) {
+  // advance: the kernels read exact = min(state[0] + 1, W) and the combine step then adds 1 to
+  // both lengths (one launch fewer than a separate advance between update and attention)
+  const int64_t lag = (seq_state && advance) ? 1 : 0;
+  int64_t* adv = lag ? seq_state : nullptr;
   // with a device-resident state the window length is read on the device; `exact_len` is then
   // its bound (the window size) and sizes the split-K grid
   if (B * Hkv == 0) return cudaSuccess;
@@ -708,7 +725,7 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
             static_cast<const TY*>(q), qs[0], qs[1], static_cast<const TY*>(kp), kps[0], kps[1], kps[2],
             static_cast<const TY*>(vp), vps[0], vps[1], vps[2], counts, cs[0], cs[1], cs[2], lengths, ls[0], ls[1],
             static_cast<const TY*>(ke), kes[0], kes[1], kes[2], static_cast<const TY*>(ve), ves[0], ves[1], ves[2],
-            sm_scale, exact_len, seq_state, W, static_cast<int>(G), Hkv, nc, part,
+            sm_scale, exact_len, seq_state, W, lag, static_cast<int>(G), Hkv, nc, part,
             a16(q) && (qs[0] % 8 | qs[1] % 8) == 0);
         const size_t csm = static_cast<size_t>(2 * nc) * sizeof(float);
         if (csm > 48 * 1024) {
@@ -717,7 +734,7 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
           if (ea != cudaSuccess) return ea;
         }
         decode_combine_kernel<TY, DD><<<static_cast<unsigned>(B * Hkv * G), 128, csm, st>>>(
-            part, static_cast<TY*>(out), os[0], os[1], os[2], G, Hkv, nc, head_dim);
+            part, static_cast<TY*>(out), os[0], os[1], os[2], G, Hkv, nc, head_dim, adv);
         return cudaGetLastError();
       };
       using I64 = std::integral_constant<int, 64>;
@@ -743,9 +760,9 @@ cudaError_t launch_decode_attn(int dtype, const void* q, const int64_t* qs, cons
       static_cast<const TY*>(q), qs[0], qs[1], qs[2], static_cast<const TY*>(kp), kps[0], kps[1], kps[2], kps[3], \
       static_cast<const TY*>(vp), vps[0], vps[1], vps[2], vps[3], counts, cs[0], cs[1], cs[2], lengths, ls[0],  \
       ls[1], static_cast<const TY*>(ke), kes[0], kes[1], kes[2], kes[3], static_cast<const TY*>(ve), ves[0],    \
-      ves[1], ves[2], ves[3], sm_scale, exact_len, seq_state, W, G, Hkv, head_dim, nchunk, part);               \
+      ves[1], ves[2], ves[3], sm_scale, exact_len, seq_state, W, lag, G, Hkv, head_dim, nchunk, part);          \
   decode_combine_kernel<TY, N><<<static_cast<unsigned>(B * Hkv * G), 128, csm, st>>>(                           \
-      part, static_cast<TY*>(out), os[0], os[1], os[2], G, Hkv, nchunk, head_dim);                              \
+      part, static_cast<TY*>(out), os[0], os[1], os[2], G, Hkv, nchunk, head_dim, adv);                         \
   return cudaGetLastError();
 #define DAB_DEC_BD(TY)           \
   switch (bd) {                  \

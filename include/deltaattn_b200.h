@@ -162,7 +162,10 @@ int dab_decode_attention(const void* q, const void* k_packed, const void* v_pack
  * dab_decode_attention with exact_len = min(seq_state[0], exact_window) read on the device
  * (the workspace is sized with exact_len = exact_window); dab_decode_advance adds 1 to both
  * lengths of `count` consecutive states. One decode step is update, advance, attention, the
- * order of modeling_llama.py's update, length increment and attention. */
+ * order of modeling_llama.py's update, length increment and attention. With advance != 0,
+ * dab_decode_attention_dev folds the advance into the attention call: it reads
+ * exact_len = min(seq_state[0] + 1, exact_window) and adds 1 to both lengths after its last
+ * read, so a step is update then attention (one launch fewer). */
 int dab_decode_update_dev(const void* new_k, const void* new_v, void* k_exact, void* v_exact, void* k_packed,
                           void* v_packed, int32_t* packed_counts, int32_t* packed_ts, int32_t* packed_lengths,
                           const int64_t* seq_state, float threshold, int64_t exact_window, int dtype,
@@ -172,8 +175,8 @@ int dab_decode_update_dev(const void* new_k, const void* new_v, void* k_exact, v
 int dab_decode_attention_dev(const void* q, const void* k_packed, const void* v_packed,
                              const int32_t* packed_counts, const int32_t* packed_lengths, const void* k_exact,
                              const void* v_exact, void* out, int dtype, const int64_t* strides, float sm_scale,
-                             const int64_t* seq_state, int64_t exact_window, int64_t num_kv_groups, int64_t batch,
-                             int64_t num_q_heads, int64_t head_dim, int64_t capacity, void* workspace,
+                             int64_t* seq_state, int advance, int64_t exact_window, int64_t num_kv_groups,
+                             int64_t batch, int64_t num_q_heads, int64_t head_dim, int64_t capacity, void* workspace,
                              size_t workspace_bytes, void* stream);
 int dab_decode_advance(int64_t* seq_state, int64_t count, void* stream);
 

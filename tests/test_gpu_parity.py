@@ -653,6 +653,25 @@ def test_device_decode_cache_matches_host_lengths():
     _check_ws_clean()
 
 
+def test_device_decode_cache_folded_advance_equals_separate():
+    """step() folds the length advance into the attention call (two launches); update with its
+    own advance kernel followed by attend gives bit-identical outputs, lengths and cache."""
+    layers = 2
+    a, _, steps, _ = _device_cache_setup(layers, seed=63)
+    b, _, _, _ = _device_cache_setup(layers, seed=63)
+    for q, kn, vn in steps:
+        for layer in range(layers):
+            got = a.step(layer, q[layer], kn[layer], vn[layer])
+            b.update(layer, kn[layer], vn[layer], advance=True)
+            want = b.attend(layer, q[layer], advance=False)
+            assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    torch.cuda.synchronize()
+    assert a.lengths() == b.lengths()
+    assert torch.equal(a.packed_counts, b.packed_counts) and torch.equal(a.packed_lengths, b.packed_lengths)
+    assert torch.equal(a.k_exact.view(torch.int16), b.k_exact.view(torch.int16))
+    _check_ws_clean()
+
+
 def test_device_decode_cache_graph_replay():
     """A decode step over every layer captured once in a CUDA graph and replayed per token
     equals the eager steps token by token."""

@@ -64,7 +64,7 @@ def test_device_length_entries_reject_null_state(lib_path):
     assert lib.dab_decode_advance(None, 0, None) == 0  # nothing to advance
     rc = lib.dab_decode_update_dev(*([None] * 9), None, 0.0, 16, 2, z, z, z, z, 2, 128, 128, 0, 2, 64, None, None)
     assert rc != 0 and b"seq_state" in lib.dab_last_error()
-    rc = lib.dab_decode_attention_dev(*([None] * 8), 2, z, 1.0, None, 16, 4, 1, 8, 128, 64, None, 0, None)
+    rc = lib.dab_decode_attention_dev(*([None] * 8), 2, z, 1.0, None, 1, 16, 4, 1, 8, 128, 64, None, 0, None)
     assert rc != 0 and b"seq_state" in lib.dab_last_error()
 
 
