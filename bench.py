@@ -63,8 +63,8 @@ def hbm_kernels(dev, seed):
     """HBM-bound kernels of the path, each launch timed alone with L2 flushed before it.
 
     Returns {name: {"us": t, "bytes": algorithmic bytes, "gbs": bytes / t, "frac": gbs / peak}}:
-    delta selection (chunked_eval, cfg2 keys), device packing from a keep mask (cfg2 K/V), 2:4 N:M
-    selection (cfg2 keys),
+    delta selection (chunked_eval, cfg2 keys), device packing from a keep mask (cfg2 K/V), the
+    reference-facing scatter pack of the same mask, 2:4 N:M selection (cfg2 keys),
     decode attention (16 sequences, packed lengths U[1024, 8192], window 100, 32 q-heads) and
     the decode cache update (one token per sequence)."""
     from deltaattention_b200 import ops, synth
@@ -101,6 +101,20 @@ def hbm_kernels(dev, seed):
     nbytes = Hkv * N * 4 + kept * D * 2 * 2 * 2 + Hkv * M * 8
     out["pack_from_keep"] = {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / peak,
                              "kept_fraction": kept / (Hkv * N)}
+    # the reference-facing scatter pack (tritonModules.parallel_scatter_pack_kv_kernel) with the
+    # index map the reference builds (cumsum - 1): keep / index map read, kept K / V rows moved,
+    # timestamps written
+    from deltaattention_b200.launch import parallel_scatter_pack_kv_kernel
+    im = (torch.cumsum(keep, -1) - 1).to(torch.int32)
+    kp_s = torch.zeros((1, Hkv, M, D), dtype=torch.bfloat16, device=dev)
+    vp_s = torch.zeros_like(kp_s)
+    ts_s = torch.zeros((1, Hkv, M), dtype=torch.int32, device=dev)
+    us = timed(lambda: parallel_scatter_pack_kv_kernel[(Hkv, -(-N // 64))](
+        k_rot, v, kp_s, vp_s, ts_s, keep, im, *k_rot.stride(), *v.stride(), *kp_s.stride(), *vp_s.stride(),
+        *ts_s.stride(), *keep.stride(), *im.stride(), N, D, Hkv, BLOCK_S=64, BLOCK_D=D))
+    nbytes = Hkv * N * 8 + kept * D * 2 * 2 * 2 + kept * 4
+    out["scatter_pack"] = {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / peak}
+    del im, kp_s, vp_s, ts_s
     # 2:4 N:M selection at r = 4: candidates every 2nd key, so half of K is read; keep mask written
     from deltaattention_b200.dropin.nmDeltaFlashAttention import nm_keep_mask
     us = timed(lambda: nm_keep_mask(k_rot, 2, 4, 4))
@@ -576,7 +590,20 @@ def run_ours(args, world, rank, local):
     d1.record(stream)
     torch.cuda.synchronize()
     dense_ms = max_over_ranks(d0.elapsed_time(d1) / nd, world)
-    del q_rot, k_rot
+    # the reference's other two kernels of the same family (deltaFlashAttention.py:149-357):
+    # the sanity variant (phase-1 QK^T computed and discarded) and pure phase 1
+    variants = {}
+    pk = ops.pack_periodic(k_rot, v, period)
+    for name in ("sanity", "pure_phase1"):
+        ops.attention(q_rot, k_rot, v, pk, dense_window=W, variant=name)
+        torch.cuda.synchronize()
+        d0.record(stream)
+        for _ in range(nd):
+            ops.attention(q_rot, k_rot, v, pk, dense_window=W, variant=name)
+        d1.record(stream)
+        torch.cuda.synchronize()
+        variants[name] = {"ms": max_over_ranks(d0.elapsed_time(d1) / nd, world)}
+    del q_rot, k_rot, pk
 
     # end to end through the public API: pinned host inputs (head-major [B, H, N, d]) -> device
     # -> pinned host output; ops.delta_prefill_host overlaps each kv-head group's copies with
@@ -630,6 +657,7 @@ def run_ours(args, world, rank, local):
                 "pcie_gbs": {"h2d": (hq.numel() + hk.numel() + hv.numel()) * 2 / (e2e_ms / 1000.0) / 1e9,
                              "d2h": ho.numel() * 2 / (e2e_ms / 1000.0) / 1e9}},
         "dense_r1": {"ms_per_step": dense_ms, "speedup_of_delta_attention": dense_ms / attn_ms},
+        "variants": variants,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }

@@ -440,6 +440,8 @@ cudaError_t launch_chunked_eval(int dtype, int bd, bool cosine, const void* x, c
 // ---------------------------------------------------------------------------------------
 // scatter pack (drop-in): for kept s, Kp[idx[s]] = K[s], Vp[idx[s]] = V[s], ts[idx[s]] = s
 // ---------------------------------------------------------------------------------------
+constexpr int SP_TPG = 4;  // tokens per 8-lane group in scatter_pack_kernel
+
 template <typename T>
 __global__ void __launch_bounds__(256) scatter_pack_kernel(
     const T* __restrict__ k, const int64_t* __restrict__ unused, const T* __restrict__ v, T* __restrict__ kp,
@@ -448,25 +450,81 @@ __global__ void __launch_bounds__(256) scatter_pack_kernel(
     int64_t vs_h, int64_t vs_s, int64_t vs_d, int64_t kps_b, int64_t kps_h, int64_t kps_a, int64_t kps_d,
     int64_t vps_b, int64_t vps_h, int64_t vps_a, int64_t vps_d, int64_t tss_b, int64_t tss_h, int64_t tss_a,
     int64_t kms_b, int64_t kms_h, int64_t kms_s, int64_t ims_b, int64_t ims_h, int64_t ims_s, int64_t seq_len,
-    int64_t head_dim, int64_t num_heads, int64_t rows_covered, int64_t num_packed) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t s = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
+    int64_t head_dim, int64_t num_heads, int64_t rows_covered, int64_t num_packed, bool vec) {
+  // SP_TPG consecutive tokens per 8-lane group: their keep flags and index-map entries load
+  // together, then every kept row's loads are issued before its stores; rows move as 16-byte
+  // pieces (`vec`: unit head-dim strides, 16-byte aligned rows) or element by element
+  const int lane8 = threadIdx.x & 7;
+  const int64_t s0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 3) + (threadIdx.x >> 3)) * SP_TPG;
   const int64_t bh = blockIdx.y;
-  if (s >= seq_len || s >= rows_covered) return;
+  const int64_t lim = seq_len < rows_covered ? seq_len : rows_covered;
+  if (s0 >= lim) return;
   const int64_t b = bh / num_heads, h = bh % num_heads;
-  if (km[b * kms_b + h * kms_h + s * kms_s] != 1) return;
-  const int64_t dst = im[b * ims_b + h * ims_h + s * ims_s];
-  if (dst < 0 || dst >= num_packed) return;  // out-of-range destinations are dropped, not written
-  const T* krow = k + b * ks_b + h * ks_h + s * ks_s;
-  const T* vrow = v + b * vs_b + h * vs_h + s * vs_s;
-  T* kdst = kp + b * kps_b + h * kps_h + dst * kps_a;
-  T* vdst = vp + b * vps_b + h * vps_h + dst * vps_a;
-  for (int64_t d = lane; d < head_dim; d += 32) {
-    kdst[d * kps_d] = krow[d * ks_d];
-    vdst[d * vps_d] = vrow[d * vs_d];
+  int64_t dst[SP_TPG];
+#pragma unroll
+  for (int t = 0; t < SP_TPG; ++t) {
+    const int64_t s = s0 + t;
+    dst[t] = -1;
+    if (s < lim) {
+      const int32_t kept = km[b * kms_b + h * kms_h + s * kms_s];
+      const int64_t d = im[b * ims_b + h * ims_h + s * ims_s];
+      // out-of-range destinations are dropped, not written
+      if (kept == 1 && d >= 0 && d < num_packed) dst[t] = d;
+    }
   }
-  if (lane == 0) ts[b * tss_b + h * tss_h + dst * tss_a] = static_cast<int32_t>(s);
+  if (vec) {
+    constexpr int MAXP = 2;  // 16-byte pieces per lane and row (rows up to 256 bytes; wider rows copy by element)
+    const int64_t pieces = head_dim * static_cast<int64_t>(sizeof(T)) / 16;
+    if (pieces <= 8 * MAXP) {
+      uint4 kx[SP_TPG][MAXP], vx[SP_TPG][MAXP];
+#pragma unroll
+      for (int t = 0; t < SP_TPG; ++t) {
+        if (dst[t] < 0) continue;
+        const uint4* kr = reinterpret_cast<const uint4*>(k + b * ks_b + h * ks_h + (s0 + t) * ks_s);
+        const uint4* vr = reinterpret_cast<const uint4*>(v + b * vs_b + h * vs_h + (s0 + t) * vs_s);
+#pragma unroll
+        for (int j = 0; j < MAXP; ++j) {
+          const int64_t c = lane8 + 8 * j;
+          if (c < pieces) {
+            kx[t][j] = kr[c];
+            vx[t][j] = vr[c];
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < SP_TPG; ++t) {
+        if (dst[t] < 0) continue;
+        uint4* kd = reinterpret_cast<uint4*>(kp + b * kps_b + h * kps_h + dst[t] * kps_a);
+        uint4* vd = reinterpret_cast<uint4*>(vp + b * vps_b + h * vps_h + dst[t] * vps_a);
+#pragma unroll
+        for (int j = 0; j < MAXP; ++j) {
+          const int64_t c = lane8 + 8 * j;
+          if (c < pieces) {
+            kd[c] = kx[t][j];
+            vd[c] = vx[t][j];
+          }
+        }
+        if (lane8 == 0) ts[b * tss_b + h * tss_h + dst[t] * tss_a] = static_cast<int32_t>(s0 + t);
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < SP_TPG; ++t) {
+    if (dst[t] < 0) continue;
+    const int64_t s = s0 + t;
+    const T* krow = k + b * ks_b + h * ks_h + s * ks_s;
+    const T* vrow = v + b * vs_b + h * vs_h + s * vs_s;
+    T* kdst = kp + b * kps_b + h * kps_h + dst[t] * kps_a;
+    T* vdst = vp + b * vps_b + h * vps_h + dst[t] * vps_a;
+    for (int64_t d = lane8; d < head_dim; d += 8) {
+      kdst[d * kps_d] = krow[d * ks_d];
+      vdst[d * vps_d] = vrow[d * vs_d];
+    }
+    if (lane8 == 0) ts[b * tss_b + h * tss_h + dst[t] * tss_a] = static_cast<int32_t>(s);
+  }
 }
+
 
 cudaError_t launch_scatter_pack(int dtype, const void* k, const void* v, void* kp, void* vp, int32_t* ts,
                                 const int32_t* km, const int32_t* im, const int64_t* ks, const int64_t* vs,
@@ -475,13 +533,21 @@ cudaError_t launch_scatter_pack(int dtype, const void* k, const void* v, void* k
                                 int64_t grid_bh, int64_t rows_covered, int64_t num_packed, cudaStream_t st) {
   if (grid_bh <= 0 || rows_covered <= 0 || seq_len <= 0) return cudaSuccess;
   const int64_t rows = rows_covered < seq_len ? rows_covered : seq_len;
-  dim3 grid(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(grid_bh));
+  constexpr int64_t per_cta = 32 * SP_TPG;  // 32 eight-lane groups per CTA
+  dim3 grid(static_cast<unsigned>((rows + per_cta - 1) / per_cta), static_cast<unsigned>(grid_bh));
+  const int64_t esz = dtype == F32 ? 4 : 2;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  auto rows16 = [&](const int64_t* st3) { return (st3[0] * esz) % 16 == 0 && (st3[1] * esz) % 16 == 0 &&
+                                                 (st3[2] * esz) % 16 == 0; };
+  const bool vec = ks[3] == 1 && vs[3] == 1 && kps[3] == 1 && vps[3] == 1 && (head_dim * esz) % 16 == 0 &&
+                   al16(k) && al16(v) && al16(kp) && al16(vp) && rows16(ks) && rows16(vs) && rows16(kps) &&
+                   rows16(vps);
 #define DAB_SP(TY)                                                                                           \
   scatter_pack_kernel<TY><<<grid, 256, 0, st>>>(                                                             \
       static_cast<const TY*>(k), nullptr, static_cast<const TY*>(v), static_cast<TY*>(kp),                   \
       static_cast<TY*>(vp), ts, km, im, ks[0], ks[1], ks[2], ks[3], vs[0], vs[1], vs[2], vs[3], kps[0],      \
       kps[1], kps[2], kps[3], vps[0], vps[1], vps[2], vps[3], tss[0], tss[1], tss[2], kms[0], kms[1], kms[2], \
-      ims[0], ims[1], ims[2], seq_len, head_dim, num_heads, rows_covered, num_packed);                       \
+      ims[0], ims[1], ims[2], seq_len, head_dim, num_heads, rows_covered, num_packed, vec);                  \
   return cudaGetLastError();
   switch (dtype) {
     case F32: DAB_SP(float)

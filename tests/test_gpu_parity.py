@@ -184,6 +184,39 @@ def test_scatter_pack_matches_reference(golden):
     np.testing.assert_array_equal(ts.cpu().numpy(), g["timestamps"])
 
 
+@pytest.mark.parametrize("dt,D,layout", [(torch.bfloat16, 128, "bhsd"), (torch.float16, 96, "bshd"),
+                                          (torch.bfloat16, 100, "bhsd"), (torch.float16, 64, "dstride")])
+def test_scatter_pack_layouts_match_oracle(dt, D, layout):
+    """The reference-facing scatter pack on 16-byte row copies (unit head-dim strides,
+    aligned rows) and element copies (200-byte rows, strided head dim): packed K / V and
+    timestamps equal the oracle's packing of the same keep mask."""
+    import tritonModules as tm
+    B, H, N = 1, 3, 1500
+    k = torch.from_numpy(I.normal((B, H, N, D), seed=7)).to(dt)
+    v = torch.from_numpy(I.normal((B, H, N, D), seed=8)).to(dt)
+    keep = O.periodic_keep_mask(B, H, N, 0.3).clone()
+    keep[:, :, 7::11] = 1
+    _, kp_ref, vp_ref, ts_ref, _ = O.pack_from_keep(k, v, keep)
+    if layout == "bshd":
+        kc, vc = (t.transpose(1, 2).contiguous().cuda().transpose(1, 2) for t in (k, v))
+    elif layout == "dstride":
+        kc, vc = (t.transpose(2, 3).contiguous().cuda().transpose(2, 3) for t in (k, v))
+    else:
+        kc, vc = k.cuda(), v.cuda()
+    km = keep.cuda()
+    im = (torch.cumsum(km, -1) - 1).to(torch.int32)
+    M = int(keep.sum(-1).max())
+    kp = torch.zeros((B, H, M, D), dtype=dt, device="cuda")
+    vp = torch.zeros_like(kp)
+    ts = torch.zeros((B, H, M), dtype=torch.int32, device="cuda")
+    tm.parallel_scatter_pack_kv_kernel[(B * H, -(-N // 64))](
+        kc, vc, kp, vp, ts, km, im, *kc.stride(), *vc.stride(), *kp.stride(), *vp.stride(), *ts.stride(),
+        *km.stride(), *im.stride(), N, D, H, BLOCK_S=64, BLOCK_D=1 << (D - 1).bit_length())
+    assert torch.equal(kp.cpu().view(torch.int16), kp_ref.view(torch.int16))
+    assert torch.equal(vp.cpu().view(torch.int16), vp_ref.view(torch.int16))
+    assert torch.equal(ts.cpu(), ts_ref)
+
+
 def test_device_pack_from_keep_matches_reference(golden):
     from deltaattention_b200 import ops
     g = golden("pack_fp32")
