@@ -57,9 +57,12 @@ def _shim_and_import(ref_root: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("DELTA_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("DELTA_REFERENCE"),
+                    help="checkout of the reference project (or set DELTA_REFERENCE)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("pass --reference <reference checkout> (or set DELTA_REFERENCE)")
     import torch
     import triton
     import triton.language as tl  # noqa: F401  (annotation namespace of _sub_kernel)

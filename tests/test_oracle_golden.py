@@ -166,8 +166,9 @@ def test_decode_replay_matches_reference(golden, name, dt, use_cos):
     assert (grew > 0).any() and (grew < st["steps"]).any()
 
 
-def test_tile_counts_match_survey_table():
-    # tiles per head under the reference schedule, periodic packing, W=128
+def test_tile_counts_match_reference_schedule():
+    # tiles per head under the reference schedule (deltaFlashAttention.py:63-111 semantics),
+    # periodic packing, W=128
     assert O.tile_count(2048, 4) == 84
     assert O.tile_count(8192, 1) == 2080
     assert O.tile_count(8192, 4) == 744
