@@ -618,16 +618,17 @@ def test_decode_attention_16bit_matches_oracle(dt, D, G, B, Hkv):
     _check_ws_clean()
 
 
-def _device_cache_setup(layers, seed):
+def _device_cache_setup(layers, seed, dt=torch.bfloat16, D=128):
     """A prefilled DeviceDecodeCache plus the same state as plain tensors for the host-length
     launches of the reference API."""
     from deltaattention_b200.cache import DeviceDecodeCache
     g = torch.Generator().manual_seed(seed)
-    B, Hkv, G, D, W, N0, cap, thr = 2, 2, 4, 128, 16, 240, 160, 8.0
-    c = DeviceDecodeCache(layers, B, Hkv, D, cap, W, torch.bfloat16, threshold=thr)
+    B, Hkv, G, W, N0, cap = 2, 2, 4, 16, 240, 160
+    thr = 8.0 * (D / 128) ** 0.5  # window keys merge into the last anchor, fresh tokens append
+    c = DeviceDecodeCache(layers, B, Hkv, D, cap, W, dt, threshold=thr)
     for layer in range(layers):
-        keys = torch.from_numpy(I.ar1_keys(B, Hkv, N0, D, seed=seed + layer)).bfloat16()
-        vals = (torch.randn((B, Hkv, N0, D), generator=g) * 0.5).bfloat16()
+        keys = torch.from_numpy(I.ar1_keys(B, Hkv, N0, D, seed=seed + layer)).to(dt)
+        vals = (torch.randn((B, Hkv, N0, D), generator=g) * 0.5).to(dt)
         keep = O.periodic_keep_mask(B, Hkv, N0 - W, 0.25)
         _, kp, vp, ts, counts = O.pack_from_keep(keys[:, :, :N0 - W], vals[:, :, :N0 - W], keep)
         c.load_prefill(layer, kp.cuda(), vp.cuda(), counts.cuda(), ts.cuda(), keys[:, :, N0 - W:].cuda(),
@@ -637,9 +638,9 @@ def _device_cache_setup(layers, seed):
                 v_exact=c.v_exact.clone(), exact=[W] * layers, total=[N0] * layers)
     steps = []
     for _ in range(24):
-        steps.append(((torch.randn((layers, B, Hkv * G, D), generator=g) * 0.5).bfloat16().cuda(),
-                      (torch.randn((layers, B, Hkv, 1, D), generator=g) * 0.5).bfloat16().cuda(),
-                      (torch.randn((layers, B, Hkv, 1, D), generator=g) * 0.5).bfloat16().cuda()))
+        steps.append(((torch.randn((layers, B, Hkv * G, D), generator=g) * 0.5).to(dt).cuda(),
+                      (torch.randn((layers, B, Hkv, 1, D), generator=g) * 0.5).to(dt).cuda(),
+                      (torch.randn((layers, B, Hkv, 1, D), generator=g) * 0.5).to(dt).cuda()))
     return c, host, steps, dict(B=B, Hkv=Hkv, G=G, D=D, W=W, thr=thr)
 
 
@@ -663,12 +664,13 @@ def _host_length_step(host, layer, q, k_new, v_new, p):
     return out
 
 
-def test_device_decode_cache_matches_host_lengths():
-    """DeviceDecodeCache (lengths on the device, advanced by a kernel) gives bit-identical
+@pytest.mark.parametrize("dt,D", [(torch.bfloat16, 128), (torch.float16, 64)])
+def test_device_decode_cache_matches_host_lengths(dt, D):
+    """DeviceDecodeCache (lengths on the device, advanced on the device) gives bit-identical
     outputs and cache contents to the reference-API launches with host lengths, over steps
     that both merge into and append to the packed history."""
     layers = 2
-    c, host, steps, p = _device_cache_setup(layers, seed=61)
+    c, host, steps, p = _device_cache_setup(layers, seed=61, dt=dt, D=D)
     for q, kn, vn in steps:
         for layer in range(layers):
             got = c.step(layer, q[layer], kn[layer], vn[layer])
@@ -705,12 +707,13 @@ def test_device_decode_cache_folded_advance_equals_separate():
     _check_ws_clean()
 
 
-def test_device_decode_cache_graph_replay():
+@pytest.mark.parametrize("dt,D", [(torch.bfloat16, 128), (torch.float16, 64)])
+def test_device_decode_cache_graph_replay(dt, D):
     """A decode step over every layer captured once in a CUDA graph and replayed per token
     equals the eager steps token by token."""
     layers = 2
-    eager, _, steps, _ = _device_cache_setup(layers, seed=62)
-    graphed, _, _, _ = _device_cache_setup(layers, seed=62)
+    eager, _, steps, _ = _device_cache_setup(layers, seed=62, dt=dt, D=D)
+    graphed, _, _, _ = _device_cache_setup(layers, seed=62, dt=dt, D=D)
     q0, k0, v0 = steps[0]
     for layer in range(layers):  # one eager step on both (kernel attributes are set outside capture)
         eager.step(layer, q0[layer], k0[layer], v0[layer])
