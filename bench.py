@@ -604,6 +604,20 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize()
         variants[name] = {"ms": max_over_ranks(d0.elapsed_time(d1) / nd, world)}
     del q_rot, k_rot, pk
+    # the reference's threshold ("row" delta) mode as a whole layer-op: RoPE, delta scan,
+    # device packing (with the one packed-length read-back modeling_llama.py:656 also makes)
+    # and the two-phase attention; raw Euclidean threshold 11 keeps about 1 key in 4 here
+    for _ in range(2):
+        ops.delta_prefill(q, k, v, cos, sin, mode="delta", threshold=11.0, dense_window=W)
+    torch.cuda.synchronize()
+    d0.record(stream)
+    for _ in range(nd):
+        ops.delta_prefill(q, k, v, cos, sin, mode="delta", threshold=11.0, dense_window=W)
+    d1.record(stream)
+    torch.cuda.synchronize()
+    delta_ms = max_over_ranks(d0.elapsed_time(d1) / nd, world)
+    delta_mode = {"ms_per_layer_op": delta_ms, "tokens_per_s": B * N * world / (delta_ms / 1000.0),
+                  "threshold": 11.0, "selection": "Euclidean delta scan, chunk 512"}
 
     # end to end through the public API: pinned host inputs (head-major [B, H, N, d]) -> device
     # -> pinned host output; ops.delta_prefill_host overlaps each kv-head group's copies with
@@ -658,6 +672,7 @@ def run_ours(args, world, rank, local):
                              "d2h": ho.numel() * 2 / (e2e_ms / 1000.0) / 1e9}},
         "dense_r1": {"ms_per_step": dense_ms, "speedup_of_delta_attention": dense_ms / attn_ms},
         "variants": variants,
+        "delta_mode": delta_mode,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }
