@@ -420,6 +420,24 @@ def test_native_gqa_prefill_matches_oracle(mode):
     _check_ws_clean()
 
 
+@pytest.mark.parametrize("threshold", [8.0, 11.0, 14.0])
+def test_delta_mode_tc_matches_simt(threshold):
+    """Threshold-selected anchors carry different run-length counts within a block (the
+    tcgen05 kernel's per-key-count path); it agrees with the CUDA-core kernel within the bf16
+    tolerance at N=4096, GQA 4:1."""
+    from deltaattention_b200 import ops, synth
+    B, Hq, Hkv, N, D = 1, 8, 2, 4096, 128
+    q, k, v = synth.layer_inputs(B, Hq, Hkv, N, D, torch.bfloat16, seed=33, device="cuda")
+    cos, sin = synth.rope_tables(N, D, 5e5, torch.bfloat16, device="cuda")
+    out, packed, k_rot = ops.delta_prefill(q, k, v, cos, sin, mode="delta", threshold=threshold, return_packed=True)
+    c = packed.counts
+    assert (c[:, :, :128].amax(-1) != c[:, :, :128].amin(-1)).any(), "counts should differ within a block"
+    q_rot = ops.rope(q, cos, sin)
+    ref = ops.attention(q_rot, k_rot, v, packed, force_simt=True)
+    _cmp(out, ref, torch.bfloat16, f"delta tc vs simt, threshold {threshold}")
+    _check_ws_clean()
+
+
 @pytest.mark.parametrize("B,group,qgroup", [(2, 1, None), (1, 2, None), (1, 3, None), (2, 1, 1), (1, 1, 2)])
 def test_host_pipelined_prefill_equals_device_call(B, group, qgroup):
     """ops.delta_prefill_host (kv-head groups, copies overlapped with compute on three streams)
