@@ -240,7 +240,7 @@ def delta_prefill_varlen(q, k, v, cos, sin, cu_seqlens, *, selection="nm", n=2, 
     list of per-sequence (Packed, post-RoPE keys) for the decode-cache hand-off.
     """
     from .dropin.nmDeltaFlashAttention import nm_keep_mask, nm_num_packed
-    L.require_cuda(q, k, v, cos, sin, out)
+    # argument checks first (host logic only), then the device requirement
     if q.shape[0] != 1 or k.shape[0] != 1:
         raise ValueError("delta_prefill_varlen: sequences are packed along dim 2 of [1, H, T, d] tensors")
     cu = [int(x) for x in cu_seqlens]
@@ -251,6 +251,7 @@ def delta_prefill_varlen(q, k, v, cos, sin, cu_seqlens, *, selection="nm", n=2, 
         raise ValueError("delta_prefill_varlen: cos / sin are shorter than the longest sequence")
     if selection not in ("nm", "periodic"):
         raise ValueError(f"delta_prefill_varlen: unknown selection {selection}")
+    L.require_cuda(q, k, v, cos, sin, out)
     dev = q.device
     if out is None:
         out = torch.empty((1, q.shape[1], T, q.shape[3]), dtype=q.dtype, device=dev)

@@ -146,3 +146,24 @@ def test_bench_max_over_ranks_gloo_world2():
         p.join(120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert dict(out) == {0: 2.5, 1: 2.5}
+
+
+@pytest.mark.parametrize("cu,msg", [([0, 100, 100, 300], "rise strictly"), ([0, 150, 299], "rise strictly"),
+                                    ([5, 300], "rise strictly"), ([0, 300], "shorter than the longest")])
+def test_varlen_prefill_rejects_bad_offsets(cu, msg):
+    """delta_prefill_varlen checks cu_seqlens (strictly rising from 0 to the packed length) and
+    the RoPE table length on the host, before any device work."""
+    from deltaattention_b200 import ops
+    q = torch.zeros((1, 4, 300, 64), dtype=torch.bfloat16)
+    k = torch.zeros((1, 2, 300, 64), dtype=torch.bfloat16)
+    cos = torch.zeros((1, 256, 64), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match=msg):
+        ops.delta_prefill_varlen(q, k, k, cos, cos, cu)
+
+
+def test_varlen_prefill_rejects_unknown_selection():
+    from deltaattention_b200 import ops
+    q = torch.zeros((1, 4, 300, 64), dtype=torch.bfloat16)
+    cos = torch.zeros((1, 512, 64), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="unknown selection"):
+        ops.delta_prefill_varlen(q, q, q, cos, cos, [0, 300], selection="delta")
