@@ -34,7 +34,8 @@ __global__ void __launch_bounds__(128) decode_update_kernel(
   const int g = lane & 7;
   const int64_t pid = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (pid >= programs) return;
-  const int64_t b = pid / num_heads, h = pid % num_heads;
+  const int pb = static_cast<int>(pid) / static_cast<int>(num_heads);  // 32-bit: pid < programs << 2^31
+  const int64_t b = pb, h = static_cast<int>(pid) - pb * static_cast<int>(num_heads);
   const int64_t w = exact_seq_len % W;
   T* ek = ke + b * es_b + h * es_h + w * es_s;
   T* ev = ve + b * es_b + h * es_h + w * es_s;
@@ -216,7 +217,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t chunk = blockIdx.x;
   const int64_t bk = blockIdx.y;
-  const int64_t b = bk / Hkv, hk = bk % Hkv;
+  const int b32 = static_cast<int>(bk) / static_cast<int>(Hkv);  // 32-bit: grid y extent << 2^31
+  const int64_t b = b32, hk = static_cast<int>(bk) - b32 * static_cast<int>(Hkv);
   const int64_t plen = lengths[b * ls_b + hk * ls_h];
   const int64_t total = plen + exact_len;
   const int64_t k0 = chunk * DEC_KC;
@@ -323,10 +325,11 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
   float* sl = cmb + nchunk;
   __shared__ float red[4];
   __shared__ float2 wsum[4][BD / 2];
-  const int64_t bh = blockIdx.x;  // (b, q-head)
-  const int64_t Hq = Hkv * G;
-  const int64_t b = bh / Hq, h = bh % Hq;
-  const int64_t hk = h / G, g = h % G;
+  // 32-bit division (grid extent and head counts are far below 2^31)
+  const int hq32 = static_cast<int>(Hkv * G), g32 = static_cast<int>(G);
+  const int b32 = static_cast<int>(blockIdx.x) / hq32, h32 = static_cast<int>(blockIdx.x) - b32 * hq32;
+  const int hk32 = h32 / g32;
+  const int64_t b = b32, h = h32, hk = hk32, g = h32 - hk32 * g32;
   const int64_t bk = b * Hkv + hk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* base = part + (bk * nchunk * G + g) * (BD + 2);
@@ -499,7 +502,9 @@ __global__ void __launch_bounds__(DEC_NW * 32, 5) decode_attn_mma_kernel(
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t chunk = blockIdx.x;
   const int64_t bk = blockIdx.y;
-  const int64_t b = bk / Hkv, hk = bk % Hkv;
+  // 32-bit division (the grid's y extent and the head count are far below 2^31)
+  const int b32 = static_cast<int>(blockIdx.y) / static_cast<int>(Hkv);
+  const int64_t b = b32, hk = static_cast<int>(blockIdx.y) - b32 * static_cast<int>(Hkv);
   const int64_t plen = lengths[b * ls_b + hk * ls_h];
   const int64_t total = plen + exact_len;
   const int64_t k0 = chunk * DEC_VKC;

@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(256) chunked_eval_kernel(
   const int64_t chunk = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 3) + (threadIdx.x >> 3);
   const int64_t bh = blockIdx.y;
   if (chunk >= grid_chunks || bh >= grid_bh) return;
-  const int64_t b = bh / num_heads, h = bh % num_heads;
+  const int64_t b = static_cast<int>(bh) / static_cast<int>(num_heads), h = bh - b * num_heads;  // bh: a grid index
   const int64_t start = chunk * chunk_size;
   if (start >= seq_len) return;
   const int64_t end = min(start + chunk_size, seq_len);
@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(spec_warps<T, BD>() * 32) delta_scan_spec_kern
   const int q = lane & 3;   // its accumulators: 2q and 2q + 1
   const int64_t chunk = static_cast<int64_t>(blockIdx.x) * spec_warps<T, BD>() + (threadIdx.x >> 5);
   const int64_t bh = blockIdx.y;
-  const int64_t b = bh / num_heads, h = bh % num_heads;
+  const int64_t b = static_cast<int>(bh) / static_cast<int>(num_heads), h = bh - b * num_heads;  // bh: a grid index
   const int64_t start = chunk * chunk_size;
   if (chunk >= num_chunks || start >= seq_len) return;  // whole warps leave; no CTA-wide barrier follows
   const int n = static_cast<int>(min(chunk_size, seq_len - start));
@@ -459,7 +459,7 @@ __global__ void __launch_bounds__(256) scatter_pack_kernel(
   const int64_t bh = blockIdx.y;
   const int64_t lim = seq_len < rows_covered ? seq_len : rows_covered;
   if (s0 >= lim) return;
-  const int64_t b = bh / num_heads, h = bh % num_heads;
+  const int64_t b = static_cast<int>(bh) / static_cast<int>(num_heads), h = bh - b * num_heads;  // bh: a grid index
   int64_t dst[SP_TPG];
 #pragma unroll
   for (int t = 0; t < SP_TPG; ++t) {
@@ -741,7 +741,7 @@ __global__ void __launch_bounds__(PACK_TILE) keep_tile_count_kernel(const int32_
                                                                     int64_t H, int64_t N, int32_t* tile_cnt,
                                                                     int32_t* tile_first, int64_t ntile) {
   const int64_t bh = blockIdx.y, t = blockIdx.x;
-  const int64_t b = bh / H, h = bh % H;
+  const int64_t b = static_cast<int>(bh) / static_cast<int>(H), h = bh - b * H;  // bh: a grid index
   const int64_t s = t * PACK_TILE + threadIdx.x;
   const int kv = (s < N) ? (keep[b * kb + h * kh + s * ks] == 1) : 0;
   const int c = __syncthreads_count(kv);
@@ -791,7 +791,7 @@ __global__ void __launch_bounds__(PACK_TILE) keep_pack_kernel(
   __shared__ int32_t pos_of[PACK_TILE];
   __shared__ int32_t total;
   const int64_t bh = blockIdx.y, t = blockIdx.x;
-  const int64_t b = bh / H, h = bh % H;
+  const int64_t b = static_cast<int>(bh) / static_cast<int>(H), h = bh - b * H;  // bh: a grid index
   const int64_t s = t * PACK_TILE + threadIdx.x;
   const int kv = (s < N) ? (keep[b * kb + h * kh + s * ks] == 1) : 0;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -885,7 +885,7 @@ __global__ void __launch_bounds__(256) pack_pad_kernel(T* __restrict__ kp, T* __
                                                        const int32_t* __restrict__ anchors, int64_t H, int64_t D,
                                                        int64_t capacity, int vec16) {
   const int64_t bh = blockIdx.y;
-  const int64_t b = bh / H, h = bh % H;
+  const int64_t b = static_cast<int>(bh) / static_cast<int>(H), h = bh - b * H;  // bh: a grid index
   const int64_t j0 = anchors[bh] + static_cast<int64_t>(blockIdx.x) * 32;
   if (j0 >= capacity) return;
   const int64_t rows = (capacity - j0) < 32 ? (capacity - j0) : 32;
@@ -967,7 +967,7 @@ __global__ void __launch_bounds__(128) nm_select_kernel(const T* __restrict__ x,
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t bh = blockIdx.y;
   if (gid >= groups) return;
-  const int64_t b = bh / H, h = bh % H;
+  const int64_t b = static_cast<int>(bh) / static_cast<int>(H), h = bh - b * H;  // bh: a grid index
   const T* base = x + b * xb + h * xh;
   int32_t* kr = keep + b * kb + h * kh;
   const int64_t G = (N + c - 1) / c;  // candidates
@@ -1038,7 +1038,7 @@ __global__ void __launch_bounds__(128) nm_select_staged_kernel(const T* __restri
   const int64_t g0 = static_cast<int64_t>(blockIdx.x) * gpc;
   const int64_t bh = blockIdx.y;
   if (g0 >= groups) return;
-  const int64_t b = bh / H, h = bh % H;
+  const int64_t b = static_cast<int>(bh) / static_cast<int>(H), h = bh - b * H;  // bh: a grid index
   const int64_t G = (N + c - 1) / c;  // candidates of the head
   const int64_t i0 = g0 * m_group;
   const int cn = static_cast<int>(min(static_cast<int64_t>(gpc) * m_group, G - i0));  // candidates here
