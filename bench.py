@@ -2,11 +2,16 @@
 
 A step is one pass of the hot path over one layer of synthetic input: RoPE on q and k,
 periodic r=4 packing (timestamps / counts; packed K/V are strided views) and the two-phase
-count-weighted tcgen05 attention for B=1, Hq=32, Hkv=8, N=32768, d=128, bf16. Each rank
-processes its own sequence (weak scaling, no collective on the data path). Inputs (q 256
-MiB + k, v 64 MiB each) exceed the 126 MB L2, so no explicit flush is needed between steps.
+count-weighted tcgen05 attention for B=1, Hq=32, Hkv=8, N=32768, d=128, bf16.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+On N GPUs (torchrun, one rank per GPU) the one sequence is partitioned by kv-head, as the
+(batch, kv-head) units of the path are independent: each rank runs Hkv/N kv-heads with their
+query heads over the whole sequence, with no collective on the data path (strong scaling:
+the job's work is fixed). ``--shard seq`` instead gives every rank a sequence of its own
+(weak scaling). Per-GPU inputs larger than the 126 MB L2 need no flush between steps;
+smaller ones (4 and 8 GPUs) get a 256 MiB L2 flush between steps, outside the timed events.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--shard heads|seq]
 
 Prints ONE JSON line (rank 0). ``--impl reference`` times the CPU restatement of the
 reference's path (the oracle port) on this host's cores on a bounded sample of the same
@@ -34,12 +39,19 @@ UNIT = "tokens/s"
 CFG = dict(B=1, Hq=32, Hkv=8, N=32768, D=128, r=4, W=128, theta=5e5)
 
 
-def workload_config(n_gpus):
+def workload_config(n_gpus, shard="heads", flushed=False):
+    if shard == "heads":
+        par = (f"kv-head shard: {CFG['Hkv'] // n_gpus} kv-heads ({CFG['Hq'] // n_gpus} q-heads) of one sequence "
+               f"per GPU, no data-path collective")
+        gb = CFG["B"]
+    else:
+        par = f"dp{n_gpus} (one sequence per GPU, no data-path collective)"
+        gb = CFG["B"] * n_gpus
     return {"workload": "cfg2: RoPE(q,k) + periodic r=4 packing + two-phase delta attention, one layer",
-            "B_per_gpu": CFG["B"], "Hq": CFG["Hq"], "Hkv": CFG["Hkv"], "N": CFG["N"], "d": CFG["D"],
-            "r": CFG["r"], "dense_window": CFG["W"], "global_batch": CFG["B"] * n_gpus,
-            "parallelism": f"dp{n_gpus} (one sequence per GPU, no data-path collective)",
-            "l2": "inputs (384 MiB per step) larger than L2; no flush"}
+            "B": CFG["B"], "Hq": CFG["Hq"], "Hkv": CFG["Hkv"], "N": CFG["N"], "d": CFG["D"],
+            "r": CFG["r"], "dense_window": CFG["W"], "global_batch": gb, "parallelism": par,
+            "l2": ("per-GPU inputs smaller than 1.5x L2: 256 MiB L2 flush between timed steps (outside the "
+                   "per-step events)") if flushed else "per-GPU inputs larger than L2; no flush"}
 
 
 def peaks():
@@ -378,18 +390,64 @@ def traffic_per_launch():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock, power and clock-event reasons sampled DURING the timed region.
 
+    NVML is polled every `period_s` (2 ms) from a background thread, so a timed region of a
+    few tens of milliseconds still gets ten or more samples; ``nvidia-smi -lms 200`` is the
+    fallback when NVML cannot be loaded. GPUs are matched to NVML by UUID (the CUDA ordinals
+    of `gpus`), so CUDA_VISIBLE_DEVICES remapping does not confuse them."""
+
+    REASONS = (("sw_power_cap", 0x4), ("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
+               ("hw_thermal_slowdown", 0x40), ("hw_power_brake_slowdown", 0x80))
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpus):
-        self.gpus = set(gpus)
+    def __init__(self, gpus, period_s=0.002):
+        self.gpus = list(gpus)
+        self.period = period_s
+        self.samples = []  # (sm_mhz, max_mhz, power_w, reasons bitmask)
         self.proc = None
+        self.thread = None
+        self.nvml = None
         self.path = os.path.join("/tmp", f"dab_clocks_{os.getpid()}.csv")
 
+    def _handles(self):
+        import pynvml
+        pynvml.nvmlInit()
+        hs = []
+        for i in self.gpus:
+            try:
+                uid = str(torch.cuda.get_device_properties(i).uuid)
+                hs.append(pynvml.nvmlDeviceGetHandleByUUID(uid if uid.startswith("GPU-") else "GPU-" + uid))
+            except Exception:
+                hs.append(pynvml.nvmlDeviceGetHandleByIndex(i))
+        return pynvml, hs
+
+    def _poll(self, pynvml, hs):
+        while not self.stop:
+            for h in hs:
+                try:
+                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((float(sm), float(mx), pw, int(rs)))
+                except Exception:
+                    pass
+            time.sleep(self.period)
+
     def __enter__(self):
+        self.stop = False
+        try:
+            import threading
+            pynvml, hs = self._handles()
+            self.nvml = pynvml
+            self.thread = threading.Thread(target=self._poll, args=(pynvml, hs), daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
@@ -399,6 +457,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
+        self.stop = True
+        if self.thread is not None:
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -408,26 +469,53 @@ class ClockSampler:
             self.fh.close()
 
     def summary(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         sm, mx, reasons = [], [], set()
-        try:
-            for line in open(self.path):
-                f = [x.strip() for x in line.split(",")]
-                if len(f) < 9 or not f[0].isdigit() or int(f[0]) not in self.gpus:
-                    continue
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
-                for name, val in zip(["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"],
-                                     f[5:9]):
-                    if val.lower().startswith("active"):
+        src = "nvml (2 ms)"
+        if self.nvml is not None:
+            for s, m, _, rs in self.samples:
+                sm.append(s)
+                mx.append(m)
+                for name, bit in self.REASONS:
+                    if rs & bit:
                         reasons.add(name)
-        except Exception:
-            pass
+        elif self.proc is not None:
+            src = "nvidia-smi (200 ms)"
+            try:
+                for line in open(self.path):
+                    f = [x.strip() for x in line.split(",")]
+                    if len(f) < 9 or not f[0].isdigit() or int(f[0]) not in self.gpus:
+                        continue
+                    sm.append(float(f[1]))
+                    mx.append(float(f[2]))
+                    for name, val in zip(["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                                          "sw_power_cap"], f[5:9]):
+                        if val.lower().startswith("active"):
+                            reasons.add(name)
+            except Exception:
+                pass
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"]}
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "source": src}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "sm_mhz_min": min(sm),
+                "reasons": sorted(reasons), "samples": len(sm), "source": src}
+
+
+def pick_peak(clocks, timed_s):
+    """The roofline denominator for the attention launch: the burst bf16 figure when the timed
+    region ran at (>= 95% of) the maximum SM clock, or was too short to sample and under a second
+    (the burst figure is measured at that clock), else the sustained power-capped figure."""
+    burst, sustained, src = peaks()
+    sm, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    if sm and mx:
+        at_max = sm >= 0.95 * mx
+        why = f"median SM clock {sm:.0f} of max {mx:.0f} MHz over the timed region ({timed_s * 1e3:.0f} ms)"
+    else:
+        at_max = timed_s < 1.0
+        why = f"no clock samples; timed region {timed_s * 1e3:.0f} ms"
+    if at_max:
+        return burst, f"{src} bf16 burst ({why}); sustained {sustained}", sustained
+    return sustained, f"{src} bf16 sustained ({why}); burst {burst}", burst
 
 
 def dist_setup():
@@ -465,22 +553,37 @@ def max_over_ranks(x, world):
 _CPU_INPUTS = {}
 
 
-def cpu_sample(heads=(0,), stride=1, N=CFG["N"]):
-    """Oracle (CPU restatement of the reference path) on q-heads `heads` of one cfg2 layer,
-    attention restricted to every `stride`-th 128-row query block.
-
-    Returns (seconds, tokens-equivalent): the sample's share of one layer's N tokens."""
+def _cpu_inputs(N):
     from deltaattention_b200 import synth
-    from oracle import delta_oracle as O
     if N not in _CPU_INPUTS:
         q, k, v = synth.layer_inputs(1, CFG["Hq"], CFG["Hkv"], N, CFG["D"], torch.bfloat16, seed=0, device="cpu")
         _CPU_INPUTS[N] = (q, k, v) + synth.rope_tables(N, CFG["D"], CFG["theta"], torch.bfloat16)
-    q, k, v, cos, sin = _CPU_INPUTS[N]
-    kv_heads = sorted({h // (CFG["Hq"] // CFG["Hkv"]) for h in heads})
+    return _CPU_INPUTS[N]
+
+
+def cpu_sample(heads=(0, 1, 2, 3), stride=1, N=CFG["N"]):
+    """Oracle (CPU restatement of the reference path) on q-heads `heads` of one cfg2 layer:
+    RoPE of the sampled query rows and of the heads' kv-heads, periodic packing, and the
+    two-phase attention on every `stride`-th 128-row query block.
+
+    `heads` should be whole GQA groups (the default is kv-head 0's four q-heads), so the
+    kv-head's RoPE and packing are charged to all of its query heads. Returns (seconds,
+    tokens-equivalent): the sample's share of one layer's N tokens."""
+    from oracle import delta_oracle as O
+    q, k, v, cos, sin = _cpu_inputs(N)
+    G = CFG["Hq"] // CFG["Hkv"]
+    kv_heads = sorted({h // G for h in heads})
     nmb = -(-N // 128)
     blocks = list(range(0, nmb, stride))
     t0 = time.perf_counter()
-    q_ref = O.apply_rope(q[:, list(heads)].contiguous(), cos, sin)
+    qs = q[:, list(heads)].contiguous()
+    if stride == 1:
+        q_ref = O.apply_rope(qs, cos, sin)
+    else:  # only the sampled rows' RoPE is charged (the other rows are zeros, not attended)
+        q_ref = torch.zeros_like(qs)
+        for b_ in blocks:
+            sl = slice(128 * b_, min(N, 128 * b_ + 128))
+            q_ref[:, :, sl] = O.apply_rope(qs[:, :, sl], cos[:, sl], sin[:, sl])
     k_ref = O.apply_rope(k[:, kv_heads].contiguous(), cos, sin)
     vv = v[:, kv_heads].contiguous()
     keep = O.periodic_keep_mask(1, len(kv_heads), N, 1.0 / CFG["r"])
@@ -492,17 +595,44 @@ def cpu_sample(heads=(0,), stride=1, N=CFG["N"]):
     return dt, 128 * len(blocks) * len(heads) / CFG["Hq"]
 
 
+def cpu_eager_dense_sample(heads=(0, 1, 2, 3), blocks=8, N=CFG["N"]):
+    """The reference's eager dense attention (eager_attention_forward, modeling_llama.py:235-276:
+    QK^T over all N keys, causal mask, fp32 softmax, PV) on CPU: the r = 1 CPU point.
+
+    Runs `blocks` 128-row query blocks spread evenly over the sequence for q-heads `heads`
+    (eager attention costs the same N keys per row at every position). Returns (seconds,
+    tokens-equivalent)."""
+    from oracle import delta_oracle as O
+    q, k, v, cos, sin = _cpu_inputs(N)
+    G = CFG["Hq"] // CFG["Hkv"]
+    kv_heads = sorted({h // G for h in heads})
+    k_ref = O.apply_rope(k[:, kv_heads].contiguous(), cos, sin)
+    vv = v[:, kv_heads].contiguous()
+    nmb = -(-N // 128)
+    picks = sorted({min(nmb - 1, (i * nmb) // blocks) for i in range(blocks)})
+    qs = q[:, list(heads)].contiguous()
+    t0 = time.perf_counter()
+    for b_ in picks:
+        sl = slice(128 * b_, min(N, 128 * b_ + 128))
+        qr = O.apply_rope(qs[:, :, sl], cos[:, sl], sin[:, sl])
+        qfull = torch.zeros_like(qs)
+        qfull[:, :, sl] = qr
+        O.eager_attention(qfull, k_ref, vv, CFG["D"] ** -0.5, n_rep=len(heads) // len(kv_heads), query_rows=sl)
+    dt = time.perf_counter() - t0
+    return dt, 128 * len(picks) * len(heads) / CFG["Hq"]
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    heads = (0,)
-    # size each step so the whole run stays near a minute: a full q-head costs ~1.5 s here,
-    # so long runs sample every `stride`-th query block (uniform over sequence positions)
-    t_head, _ = cpu_sample(heads, stride=8)
-    t_head *= 8
-    budget = 60.0 / (args.steps + args.warmup)
-    stride = max(1, min(64, int(-(-t_head // budget))))
+    heads = (0, 1, 2, 3)  # kv-head 0 with its whole GQA group
+    # one step is the whole group over every query block when that fits the budget (the whole
+    # run stays within about three minutes); otherwise every `stride`-th query block
+    t_probe, _ = cpu_sample(heads, stride=8)
+    t_group = t_probe * 8
+    budget = 150.0 / (args.steps + args.warmup)
+    stride = max(1, min(64, int(-(-t_group // budget))))
     for _ in range(args.warmup):
         cpu_sample(heads, stride)
     secs, toks = 0.0, 0.0
@@ -511,26 +641,71 @@ def run_reference(args, world, rank):
         secs += dt
         toks += tk
     value = toks / secs
+    nmb = -(-CFG["N"] // 128)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 * secs / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, BASELINE cfg2)",
-            "config": workload_config(world), "impl": "reference",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, BASELINE cfg2)",
+            "config": workload_config(world, "heads"), "impl": "reference",
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": f"per step: q-head 0 of 32 (its kv-head's RoPE and packing, attention "
-                                       f"on every {stride}th of 256 query blocks) of one N={CFG['N']} layer; "
-                                       f"tokens scaled accordingly"},
+                             "sample": f"per step: kv-head 0 with its 4 q-heads (one whole GQA group, 4 of 32 "
+                                       f"q-heads) of one N={CFG['N']} layer: RoPE, periodic packing, two-phase "
+                                       f"attention on every {stride}th of {nmb} query blocks; tokens scaled by "
+                                       f"the sampled rows"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------------------ GPU side
+def _timed_steps(step, steps, stream, flush=None):
+    """Run `steps` steps; returns total device ms. Without `flush` one event pair brackets the
+    loop; with it, L2 is flushed between steps (outside the timed events) and the per-step
+    event times are summed."""
+    if flush is None:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(steps):
+            step(True)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1)
+    evs = []
+    for _ in range(steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step(True)
+        e1.record(stream)
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs)
+
+
+L2_BYTES = 126 * 10 ** 6
+
+
 def run_ours(args, world, rank, local):
     from deltaattention_b200 import _lib as L
     from deltaattention_b200 import ops, synth
+    from deltaattention_b200 import shard as shard_mod
     dev = torch.device("cuda", local)
     B, Hq, Hkv, N, D, r, W = CFG["B"], CFG["Hq"], CFG["Hkv"], CFG["N"], CFG["D"], CFG["r"], CFG["W"]
-    q, k, v = synth.layer_inputs(B, Hq, Hkv, N, D, torch.bfloat16, seed=1000 + rank, device=dev)
+    shard = args.shard
+    if shard == "heads" and Hkv % world:
+        raise SystemExit(f"--shard heads needs the {Hkv} kv-heads to divide over {world} GPUs")
+    # inputs: the one sequence every rank generates from the same seed (it keeps its kv-heads and
+    # their query heads), or with --shard seq a sequence of its own per rank
+    seed = 1000 if shard == "heads" else 1000 + rank
+    q_all, k_all, v_all = synth.layer_inputs(B, Hq, Hkv, N, D, torch.bfloat16, seed=seed, device=dev)
     cos, sin = synth.rope_tables(N, D, CFG["theta"], torch.bfloat16, device=dev)
+    if shard == "heads":
+        q, k, v = shard_mod.shard_layer(q_all, k_all, v_all, world, rank)
+        tokens = B * N
+    else:
+        q, k, v = q_all, k_all, v_all
+        tokens = B * N * world
+    my_hq, my_hkv = q.shape[1], k.shape[1]
+    in_bytes = (q.numel() + k.numel() + v.numel()) * 2
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if in_bytes < 1.5 * L2_BYTES else None
     period = r
     stream = torch.cuda.current_stream(dev)
     attn_events = []
@@ -553,29 +728,22 @@ def run_ours(args, world, rank, local):
         step()
     torch.cuda.synchronize()
     barrier(world)
-    with ClockSampler(range(world)) as clk:
+    with ClockSampler(range(world) if rank == 0 else [local]) as clk:
         torch.cuda.synchronize()
         barrier(world)
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        for _ in range(args.steps):
-            step(record=True)
-        t1.record(stream)
-        torch.cuda.synchronize()
+        total_ms = _timed_steps(step, args.steps, stream, flush)
         barrier(world)
-        clocks = clk.summary()
-    ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world)
+    clocks = clk.summary()
+    ms = max_over_ranks(total_ms / args.steps, world)
     attn_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in attn_events) / len(attn_events), world)
     codes = L.workspace_errors()
     if any(codes):
         raise RuntimeError(f"bounded device wait timed out during the bench: {codes}")
-    tokens = B * N * world
     value = tokens / (ms / 1000.0)
 
     if args.only_step:
         if rank == 0:
-            print(json.dumps({"ms_per_step": ms, "attn_ms": attn_ms}), flush=True)
+            print(json.dumps({"ms_per_step": ms, "attn_ms": attn_ms, "clocks": clocks}), flush=True)
         return
     # dense (r = 1) comparator through the same kernel family: causal flash with GQA by index
     q_rot, k_rot = ops.rope(q, cos, sin), ops.rope(k, cos, sin)
@@ -590,34 +758,64 @@ def run_ours(args, world, rank, local):
     d1.record(stream)
     torch.cuda.synchronize()
     dense_ms = max_over_ranks(d0.elapsed_time(d1) / nd, world)
-    # the reference's other two kernels of the same family (deltaFlashAttention.py:149-357):
-    # the sanity variant (phase-1 QK^T computed and discarded) and pure phase 1
-    variants = {}
-    pk = ops.pack_periodic(k_rot, v, period)
-    for name in ("sanity", "pure_phase1"):
-        ops.attention(q_rot, k_rot, v, pk, dense_window=W, variant=name)
+    extra = {}
+    if world == 1:
+        # the reference's other two kernels of the same family (deltaFlashAttention.py:149-357):
+        # the sanity variant (phase-1 QK^T computed and discarded) and pure phase 1
+        variants = {}
+        pk = ops.pack_periodic(k_rot, v, period)
+        for name in ("sanity", "pure_phase1"):
+            ops.attention(q_rot, k_rot, v, pk, dense_window=W, variant=name)
+            torch.cuda.synchronize()
+            d0.record(stream)
+            for _ in range(nd):
+                ops.attention(q_rot, k_rot, v, pk, dense_window=W, variant=name)
+            d1.record(stream)
+            torch.cuda.synchronize()
+            variants[name] = {"ms": d0.elapsed_time(d1) / nd}
+        extra["variants"] = variants
+        del pk
+        # the reference's threshold ("row" delta) mode as a whole layer-op: RoPE, delta scan,
+        # device packing and the two-phase attention; raw Euclidean threshold 11 keeps about 1
+        # key in 4 here
+        for _ in range(2):
+            ops.delta_prefill(q, k, v, cos, sin, mode="delta", threshold=11.0, dense_window=W)
         torch.cuda.synchronize()
         d0.record(stream)
         for _ in range(nd):
-            ops.attention(q_rot, k_rot, v, pk, dense_window=W, variant=name)
+            ops.delta_prefill(q, k, v, cos, sin, mode="delta", threshold=11.0, dense_window=W)
         d1.record(stream)
         torch.cuda.synchronize()
-        variants[name] = {"ms": max_over_ranks(d0.elapsed_time(d1) / nd, world)}
-    del q_rot, k_rot, pk
-    # the reference's threshold ("row" delta) mode as a whole layer-op: RoPE, delta scan,
-    # device packing (with the one packed-length read-back modeling_llama.py:656 also makes)
-    # and the two-phase attention; raw Euclidean threshold 11 keeps about 1 key in 4 here
-    for _ in range(2):
-        ops.delta_prefill(q, k, v, cos, sin, mode="delta", threshold=11.0, dense_window=W)
-    torch.cuda.synchronize()
-    d0.record(stream)
-    for _ in range(nd):
-        ops.delta_prefill(q, k, v, cos, sin, mode="delta", threshold=11.0, dense_window=W)
-    d1.record(stream)
-    torch.cuda.synchronize()
-    delta_ms = max_over_ranks(d0.elapsed_time(d1) / nd, world)
-    delta_mode = {"ms_per_layer_op": delta_ms, "tokens_per_s": B * N * world / (delta_ms / 1000.0),
-                  "threshold": 11.0, "selection": "Euclidean delta scan, chunk 512"}
+        delta_ms = d0.elapsed_time(d1) / nd
+        extra["delta_mode"] = {"ms_per_layer_op": delta_ms, "tokens_per_s": B * N / (delta_ms / 1000.0),
+                               "threshold": 11.0, "selection": "Euclidean delta scan, chunk 512"}
+    else:
+        # verification, outside the timed region: the gathered kv-head shards equal one GPU's
+        # computation of the whole layer, bit for bit (the heads are independent)
+        if shard == "heads":
+            full = shard_mod.gather_heads(step(), world)
+            if rank == 0:
+                qr_, kr_ = ops.rope(q_all, cos, sin), ops.rope(k_all, cos, sin)
+                want = ops.attention(qr_, kr_, v_all, ops.pack_periodic(kr_, v_all, period), dense_window=W)
+                extra["verify"] = {"gathered_shards_equal_one_gpu": bool(torch.equal(
+                    full.view(torch.int16), want.contiguous().view(torch.int16)))}
+                del qr_, kr_, want
+            del full
+            barrier(world)
+        # beside the kv-head-sharded sequence: every GPU running a whole cfg2 layer of its own
+        # (one sequence per GPU, the data-parallel alternative), timed the same way
+        def dp_step(record=False):
+            qr_, kr_ = ops.rope(q_all, cos, sin), ops.rope(k_all, cos, sin)
+            ops.attention(qr_, kr_, v_all, ops.pack_periodic(kr_, v_all, period), dense_window=W)
+        for _ in range(3):
+            dp_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        dp_ms = max_over_ranks(_timed_steps(dp_step, args.steps, stream) / args.steps, world)
+        barrier(world)
+        extra["dp_one_sequence_per_gpu"] = {"value": B * N * world / (dp_ms / 1000.0), "unit": UNIT,
+                                            "ms_per_step": dp_ms, "scaling": "weak"}
+    del q_rot, k_rot
 
     # end to end through the public API: pinned host inputs (head-major [B, H, N, d]) -> device
     # -> pinned host output; ops.delta_prefill_host overlaps each kv-head group's copies with
@@ -625,7 +823,7 @@ def run_ours(args, world, rank, local):
     hq = q.contiguous().cpu().pin_memory()
     hk = k.contiguous().cpu().pin_memory()
     hv = v.contiguous().cpu().pin_memory()
-    ho = torch.empty((B, Hq, N, D), dtype=torch.bfloat16).pin_memory()
+    ho = torch.empty((B, my_hq, N, D), dtype=torch.bfloat16).pin_memory()
 
     def e2e_step():
         ops.delta_prefill_host(hq, hk, hv, cos, sin, out=ho, keep_rate=1.0 / r, dense_window=W)
@@ -643,52 +841,64 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(s0.elapsed_time(s1) / ne, world)
+    # every rank copies its own share: the job's bytes are world x this rank's
+    h2d = (hq.numel() + hk.numel() + hv.numel()) * 2 * world
+    d2h = ho.numel() * 2 * world
+    # DRAM bytes of the committed ncu capture (a whole cfg2 launch, 8 kv-heads) scaled to this
+    # rank's kv-heads (the traffic is per head)
+    traffic = traffic_per_launch()
+    traffic = traffic * my_hkv / Hkv if traffic else None
 
-    burst, sustained, src = peaks()
+    timed_s = total_ms / 1000.0
+    peak, peak_kind, other = pick_peak(clocks, timed_s)
     tiles = ops.tile_count_periodic(N, r, W)
-    flops = B * Hq * tiles * 4 * 128 * 128 * D
+    flops = B * my_hq * tiles * 4 * 128 * 128 * D
     achieved = flops / (attn_ms / 1000.0) / 1e12
+    burst, sustained, _ = peaks()
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if shard == "heads" else "weak",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded AR(1) keys + offsets, 0.5*N(0,1) q/v: BASELINE cfg2 distributions)",
-        "config": workload_config(world),
-        # the attention launch is timed inside `steps` back-to-back steps (the clock record shows
-        # the power-capped regime), so its denominator is the sustained GEMM figure; the burst
-        # fraction is reported beside it
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
-                     "frac": achieved / sustained, "traffic": traffic_per_launch(),
+        "config": workload_config(world, shard, flush is not None),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic,
                      "kernel": "attn_tc_kernel<128,bf16>", "attn_ms_per_launch": attn_ms,
-                     "flops_per_launch": flops, "tiles_per_head": tiles,
-                     "peak_kind": f"{src} bf16 sustained (timed inside the step loop; burst {burst})",
-                     "frac_of_burst": achieved / burst},
-        "e2e": {"value": B * N * world / (e2e_ms / 1000.0), "unit": UNIT, "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": (hq.numel() + hk.numel() + hv.numel()) * 2,
-                "d2h_bytes_per_step": ho.numel() * 2,
+                     "flops_per_launch": flops, "tiles_per_head": tiles, "peak_kind": peak_kind,
+                     "frac_of_burst": achieved / burst, "frac_of_sustained": achieved / sustained},
+        "e2e": {"value": tokens / (e2e_ms / 1000.0), "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "ops.delta_prefill_host (pinned head-major host buffers; one kv-head per group, "
                        "H2D / compute / D2H on three streams)",
-                "pcie_gbs": {"h2d": (hq.numel() + hk.numel() + hv.numel()) * 2 / (e2e_ms / 1000.0) / 1e9,
-                             "d2h": ho.numel() * 2 / (e2e_ms / 1000.0) / 1e9}},
+                "pcie_gbs_per_gpu": {"h2d": h2d / world / (e2e_ms / 1000.0) / 1e9,
+                                     "d2h": d2h / world / (e2e_ms / 1000.0) / 1e9}},
         "dense_r1": {"ms_per_step": dense_ms, "speedup_of_delta_attention": dense_ms / attn_ms},
-        "variants": variants,
-        "delta_mode": delta_mode,
-        "gpu_launches": launches_per_step * args.steps,
+        **extra,
+        "gpu_launches": launches_per_step * args.steps * world,
         "clocks": clocks,
     }
-    if not args.no_sweep:
+    if world == 1 and not args.no_sweep:
         line["sweep"] = sweep(dev, 3000 + rank)
-    hk = hbm_kernels(dev, 2000 + rank)
-    line["hbm_kernels"] = {"peak_gbs": hbm_peak()[0], "peak_kind": hbm_peak()[1], **hk}
-    if not args.no_sweep:
+    if world == 1:
+        hk_ = hbm_kernels(dev, 2000 + rank)
+        line["hbm_kernels"] = {"peak_gbs": hbm_peak()[0], "peak_kind": hbm_peak()[1], **hk_}
+    if world == 1 and not args.no_sweep:
         line["decode_step"] = decode_step(dev, 4000 + rank)
         line["serving_cfg5"] = serving(dev, 5000 + rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
         dt, tk = cpu_sample(tuple(range(8)))
+        de, te = cpu_eager_dense_sample()
         line["cpu_baseline"] = {"value": tk / dt, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                                 "sample": f"8 of 32 q-heads (2 whole GQA groups) of one N={N} layer (RoPE, "
-                                          f"packing, two-phase attention), {dt:.1f} s; tokens scaled by 8/32"}
+                                          f"packing, two-phase attention), {dt:.1f} s; tokens scaled by 8/32",
+                                "eager_dense_r1": {"value": te / de, "unit": UNIT, "seconds": de,
+                                                   "sample": "the reference's eager dense attention "
+                                                             "(modeling_llama.py:235-276) for 8 query blocks of "
+                                                             "q-heads 0-3 spread over the sequence, all N keys; "
+                                                             "tokens scaled by the rows computed"},
+                                "os_cpu_count": os.cpu_count()}
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -699,6 +909,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--shard", default="heads", choices=["heads", "seq"],
+                    help="multi-GPU partition: kv-heads of one sequence (default) or one sequence per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the cfg3 N / r sweep")
     ap.add_argument("--n", type=int, default=None, help="sequence length override (profiling small cases)")

@@ -37,6 +37,7 @@ SIGNATURES = {
                                I64, I64, I64, I64, I64, I64, P, SZ, I32, P]),
     "dab_hybrid_flash_noalloc": (I32, [I32, P, P, P, P, P, P, P, I32, P, I32, PI64, F32, I64, I64, I64, I64, I64,
                                        I64, I64, I64, I64, I64, I64, I64, I32, P]),
+    "dab_noalloc_error": (I32, [PI32, P]),
     "dab_attn_fwd_flat": (I32, [P, P, P, F32, P, I32, PI64, I64, I64, I64, I64, I64, I64, I32, I64, I64, I64, P,
                                 SZ, I32, P]),
     "dab_decode_update": (I32, [P, P, P, P, P, P, P, P, P, I64, I64, F32, I64, I32, PI64, PI64, PI64, PI64, I64,

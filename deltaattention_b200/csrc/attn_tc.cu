@@ -364,16 +364,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       }
     }
   kprod_done:
-    // drain: every copy this warp issued must land before the CTA exits
+    // drain: every copy this warp issued must land before the CTA exits (bounded; a copy that
+    // never lands is reported as ERR_TIMEOUT_DRAIN)
     if (lane == 0) {
-      for (int q = (kpos > NK ? kpos - NK : 0); q < kpos; ++q) {
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(k_full + q % NK, (q / NK) & 1) && globaltimer() - t0 < 50000000ull) {}
-      }
-      if (q_issued > 0) {
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(q_full, (q_issued - 1) & 1) && globaltimer() - t0 < 50000000ull) {}
-      }
+      bool drained = true;
+      for (int q = (kpos > NK ? kpos - NK : 0); q < kpos && drained; ++q)
+        drained = mbar_drain(k_full + q % NK, (q / NK) & 1, p.err);
+      if (drained && q_issued > 0) mbar_drain(q_full, (q_issued - 1) & 1, p.err);
     }
   } else if (warp == 3) {
     // ================================================================ V (+ counts) producer
@@ -436,10 +433,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
     }
   vprod_done:
     if (lane == 0) {
-      for (int q = (vpos > NV ? vpos - NV : 0); q < vpos; ++q) {
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(v_full + q % NV, (q / NV) & 1) && globaltimer() - t0 < 50000000ull) {}
-      }
+      bool drained = true;
+      for (int q = (vpos > NV ? vpos - NV : 0); q < vpos && drained; ++q)
+        drained = mbar_drain(v_full + q % NV, (q / NV) & 1, p.err);
     }
   } else if (warp == 1 || warp == 2) {
     // ================================================================ MMA issuers
@@ -598,8 +594,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       }
       // wait for every MMA this warp issued before TMEM can be released (one commit per warp)
       umma_commit(mma_done);
-      const uint64_t t0 = globaltimer();
-      while (!mbar_try_wait(mma_done, 0) && globaltimer() - t0 < 50000000ull) {}
+      if (lane == 0) mbar_drain(mma_done, 0, p.err);
+      __syncwarp();
     }
   } else if (warp >= 4) {
     // ================================================================ softmax + epilogue

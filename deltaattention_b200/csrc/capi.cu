@@ -331,6 +331,16 @@ int dab_hybrid_flash_noalloc(int variant, const void* q, const void* k_dense, co
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e, "dab_hybrid_flash_noalloc (cudaGetDevice)");
   if (dev < 0 || dev >= kMaxDevices) return fail(1, "dab_hybrid_flash_noalloc: device ordinal out of range");
+  // the scratch used is the current device's copy: the tensors must live on that device
+  if (q) {
+    cudaPointerAttributes pa;
+    e = cudaPointerGetAttributes(&pa, q);
+    if (e != cudaSuccess) return cuda_status(e, "dab_hybrid_flash_noalloc (cudaPointerGetAttributes)");
+    if ((pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged) && pa.device != dev)
+      return fail(1, "dab_hybrid_flash_noalloc: q lives on device " + std::to_string(pa.device) +
+                         " but device " + std::to_string(dev) +
+                         " is current; make the tensors' device current (dab_set_device) first");
+  }
   void* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
@@ -354,6 +364,24 @@ int dab_hybrid_flash_noalloc(int variant, const void* q, const void* k_dense, co
                        sm_scale, seq_len_q, seq_len_k, num_packed, head_dim, num_heads, dense_window, grid_m,
                        grid_bh, block_m, block_n, block_d, kv_group, scratch, DAB_NOALLOC_SCRATCH_BYTES,
                        force_simt, static_cast<cudaStream_t>(stream), "hybrid_flash_noalloc");
+}
+
+int dab_noalloc_error(int* code, void* stream) {
+  if (!code) return fail(1, "dab_noalloc_error: null argument");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "dab_noalloc_error (cudaGetDevice)");
+  if (dev < 0 || dev >= kMaxDevices) return fail(1, "dab_noalloc_error: device ordinal out of range");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    scratch = g_noalloc_ptr[dev];
+  }
+  if (!scratch) {  // no dab_hybrid_flash_noalloc call on this device yet
+    *code = 0;
+    return 0;
+  }
+  return dab_workspace_error(scratch, code, stream);
 }
 
 int dab_attn_fwd_flat(const void* q, const void* k, const void* v, float sm_scale, void* out, int dtype,

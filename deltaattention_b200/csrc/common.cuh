@@ -27,6 +27,7 @@ enum DevError : int {
   ERR_TIMEOUT_MMA = 0x102,
   ERR_TIMEOUT_SOFTMAX = 0x103,
   ERR_TIMEOUT_EPILOGUE = 0x104,
+  ERR_TIMEOUT_DRAIN = 0x105,  // teardown: copies or MMAs issued by this CTA did not complete
 };
 
 // ------------------------------------------------------------------ dtype helpers
@@ -137,6 +138,21 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parit
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const Abort& ab, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   return mbar_wait_slow(bar, parity, ab, code);
+}
+
+// Teardown wait for work this CTA already issued (bulk copies landing in its shared memory,
+// MMAs writing its TMEM): it ignores the abort flag, since issued work completes whether or
+// not the CTA gave up, and after DAB_WAIT_TIMEOUT_NS records ERR_TIMEOUT_DRAIN in the error
+// word and returns false, so the host learns that the CTA exited with that work outstanding.
+static __device__ __noinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, int* err_gmem) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait_sleep(bar, parity, 100000u)) {
+    if (globaltimer() - t0 > DAB_WAIT_TIMEOUT_NS) {
+      if (err_gmem) atomicCAS(err_gmem, 0, static_cast<int>(ERR_TIMEOUT_DRAIN));
+      return false;
+    }
+  }
+  return true;
 }
 
 // ------------------------------------------------------------------ TMA

@@ -102,12 +102,18 @@ int dab_hybrid_flash(int variant, const void* q, const void* k_dense, const void
  * against the reference's launch signature alone, which has no scratch argument.
  * - Limit: dab_hybrid_flash_workspace_size(grid_bh / num_heads, num_heads / kv_group,
  *   seq_len_q, num_packed) must not exceed DAB_NOALLOC_SCRATCH_BYTES; larger calls return 1
- *   with a message naming both sizes (e.g. 128 k queries x 64 timestamp heads still fit).
+ *   with a message naming both sizes. The size is 256 + 8*B*H*ceil(Nq/128) +
+ *   8*B*H*ceil(num_packed/128) bytes (each array rounded up to 256; H = timestamp heads), so
+ *   e.g. 128 k queries x 64 timestamp heads fit while num_packed <= 64 k (r >= 2), not at r = 1.
+ * - The scratch used is the current device's copy; q must live on the current device (else
+ *   the call returns 1).
  * - The first call on a device resolves the scratch address for that device (with that
- *   device current); make it before any stream capture.
+ *   device current); make it before any stream capture. The address is kept for the life of
+ *   the process: do not cudaDeviceReset a device this entry point has used.
  * - The array keeps the last call's contents. Only its 256-byte header (the device error word
  *   a timed-out in-kernel wait sets) must start at zero, and every call clears it on its stream
  *   first; every other scratch byte a call reads is written earlier in the same call.
+ *   dab_noalloc_error reads that word after a call.
  * - Calls that overlap on one device (other streams or threads) share the scratch and race;
  *   serialise them. */
 int dab_hybrid_flash_noalloc(int variant, const void* q, const void* k_dense, const void* v_dense,
@@ -117,6 +123,12 @@ int dab_hybrid_flash_noalloc(int variant, const void* q, const void* k_dense, co
                              int64_t num_packed, int64_t head_dim, int64_t num_heads, int64_t dense_window,
                              int64_t grid_m, int64_t grid_bh, int64_t block_m, int64_t block_n, int64_t block_d,
                              int64_t kv_group, int force_simt, void* stream);
+
+/* No counterpart in the reference. Reads and clears the error word of the current device's
+ * dab_hybrid_flash_noalloc scratch (nonzero: a bounded in-kernel wait of the last call timed
+ * out and its output is not valid); 0 when no call has run on the device. Synchronises
+ * `stream`, so call it on the stream of the call it checks. */
+int dab_noalloc_error(int* code, void* stream);
 
 /* _attn_fwd_flat[grid](Q, K, V, sm_scale, Out, 16 strides (q, k, v, out), Z, H, N_CTX,
  *   HEAD_DIM, BLOCK_M, BLOCK_N, IS_CAUSAL) - flashAttention.py:5-91, wrapper

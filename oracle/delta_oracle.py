@@ -466,13 +466,20 @@ def flash_attention(q, k, v, causal: bool = True, sm_scale: Optional[float] = No
     return out.to(q.dtype)
 
 
-def eager_attention(q, k, v, sm_scale: float, n_rep: int = 1):
-    """``eager_attention_forward`` (modeling_llama.py:235-276) with a causal mask, fp32 softmax."""
+def eager_attention(q, k, v, sm_scale: float, n_rep: int = 1, query_rows: Optional[slice] = None):
+    """``eager_attention_forward`` (modeling_llama.py:235-276) with a causal mask, fp32 softmax.
+
+    ``query_rows`` (a slice of positions) computes only those query rows against all N keys,
+    with the causal mask at their absolute positions; the output then holds those rows."""
     k = k.repeat_interleave(n_rep, dim=1)
     v = v.repeat_interleave(n_rep, dim=1)
-    N = q.shape[2]
+    N = k.shape[2]
+    rows = torch.arange(N)
+    if query_rows is not None:
+        q = q[:, :, query_rows]
+        rows = rows[query_rows]
     w = torch.matmul(q, k.transpose(2, 3)) * sm_scale
-    mask = torch.full((N, N), float("-inf"), dtype=w.dtype).triu(1)
+    mask = torch.where(torch.arange(N)[None, :] > rows[:, None], float("-inf"), 0.0).to(w.dtype)
     w = w + mask
     w = torch.softmax(w, dim=-1, dtype=torch.float32).to(q.dtype)
     return torch.matmul(w, v)

@@ -1,0 +1,152 @@
+"""GPU parity at the sizes the benchmark measures, against the CPU oracle (never against
+another kernel of this library).
+
+* cfg3 (long-context sweep): N = 131072 at r = 2 and r = 8, N = 65536 at r = 4.
+* the reference's threshold ("row" delta) mode at cfg2 length, with per-key run-length counts
+  that differ inside packed blocks.
+* cfg5 (batched varlen serving, 2:4 N:M selection at r = 4): every sequence of a varlen batch.
+
+The GPU computes every head and query block; the oracle checks two q-heads (one per kv-head
+group) on the first, middle and last query blocks, where the schedule differs most (no phase 1,
+half the packed history, all of it). Selection, packing, timestamps and counts are compared
+bit for bit; attention outputs within max-abs 2e-2 and mean-abs 2e-3 (bf16).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import delta_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL_BF16 = (2e-2, 2e-3)  # max-abs, mean-abs
+
+
+@pytest.fixture(scope="module", autouse=True)
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import deltaattention_b200 as d
+    d._lib.load()
+    return d
+
+
+def _blocks(n_rows, k=8):
+    nmb = -(-n_rows // 128)
+    mid = nmb // 2
+    picks = list(range(min(k, nmb))) + list(range(max(0, mid - k // 2), min(nmb, mid + k // 2))) + \
+        list(range(max(0, nmb - k), nmb))
+    return sorted(set(picks))
+
+
+def _cmp_rows(out, ref, blocks, n_rows, what):
+    """out / ref [R, d] rows of one head; compares the rows of `blocks`."""
+    rows = torch.cat([torch.arange(128 * b, min(n_rows, 128 * b + 128)) for b in blocks])
+    o, r = out[rows].float().cpu(), ref[rows].float()
+    assert torch.isfinite(o).all(), what
+    err = (o - r).abs()
+    mx, mean = TOL_BF16
+    assert err.max().item() <= mx and err.mean().item() <= mean, (what, err.max().item(), err.mean().item())
+
+
+def _check_ws_clean():
+    from deltaattention_b200 import _lib as L
+    torch.cuda.synchronize()
+    codes = L.workspace_errors()
+    assert all(c == 0 for c in codes), f"a bounded device wait timed out: {[hex(c) for c in codes]}"
+
+
+@pytest.mark.parametrize("N,r", [(131072, 2), (131072, 8), (65536, 4)])
+def test_cfg3_long_context_matches_oracle(N, r):
+    """BASELINE config 3 points (Llama-3.1-8B layer shapes per head, GQA 4:1, bf16, theta 5e5,
+    periodic r): the whole layer-op on the GPU, sampled query blocks of q-heads 0 and 5 on the
+    oracle."""
+    from deltaattention_b200 import ops, synth
+    Hq, Hkv, D = 8, 2, 128
+    q, k, v = synth.layer_inputs(1, Hq, Hkv, N, D, torch.bfloat16, seed=70 + r, device="cpu")
+    cos, sin = synth.rope_tables(N, D, 5e5, torch.bfloat16)
+    out, packed, k_rot = ops.delta_prefill(q.cuda(), k.cuda(), v.cuda(), cos.cuda(), sin.cuda(), keep_rate=1.0 / r,
+                                           return_packed=True)
+    heads = [0, 5]  # kv-heads 0 and 1
+    q_ref = O.apply_rope(q[:, heads].contiguous(), cos, sin)
+    k_ref = O.apply_rope(k.contiguous(), cos, sin)
+    assert torch.equal(k_rot.cpu().view(torch.int16), k_ref.view(torch.int16))
+    keep = O.periodic_keep_mask(1, Hkv, N, 1.0 / r)
+    _, kp, vp, ts, cnt = O.pack_from_keep(k_ref, v.contiguous(), keep)
+    np.testing.assert_array_equal(packed.timestamps.cpu().numpy(), ts.numpy())
+    np.testing.assert_array_equal(packed.counts.cpu().numpy(), cnt.numpy())
+    blocks = _blocks(N)
+    ref = O.hybrid_attention(q_ref, k_ref, v.contiguous(), kp, vp, ts, cnt.float(), D ** -0.5, 128, n_rep=1,
+                             query_blocks=blocks)
+    for j, h in enumerate(heads):
+        _cmp_rows(out[0, h], ref[0, j], blocks, N, f"cfg3 N={N} r={r} head {h}")
+    _check_ws_clean()
+
+
+@pytest.mark.parametrize("threshold", [11.0, 15.0])
+def test_delta_mode_cfg2_length_matches_oracle(threshold):
+    """The paper's own selection (squared-Euclidean threshold, chunks of 512) at cfg2 length:
+    keep mask, packed timestamps and counts bit-exact; attention (which takes the per-key-count
+    path in blocks whose counts differ) within the bf16 tolerance on sampled blocks."""
+    from deltaattention_b200 import ops, synth
+    N, Hq, Hkv, D = 32768, 8, 2, 128
+    q, k, v = synth.layer_inputs(1, Hq, Hkv, N, D, torch.bfloat16, seed=80, device="cpu")
+    cos, sin = synth.rope_tables(N, D, 5e5, torch.bfloat16)
+    out, packed, k_rot = ops.delta_prefill(q.cuda(), k.cuda(), v.cuda(), cos.cuda(), sin.cuda(), mode="delta",
+                                           threshold=threshold, chunk_size=512, return_packed=True)
+    heads = [0, 5]
+    q_ref = O.apply_rope(q[:, heads].contiguous(), cos, sin)
+    k_ref = O.apply_rope(k.contiguous(), cos, sin)
+    keep, _ = O.delta_keep_mask(k_ref, threshold ** 2, False, 512, N // 512)
+    np.testing.assert_array_equal(packed.keep_mask.cpu().numpy(), keep.numpy())
+    _, kp, vp, ts, cnt = O.pack_from_keep(k_ref, v.contiguous(), keep)
+    assert packed.k.shape[2] == kp.shape[2]
+    np.testing.assert_array_equal(packed.timestamps.cpu().numpy(), ts.numpy())
+    np.testing.assert_array_equal(packed.counts.cpu().numpy(), cnt.numpy())
+    assert (cnt[:, :, :128].amax(-1) != cnt[:, :, :128].amin(-1)).any(), "counts should differ within a block"
+    blocks = _blocks(N)
+    ref = O.hybrid_attention(q_ref, k_ref, v.contiguous(), kp, vp, ts, cnt.float(), D ** -0.5, 128, n_rep=1,
+                             query_blocks=blocks)
+    for j, h in enumerate(heads):
+        _cmp_rows(out[0, h], ref[0, j], blocks, N, f"delta thr {threshold} head {h}")
+    _check_ws_clean()
+
+
+def test_cfg5_varlen_nm_sequences_match_oracle():
+    """BASELINE config 5 prefill (Llama-3.1-8B layer shapes, lengths U[4096, 32768] packed with
+    cu_seqlens, 2:4 N:M at r = 4, q / v ~ N(0, 1), AR(1) keys): every sequence's keep mask and
+    packed history bit-exact, its attention on sampled blocks of q-heads 0 and 13, against the
+    oracle's N:M selection, packing and two-phase attention on that sequence alone."""
+    from deltaattention_b200 import ops, synth
+    Hq, Hkv, D = 32, 8, 128
+    gen = torch.Generator().manual_seed(55)
+    lens = torch.randint(4096, 32769, (4,), generator=gen).tolist()
+    cu = [0]
+    for n_ in lens:
+        cu.append(cu[-1] + n_)
+    T = cu[-1]
+    q, k, v = synth.layer_inputs(1, Hq, Hkv, T, D, torch.bfloat16, seed=56, device="cpu", qv_scale=1.0,
+                                 key_offset=False)
+    cos, sin = synth.rope_tables(max(lens), D, 5e5, torch.bfloat16)
+    out, packed = ops.delta_prefill_varlen(q.cuda(), k.cuda(), v.cuda(), cos.cuda(), sin.cuda(), cu, selection="nm",
+                                           n=2, m=4, ratio=4, streams=3, return_packed=True)
+    torch.cuda.synchronize()
+    heads, kvh = [0, 13], [0, 3]
+    for i, (s0, s1) in enumerate(zip(cu, cu[1:])):
+        n_ = s1 - s0
+        c_, s_ = cos[:, :n_], sin[:, :n_]
+        q_ref = O.apply_rope(q[:, heads, s0:s1].contiguous(), c_, s_)
+        k_ref = O.apply_rope(k[:, kvh, s0:s1].contiguous(), c_, s_)
+        keep = O.nm_keep_mask(k_ref, 2, 4, 4)
+        _, kp, vp, ts, cnt = O.pack_from_keep(k_ref, v[:, kvh, s0:s1].contiguous(), keep)
+        got, got_k = packed[i]
+        assert torch.equal(got_k[:, kvh].cpu().view(torch.int16), k_ref.view(torch.int16)), i
+        np.testing.assert_array_equal(got.keep_mask[:, kvh].cpu().numpy(), keep.numpy())
+        np.testing.assert_array_equal(got.timestamps[:, kvh].cpu().numpy(), ts.numpy())
+        np.testing.assert_array_equal(got.counts[:, kvh].cpu().numpy(), cnt.numpy())
+        blocks = _blocks(n_, 4)
+        ref = O.hybrid_attention(q_ref, k_ref, v[:, kvh, s0:s1].contiguous(), kp, vp, ts, cnt.float(), D ** -0.5,
+                                 128, n_rep=1, query_blocks=blocks)
+        for j, h in enumerate(heads):
+            _cmp_rows(out[0, h, s0:s1], ref[0, j], blocks, n_, f"cfg5 sequence {i} (N={n_}) head {h}")
+    _check_ws_clean()

@@ -148,6 +148,67 @@ def test_bench_max_over_ranks_gloo_world2():
     assert dict(out) == {0: 2.5, 1: 2.5}
 
 
+def _shard_rank_main(rank, world, port, out):
+    """One gloo rank of the kv-head partition: it runs the oracle layer-op on its kv-heads only
+    and gathers every rank's output heads."""
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from deltaattention_b200 import shard, synth
+        from oracle import delta_oracle as O
+        B, Hq, Hkv, N, D = 1, 8, 4, 384, 64
+        q, k, v = synth.layer_inputs(B, Hq, Hkv, N, D, torch.float32, seed=3, device="cpu")
+        cos, sin = synth.rope_tables(N, D, 1e4, torch.float32)
+        ql, kl, vl = shard.shard_layer(q, k, v, world, rank)
+        qr, kr = O.apply_rope(ql.contiguous(), cos, sin), O.apply_rope(kl.contiguous(), cos, sin)
+        keep = O.periodic_keep_mask(B, kl.shape[1], N, 0.25)
+        _, kp, vp, ts, cnt = O.pack_from_keep(kr, vl.contiguous(), keep)
+        o = O.hybrid_attention(qr, kr, vl.contiguous(), kp, vp, ts, cnt.float(), D ** -0.5, 128, n_rep=Hq // Hkv)
+        full = shard.gather_heads(o, world)
+        out[rank] = (shard.kv_head_range(Hkv, world, rank), full.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_kv_head_shard_gloo_world2_equals_single_rank():
+    """The bench's multi-GPU partition on two gloo ranks: each rank takes half the kv-heads
+    (with their query heads) of one sequence, and the gathered output equals the one-rank
+    computation of the whole layer exactly (the heads are independent)."""
+    import numpy as np
+    import torch.multiprocessing as mp
+    from deltaattention_b200 import shard, synth
+    from oracle import delta_oracle as O
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_shard_rank_main, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert out[0][0] == (0, 2) and out[1][0] == (2, 4)
+    B, Hq, Hkv, N, D = 1, 8, 4, 384, 64
+    q, k, v = synth.layer_inputs(B, Hq, Hkv, N, D, torch.float32, seed=3, device="cpu")
+    cos, sin = synth.rope_tables(N, D, 1e4, torch.float32)
+    qr, kr = O.apply_rope(q.contiguous(), cos, sin), O.apply_rope(k.contiguous(), cos, sin)
+    keep = O.periodic_keep_mask(B, Hkv, N, 0.25)
+    _, kp, vp, ts, cnt = O.pack_from_keep(kr, v.contiguous(), keep)
+    want = O.hybrid_attention(qr, kr, v.contiguous(), kp, vp, ts, cnt.float(), D ** -0.5, 128, n_rep=Hq // Hkv)
+    for r in range(2):
+        np.testing.assert_array_equal(out[r][1], want.numpy())
+
+
+def test_kv_head_range_rejects_uneven_split():
+    from deltaattention_b200 import shard
+    assert [shard.kv_head_range(8, 4, r) for r in range(4)] == [(0, 2), (2, 4), (4, 6), (6, 8)]
+    with pytest.raises(ValueError, match="divide"):
+        shard.kv_head_range(8, 3, 0)
+    with pytest.raises(ValueError, match="outside"):
+        shard.kv_head_range(8, 2, 2)
+
+
 @pytest.mark.parametrize("cu,msg", [([0, 100, 100, 300], "rise strictly"), ([0, 150, 299], "rise strictly"),
                                     ([5, 300], "rise strictly"), ([0, 300], "shorter than the longest")])
 def test_varlen_prefill_rejects_bad_offsets(cu, msg):

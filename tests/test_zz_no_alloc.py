@@ -1,6 +1,7 @@
 """dab_hybrid_flash_noalloc (static device scratch, no caller workspace) against
 dab_hybrid_flash with a workspace. Collected last (file name) so it also runs after every
 other test has used the library in the same process."""
+import ctypes
 import os
 import sys
 
@@ -49,6 +50,10 @@ def test_noalloc_matches_workspace_entry_point(variant):
         err = (out.float() - ref.float()).abs()
         assert torch.isfinite(out.float()).all()
         assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3, (variant, err.max().item())
+        # the static scratch's own error word: no bounded in-kernel wait of this call timed out
+        code = ctypes.c_int(-1)
+        L.check(L.load().dab_noalloc_error(ctypes.byref(code), L.stream_of(q)), "noalloc_error")
+        assert code.value == 0, hex(code.value)
     assert all(c == 0 for c in L.workspace_errors())
 
 
