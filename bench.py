@@ -392,8 +392,8 @@ def traffic_per_launch():
 class ClockSampler:
     """SM clock, power and clock-event reasons sampled DURING the timed region.
 
-    NVML is polled every `period_s` (2 ms) from a background thread, so a timed region of a
-    few tens of milliseconds still gets ten or more samples; ``nvidia-smi -lms 200`` is the
+    NVML is polled every `period_s` (0.5 ms plus the query time) from a background thread, so
+    a timed region of a few tens of milliseconds still gets ten or more samples; ``nvidia-smi -lms 200`` is the
     fallback when NVML cannot be loaded. GPUs are matched to NVML by UUID (the CUDA ordinals
     of `gpus`), so CUDA_VISIBLE_DEVICES remapping does not confuse them."""
 
@@ -403,7 +403,7 @@ class ClockSampler:
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpus, period_s=0.002):
+    def __init__(self, gpus, period_s=0.0005):
         self.gpus = list(gpus)
         self.period = period_s
         self.samples = []  # (sm_mhz, max_mhz, power_w, reasons bitmask)
@@ -425,16 +425,22 @@ class ClockSampler:
         return pynvml, hs
 
     def _poll(self, pynvml, hs):
+        # two queries per sample (SM clock, event reasons); the maximum clock is read once and
+        # the power every eighth sample, so that a sample takes well under a millisecond
+        mxs = [float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)) for h in hs]
+        pws = [0.0] * len(hs)
+        n = 0
         while not self.stop:
-            for h in hs:
+            for i, h in enumerate(hs):
                 try:
                     sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
-                    mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
-                    pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
                     rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-                    self.samples.append((float(sm), float(mx), pw, int(rs)))
+                    if n % 8 == 0:
+                        pws[i] = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    self.samples.append((float(sm), mxs[i], pws[i], int(rs)))
                 except Exception:
                     pass
+            n += 1
             time.sleep(self.period)
 
     def __enter__(self):
@@ -470,7 +476,7 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], [], set()
-        src = "nvml (2 ms)"
+        src = "nvml (~1 ms)"
         if self.nvml is not None:
             for s, m, _, rs in self.samples:
                 sm.append(s)
