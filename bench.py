@@ -127,6 +127,18 @@ def hbm_kernels(dev, seed):
     nbytes = Hkv * N * 8 + kept * D * 2 * 2 * 2 + kept * 4
     out["scatter_pack"] = {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / peak}
     del im, kp_s, vp_s, ts_s
+    # the fused key compression of delta mode (RoPE(k) + delta scan + packing, one launch, packed
+    # length left on the device): raw K read, rotated K written, the kept V rows read, packed K / V
+    # and timestamps / counts (int32 + fp32) written, keep mask written, cos / sin read once
+    _, k_raw, _ = synth.layer_inputs(1, Hkv, Hkv, N, D, torch.bfloat16, seed=seed, device=dev)
+    us = timed(lambda: ops.delta_compress(k_raw, v, cos, sin, thr, "euclidean", 512))
+    _, pkc = ops.delta_compress(k_raw, v, cos, sin, thr, "euclidean", 512)
+    A = int(pkc.anchors.sum().item())
+    nbytes = 2 * k_raw.numel() * 2 + A * D * 2 * 3 + A * 12 + Hkv * N * 4 + 2 * N * D * 2
+    out["delta_compress"] = {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / peak,
+                             "kept_fraction": A / (Hkv * N),
+                             "replaces": "rope(k) + delta_select + pack_from_keep + the packed-length read-back"}
+    del k_raw, pkc
     # 2:4 N:M selection at r = 4: candidates every 2nd key, so half of K is read; keep mask written
     from deltaattention_b200.dropin.nmDeltaFlashAttention import nm_keep_mask
     us = timed(lambda: nm_keep_mask(k_rot, 2, 4, 4))

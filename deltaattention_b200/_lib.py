@@ -35,6 +35,8 @@ SIGNATURES = {
     "dab_hybrid_flash_workspace_size": (SZ, [I64, I64, I64, I64]),
     "dab_hybrid_flash": (I32, [I32, P, P, P, P, P, P, P, I32, P, I32, PI64, F32, I64, I64, I64, I64, I64, I64,
                                I64, I64, I64, I64, I64, I64, P, SZ, I32, P]),
+    "dab_hybrid_flash_devlen": (I32, [I32, P, P, P, P, P, P, P, I32, P, P, I32, PI64, F32, I64, I64, I64, I64, I64,
+                                      I64, I64, I64, I64, I64, I64, I64, P, SZ, P]),
     "dab_hybrid_flash_noalloc": (I32, [I32, P, P, P, P, P, P, P, I32, P, I32, PI64, F32, I64, I64, I64, I64, I64,
                                        I64, I64, I64, I64, I64, I64, I64, I32, P]),
     "dab_noalloc_error": (I32, [PI32, P]),
@@ -55,6 +57,9 @@ SIGNATURES = {
     "dab_pack_from_keep_workspace_size": (SZ, [I64, I64, I64]),
     "dab_nm_select": (I32, [P, PI64, P, PI64, I32, I64, I64, I64, I64, I64, I64, I64, P]),
     "dab_nm_num_packed": (I64, [I64, I64, I64, I64]),
+    "dab_delta_compress_workspace_size": (SZ, [I64, I64, I64, I64]),
+    "dab_delta_compress": (I32, [P, PI64, P, PI64, P, P, PI64, P, PI64, P, PI64, P, P, PI64, P, P, P, PI64, P, I32,
+                                 I64, I64, I64, I64, F32, I32, I64, I64, P, SZ, P]),
     "dab_pack_from_keep": (I32, [P, PI64, P, PI64, P, PI64, P, P, PI64, P, P, PI64, P, I32, I64, I64, I64, I64,
                                  I64, P, P, P, SZ, P]),
 }
@@ -143,10 +148,11 @@ def workspace(device: torch.device, stream: int, nbytes: int, tag: str = "attn")
 
 
 def workspace_errors() -> list:
-    """Read and clear the error word of every attention workspace (synchronises)."""
+    """Read and clear the error word of every attention and key-compression workspace
+    (synchronises)."""
     codes = []
     for (tag, dev, st), buf in list(_ws_cache.items()):
-        if tag != "attn":
+        if tag not in ("attn", "compress"):
             continue
         code = ctypes.c_int(0)
         check(load().dab_workspace_error(ptr(buf), ctypes.byref(code), ctypes.c_void_p(st)), "workspace_error")

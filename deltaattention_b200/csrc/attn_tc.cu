@@ -54,18 +54,43 @@ template <int D> struct TcCfg {
 // for every query block mb: n1 = first j with T_j >= 128*mb - window, last_safe = T_{n1-1}
 // (or -1), dense start block = (last_safe + 1) // 128. Also the smallest valid timestamp of
 // every packed block for the pure-phase-1 variant (count > 0 and index < num_packed).
+//
+// Device packed length (`anchors` non-null): head bh keeps anchors[bh] rows and the packed
+// length is M = max over heads (written to len_out[0]); keys in [anchors[bh], M) are the
+// reference's zero padding (timestamp 0, count 0) and are scheduled as such without being
+// read, keys >= M are the masked lanes. `nblk` is then the capacity in blocks (the row stride
+// of blkmin / blkw); only the first ceil(M / 128) blocks are scheduled.
 __global__ void __launch_bounds__(256) schedule_kernel(const int32_t* __restrict__ ts, int64_t tsb, int64_t tsh,
                                                        int64_t tsn, const void* counts, int64_t cb, int64_t ch,
                                                        int64_t cn, int counts_is_int, int Hts, int num_packed,
                                                        int seq_k, int window, int nmb, int nblk, int2* sched,
-                                                       int32_t* blkmin, int want_blkmin, float* blkw) {
+                                                       int32_t* blkmin, int want_blkmin, float* blkw,
+                                                       const int32_t* __restrict__ anchors, int nheads_total,
+                                                       int* len_out) {
   extern __shared__ int32_t sT[];  // nblk block maxima
   const int bh = blockIdx.x;
   const int b = bh / Hts, h = bh % Hts;
   const int32_t* tsr = ts + b * tsb + h * tsh;
+  const int tid = threadIdx.x;
+  const int wstride = nblk;  // row stride of blkmin / blkw (the capacity in blocks)
+  int nreal = num_packed;  // keys of this head read from memory
+  if (anchors) {
+    __shared__ int red[8];
+    int m = 0;
+    for (int i = tid; i < nheads_total; i += blockDim.x) m = max(m, anchors[i]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    m = red[0];
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) m = max(m, red[w]);
+    num_packed = min(m, num_packed);
+    nreal = min(anchors[bh], num_packed);
+    nblk = (num_packed + TC_BN - 1) / TC_BN;
+    if (bh == 0 && tid == 0) *len_out = num_packed;
+  }
   // four threads per packed block, 32 consecutive keys each: every thread requests all of its
   // timestamps and counts before using any (one memory round trip per 64 blocks)
-  const int tid = threadIdx.x;
   for (int j0 = 0; j0 < nblk; j0 += 64) {
     const int j = j0 + (tid >> 2);
     const int k0 = j * TC_BN + (tid & 3) * 32;
@@ -77,9 +102,9 @@ __global__ void __launch_bounds__(256) schedule_kernel(const int32_t* __restrict
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         const int key = k0 + e;
-        tv[e] = seq_k + 1;  // masked lanes of a partial block
+        tv[e] = key < num_packed ? 0 : seq_k + 1;  // zero padding, or a masked lane
         cv[e] = 0.f;
-        if (key < num_packed) {
+        if (key < nreal) {
           tv[e] = tsr[static_cast<int64_t>(key) * tsn];
           const int64_t off = b * cb + h * ch + static_cast<int64_t>(key) * cn;
           cv[e] = counts_is_int ? static_cast<float>(static_cast<const int32_t*>(counts)[off])
@@ -105,10 +130,10 @@ __global__ void __launch_bounds__(256) schedule_kernel(const int32_t* __restrict
     }
     if ((tid & 3) == 0 && j < nblk) {
       sT[j] = tmax;
-      if (want_blkmin) blkmin[static_cast<int64_t>(bh) * nblk + j] = tmin;
+      if (want_blkmin) blkmin[static_cast<int64_t>(bh) * wstride + j] = tmin;
       // a block whose valid keys share one count c is weighted by adding log2(c) to the
       // exponent (exact for powers of two); mixed counts are applied per key
-      blkw[static_cast<int64_t>(bh) * nblk + j] = (cmin == cmax) ? log2f(cmin) : __int_as_float(0x7FC00000);
+      blkw[static_cast<int64_t>(bh) * wstride + j] = (cmin == cmax) ? log2f(cmin) : __int_as_float(0x7FC00000);
     }
   }
   __syncthreads();
@@ -180,8 +205,14 @@ struct TileSeq {
   int pmax, dlo, dhi;
   int state, cur;  // state 0: packed, 1: dense, 2: done
   int mb_lo[2];
+  int vblk;  // packed blocks of the unit's kv-head holding rows (later ones are zero padding)
 
-  __device__ __forceinline__ void init(const TcParams& p, const Unit& U) {
+  // `num_packed`: the packed length (the host value, or the device maximum of the heads' anchors)
+  __device__ __forceinline__ void init(const TcParams& p, const Unit& U, int num_packed) {
+    // with a device packed length, blocks past the head's own anchors are the reference's zero
+    // padding: K = V = 0 and count 0 add nothing to O or l, so they are not loaded or computed
+    // (the schedule pre-pass still counts their zero timestamps in the phase-1 stop rule)
+    vblk = p.anchors ? (p.anchors[U.b * p.Hts + U.hts[0]] + TC_BN - 1) / TC_BN : INT32_MAX;
     #pragma unroll
     for (int x = 0; x < 2; ++x) {
       n1[x] = 0; ds[x] = 0; de[x] = 0;
@@ -195,7 +226,7 @@ struct TileSeq {
         ds[x] = s.y;
         de[x] = (hi + TC_BN - 1) / TC_BN;
       } else if (p.variant == TC_PURE) {
-        n1[x] = p.nblk;
+        n1[x] = (num_packed + TC_BN - 1) / TC_BN;
       } else {
         ds[x] = 0;
         de[x] = p.causal ? (hi + TC_BN - 1) / TC_BN : (p.seq_k + TC_BN - 1) / TC_BN;
@@ -216,6 +247,7 @@ struct TileSeq {
     while (state == 0) {
       if (cur >= pmax) { state = 1; cur = dlo; break; }
       const int j = cur++;
+      if (j >= vblk) continue;  // zero padding of this head (device packed length)
       int use = 0;
       #pragma unroll
       for (int x = 0; x < 2; ++x) {
@@ -322,6 +354,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
   tc_fence_after();
   const uint32_t tmem = *tmem_base_smem;
   const Abort ab{abort_flag, p.err};
+  // the packed length: the host's, or the maximum of the heads' anchors that the schedule
+  // pre-pass (the previous launch on this stream) wrote to the workspace
+  const int num_packed = p.anchors ? *p.len_dev : p.num_packed;
   const int G = gridDim.x;
   const int n_iter = (p.num_units + G - 1) / G;
 
@@ -348,7 +383,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       }
       ++q_issued;
       TileSeq seq;
-      seq.init(p, U);
+      seq.init(p, U, num_packed);
       TileInfo t;
       while (seq.next(p, U, t)) {
         const int slot = kpos % NK;
@@ -381,7 +416,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       const Unit U = decode_unit(p, u);
       const int hk = U.hts[0];  // both tiles of a unit share the K/V head
       TileSeq seq;
-      seq.init(p, U);
+      seq.init(p, U, num_packed);
       TileInfo t;
       while (seq.next(p, U, t)) {
         if (!t.needs_v) continue;
@@ -393,7 +428,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           // the same barrier when rows are contiguous and aligned, else lane loads
           float* c = auxc + slot * TC_BN;
           int32_t* tt = auxt + slot * TC_BN;
-          const int nkeys = min(TC_BN, p.num_packed - t.idx * TC_BN);
+          // with a device packed length every row of a block the head holds is written (rows
+          // past its anchors up to the block end are zeros), so the whole block is copied
+          const int nkeys = p.anchors ? TC_BN : min(TC_BN, num_packed - t.idx * TC_BN);
           if (p.meta_bulk) {
             meta_bytes = static_cast<uint32_t>(nkeys) * 4u * (p.variant == TC_PURE ? 2u : 1u);
             if (lane == 0) {
@@ -409,7 +446,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
               const int key = t.idx * TC_BN + e;
               uint32_t cv = 0;
               int32_t tv2 = 0;
-              if (key < p.num_packed) {
+              if (p.anchors || key < num_packed) {
                 const int64_t off = U.b * p.cs_b + static_cast<int64_t>(hk) * p.cs_h + static_cast<int64_t>(key) * p.cs_n;
                 cv = static_cast<const uint32_t*>(p.counts)[off];
                 if (p.variant == TC_PURE)
@@ -517,7 +554,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         auto uses = [&](const TileInfo& t) { return mine && (t.use >> x & 1); };
 
         TileSeq seq;
-        seq.init(p, U);
+        seq.init(p, U, num_packed);
         TileInfo cur, nxt;
         bool have_cur = seq.next(p, U, cur);
         int cur_v = -1;
@@ -616,7 +653,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       float m_used = -INFINITY, l = 0.f;
       bool o_has = false;
       TileSeq seq;
-      seq.init(p, U);
+      seq.init(p, U, num_packed);
       const float* wrow = p.blkw + (static_cast<int64_t>(U.b) * p.Hts + U.hts[x]) * p.nblk;
       TileInfo t;
       bool ok = true;
@@ -652,7 +689,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             for (int e = 0; e < 32; ++e) {
               const int j = w * 32 + e;
               const float cj = cint ? static_cast<float>(static_cast<int32_t>(cnt[j])) : __uint_as_float(cnt[j]);
-              const bool v = (n0 + j < p.num_packed) && cj > 0.f && tsv[j] <= row;
+              const bool v = (n0 + j < num_packed) && cj > 0.f && tsv[j] <= row;
               bits |= (v ? 1u : 0u) << e;
             }
             if (w == 0) vm[0] = bits; else if (w == 1) vm[1] = bits; else if (w == 2) vm[2] = bits; else vm[3] = bits;
@@ -661,7 +698,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         int lim = TC_BN;
         if (p.variant != TC_PURE) {
           if (t.packed) {
-            lim = p.num_packed - n0;
+            lim = num_packed - n0;
           } else {
             lim = p.seq_k - n0;
             if (p.variant != TC_DENSE || p.causal) lim = min(lim, row - n0 + 1);
@@ -932,7 +969,7 @@ cudaError_t launch_attn_tc(int head_dim, bool bf16, const TcParams& p, int num_s
 cudaError_t launch_schedule(const int32_t* ts, const int64_t* tss, const void* counts, const int64_t* cs,
                             int counts_is_int, int B, int Hts, int num_packed, int seq_k, int window, int nmb,
                             int nblk, int2* sched, int32_t* blkmin, int want_blkmin, float* blkw,
-                            cudaStream_t st) {
+                            const int32_t* anchors, int* len_out, cudaStream_t st) {
   if (B * Hts == 0) return cudaSuccess;
   const size_t sm = static_cast<size_t>(nblk > 0 ? nblk : 1) * sizeof(int32_t);
   if (sm > 200 * 1024) return cudaErrorInvalidValue;
@@ -943,7 +980,7 @@ cudaError_t launch_schedule(const int32_t* ts, const int64_t* tss, const void* c
   }
   schedule_kernel<<<B * Hts, 256, sm, st>>>(ts, tss[0], tss[1], tss[2], counts, cs[0], cs[1], cs[2], counts_is_int,
                                             Hts, num_packed, seq_k, window, nmb, nblk, sched, blkmin, want_blkmin,
-                                            blkw);
+                                            blkw, anchors, B * Hts, len_out);
   return cudaGetLastError();
 }
 

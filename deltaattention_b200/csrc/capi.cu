@@ -6,6 +6,7 @@
 // passed in by the caller (sizes from the *_workspace_size functions).
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <string>
 
@@ -30,7 +31,7 @@ cudaError_t launch_pack_from_keep(int, const int32_t*, const int64_t*, const voi
 cudaError_t launch_attn_simt(int, const SimtParams&, cudaStream_t);
 cudaError_t launch_attn_tc(int, bool, const TcParams&, int, cudaStream_t);
 cudaError_t launch_schedule(const int32_t*, const int64_t*, const void*, const int64_t*, int, int, int, int, int,
-                            int, int, int, int2*, int32_t*, int, float*, cudaStream_t);
+                            int, int, int, int2*, int32_t*, int, float*, const int32_t*, int*, cudaStream_t);
 cudaError_t launch_decode_update(int, int, bool, const void*, const void*, void*, void*, void*, void*, int32_t*,
                                  int32_t*, int32_t*, int64_t, int64_t, const int64_t*, float, int64_t, const int64_t*,
                                  const int64_t*, const int64_t*, const int64_t*, int64_t, int64_t, int64_t, int64_t,
@@ -44,6 +45,8 @@ cudaError_t launch_decode_advance(int64_t*, int64_t, cudaStream_t);
 size_t decode_attn_workspace(int64_t, int64_t, int64_t, int64_t, int64_t);
 cudaError_t launch_nm_select(int, const void*, const int64_t*, int32_t*, const int64_t*, int64_t, int64_t, int64_t,
                              int64_t, int, int, int64_t, cudaStream_t);
+cudaError_t launch_key_compress(int, int, bool, CompressParams, cudaStream_t);
+size_t key_compress_workspace(int64_t, int64_t, int64_t, int64_t);
 }  // namespace dab
 
 using namespace dab;
@@ -186,7 +189,8 @@ static int run_attention(int variant, int causal, const void* q, const void* kd,
                          float sm_scale, int64_t seq_q, int64_t seq_k, int64_t num_packed, int64_t head_dim,
                          int64_t num_heads, int64_t window, int64_t grid_m, int64_t grid_bh, int64_t block_m,
                          int64_t block_n, int64_t block_d, int64_t kv_group, void* workspace,
-                         size_t workspace_bytes, int force_simt, cudaStream_t st, const char* name) {
+                         size_t workspace_bytes, int force_simt, cudaStream_t st, const char* name,
+                         const int32_t* anchors = nullptr) {
   if (!q || !kd || !vd || !out) return fail(1, std::string(name) + ": null pointer");
   if (num_heads <= 0 || kv_group <= 0 || num_heads % kv_group) return fail(1, std::string(name) + ": bad heads");
   if (grid_bh % num_heads) return fail(1, std::string(name) + ": grid must cover whole batches of heads");
@@ -208,6 +212,15 @@ static int run_attention(int variant, int causal, const void* q, const void* kd,
   if (needs_packed && num_packed > 0) tc = tc && kps[3] == 1 && vps[3] == 1 && aligned16(kp) && aligned16(vp);
   const size_t need_ws = dab_hybrid_flash_workspace_size(B, Hts, seq_q, num_packed);
   if (tc && (!workspace || workspace_bytes < need_ws)) tc = false;
+  if (anchors) {
+    // device packed length: tcgen05 path only, and the capacity a whole number of blocks (every
+    // block a head holds is read whole; its rows past the anchors are zeros)
+    if (!tc || !needs_packed || num_packed <= 0 || num_packed % 128)
+      return fail(1, std::string(name) +
+                         ": the device packed length needs the tcgen05 path (bf16 / fp16, head_dim 64 / 128, "
+                         "128 x 128 blocks, unit inner strides, 16-byte aligned rows, a large enough workspace) "
+                         "and a capacity that is a positive multiple of 128");
+  }
   if (tc) {
     TcParams p;
     std::memset(&p, 0, sizeof(p));
@@ -244,6 +257,8 @@ static int run_attention(int variant, int causal, const void* q, const void* kd,
       p.num_units = static_cast<int>(p.pair_heads ? nmb * B * Hts * (kv_group / 2) : ((nmb + 1) / 2) * B * num_heads);
       p.out_vec_ok = aligned16(out) && (os[0] * 2) % 16 == 0 && (os[1] * 2) % 16 == 0 && (os[2] * 2) % 16 == 0;
       // counts (and timestamps) rows: contiguous along keys with 16-byte aligned block starts
+      p.anchors = anchors;
+      p.len_dev = reinterpret_cast<const int*>(ws + 4);  // header word 1: the device packed length
       p.meta_bulk = needs_packed && num_packed > 0 && counts && cs && cs[2] == 1 && num_packed % 4 == 0 &&
                     aligned16(counts) && (cs[0] * 4) % 16 == 0 && (cs[1] * 4) % 16 == 0 &&
                     (variant != 2 || (ts && tss && tss[2] == 1 && aligned16(ts) && (tss[0] * 4) % 16 == 0 &&
@@ -254,7 +269,7 @@ static int run_attention(int variant, int causal, const void* q, const void* kd,
                                         static_cast<int>(window), static_cast<int>(nmb), static_cast<int>(nblk),
                                         reinterpret_cast<int2*>(ws + WS_HEADER),
                                         reinterpret_cast<int32_t*>(const_cast<int32_t*>(p.blkmin)), variant == 2,
-                                        const_cast<float*>(p.blkw), st);
+                                        const_cast<float*>(p.blkw), anchors, reinterpret_cast<int*>(ws + 4), st);
         if (e != cudaSuccess) return cuda_status(e, "schedule");
       } else if (variant != 3) {
         // no packed keys: phase 1 is empty and phase 2 starts at key 0
@@ -298,6 +313,24 @@ int dab_hybrid_flash(int variant, const void* q, const void* k_dense, const void
                        sm_scale, seq_len_q, seq_len_k, num_packed, head_dim, num_heads, dense_window, grid_m,
                        grid_bh, block_m, block_n, block_d, kv_group, workspace, workspace_bytes, force_simt,
                        static_cast<cudaStream_t>(stream), "hybrid_flash");
+}
+
+int dab_hybrid_flash_devlen(int variant, const void* q, const void* k_dense, const void* v_dense,
+                            const void* k_packed, const void* v_packed, const int32_t* packed_ts,
+                            const void* packed_counts, int counts_is_int, const int32_t* anchors_per_head,
+                            void* out, int dtype, const int64_t* strides, float sm_scale, int64_t seq_len_q,
+                            int64_t seq_len_k, int64_t capacity, int64_t head_dim, int64_t num_heads,
+                            int64_t dense_window, int64_t grid_m, int64_t grid_bh, int64_t block_m, int64_t block_n,
+                            int64_t block_d, int64_t kv_group, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  if (variant < 0 || variant > 2) return fail(1, "dab_hybrid_flash_devlen: variant must be 0, 1 or 2");
+  if (!strides || !anchors_per_head) return fail(1, "dab_hybrid_flash_devlen: null strides / anchors");
+  const int64_t* s = strides;
+  return run_attention(variant, 1, q, k_dense, v_dense, k_packed, v_packed, packed_ts, packed_counts,
+                       counts_is_int, out, dtype, s + 0, s + 4, s + 8, s + 12, s + 16, s + 20, s + 23, s + 26,
+                       sm_scale, seq_len_q, seq_len_k, capacity, head_dim, num_heads, dense_window, grid_m,
+                       grid_bh, block_m, block_n, block_d, kv_group, workspace, workspace_bytes, 0,
+                       static_cast<cudaStream_t>(stream), "hybrid_flash_devlen", anchors_per_head);
 }
 
 // Static scratch of dab_hybrid_flash_noalloc (one copy per device, zeroed at module load).
@@ -549,6 +582,68 @@ int dab_pack_from_keep(const int32_t* keep_mask, const int64_t* km_strides, cons
                                            static_cast<int32_t*>(workspace), anchors_per_head, max_anchors,
                                            static_cast<cudaStream_t>(stream)),
                      "pack_from_keep");
+}
+
+size_t dab_delta_compress_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t chunk_size) {
+  return key_compress_workspace(batch, heads, seq_len, chunk_size);
+}
+
+int dab_delta_compress(const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                       const void* cos_t, const void* sin_t, const int64_t* cs_strides, void* k_rot,
+                       const int64_t* rot_strides, int32_t* keep_mask, const int64_t* km_strides, void* k_packed,
+                       void* v_packed, const int64_t* pack_strides, int32_t* packed_ts, int32_t* packed_counts,
+                       float* packed_counts_f32, const int64_t* meta_strides, int32_t* anchors_per_head, int dtype,
+                       int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, float threshold_sq,
+                       int use_cosine, int64_t chunk_size, int64_t capacity, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  const char* nm = "dab_delta_compress";
+  if (!k || !v || !cos_t || !sin_t || !k_rot || !k_packed || !v_packed || !packed_ts || !packed_counts ||
+      !anchors_per_head || !workspace || !k_strides || !v_strides || !cs_strides || !rot_strides || !pack_strides ||
+      !meta_strides || (keep_mask && !km_strides))
+    return fail(1, std::string(nm) + ": null pointer");
+  if (dtype != BF16 && dtype != F16) return fail(1, std::string(nm) + ": keys must be bf16 or fp16");
+  if (head_dim != 64 && head_dim != 128) return fail(1, std::string(nm) + ": head_dim must be 64 or 128");
+  if (chunk_size < 1 || chunk_size > 1024) return fail(1, std::string(nm) + ": chunk_size must be in [1, 1024]");
+  if (batch < 0 || heads < 0 || seq_len < 0 || capacity < 0 || seq_len >= (int64_t{1} << 31) ||
+      capacity >= (int64_t{1} << 31))
+    return fail(1, std::string(nm) + ": bad sizes");
+  if (workspace_bytes < key_compress_workspace(batch, heads, seq_len, chunk_size))
+    return fail(1, std::string(nm) + ": workspace too small");
+  // 16-byte rows everywhere: unit inner strides, 16-byte aligned bases and row / head / batch strides
+  auto ok16 = [](const void* ptr, std::initializer_list<int64_t> strides) {
+    if (reinterpret_cast<uintptr_t>(ptr) & 15) return false;
+    for (int64_t st : strides)
+      if ((st * 2) % 16) return false;
+    return true;
+  };
+  if (k_strides[3] != 1 || v_strides[3] != 1 || cs_strides[2] != 1 || rot_strides[3] != 1 || pack_strides[3] != 1 ||
+      meta_strides[2] != 1 || !ok16(k, {k_strides[0], k_strides[1], k_strides[2]}) ||
+      !ok16(v, {v_strides[0], v_strides[1], v_strides[2]}) || !ok16(cos_t, {cs_strides[0], cs_strides[1]}) ||
+      !ok16(sin_t, {cs_strides[0], cs_strides[1]}) || !ok16(k_rot, {rot_strides[0], rot_strides[1], rot_strides[2]}) ||
+      !ok16(k_packed, {pack_strides[0], pack_strides[1], pack_strides[2]}) ||
+      !ok16(v_packed, {pack_strides[0], pack_strides[1], pack_strides[2]}))
+    return fail(1, std::string(nm) + ": every row must be contiguous and 16-byte aligned");
+  const int64_t nch = (seq_len + chunk_size - 1) / chunk_size;
+  CompressParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.k = k; p.ks_b = k_strides[0]; p.ks_h = k_strides[1]; p.ks_s = k_strides[2];
+  p.v = v; p.vs_b = v_strides[0]; p.vs_h = v_strides[1]; p.vs_s = v_strides[2];
+  p.cos = cos_t; p.sin = sin_t; p.cs_b = cs_strides[0]; p.cs_s = cs_strides[1];
+  p.k_rot = k_rot; p.rs_b = rot_strides[0]; p.rs_h = rot_strides[1]; p.rs_s = rot_strides[2];
+  p.keep = keep_mask;
+  if (keep_mask) { p.km_b = km_strides[0]; p.km_h = km_strides[1]; p.km_s = km_strides[2]; }
+  p.kp = k_packed; p.vp = v_packed; p.ps_b = pack_strides[0]; p.ps_h = pack_strides[1]; p.ps_s = pack_strides[2];
+  p.ts = packed_ts; p.cnt = packed_counts; p.cnt_f = packed_counts_f32; p.ms_b = meta_strides[0];
+  p.ms_h = meta_strides[1];
+  p.anchors = anchors_per_head;
+  p.ws = static_cast<uint8_t*>(workspace);
+  p.thr = threshold_sq;
+  p.H = static_cast<int>(heads); p.N = static_cast<int>(seq_len); p.chunk = static_cast<int>(chunk_size);
+  p.nch = static_cast<int>(nch); p.cap = static_cast<int>(capacity);
+  p.total_chunks = static_cast<unsigned>(batch * heads * nch);
+  return cuda_status(launch_key_compress(dtype, static_cast<int>(head_dim), use_cosine != 0, p,
+                                         static_cast<cudaStream_t>(stream)),
+                     "delta_compress");
 }
 
 int64_t dab_nm_num_packed(int64_t seq_len, int64_t n_keep, int64_t m_group, int64_t stride) {

@@ -41,6 +41,27 @@ struct TcParams {
   int num_units;
   int out_vec_ok;          // output rows are 16-byte aligned with unit d-stride
   int meta_bulk;           // counts / timestamps rows can be bulk-copied (contiguous, 16-byte aligned)
+  // device-resident packed length (null: num_packed above is the packed length). anchors[b*Hts+h]
+  // is the kept count of each head, len_dev[0] their maximum M (the reference's packed length,
+  // written by the schedule pre-pass); num_packed / nblk then give the buffers' capacity.
+  const int32_t* anchors;
+  const int* len_dev;
+};
+
+// fused key compression (compress.cu): strides in elements
+struct CompressParams {
+  const void* k; int64_t ks_b, ks_h, ks_s;        // raw keys [B, H, N, D]
+  const void* v; int64_t vs_b, vs_h, vs_s;        // values [B, H, N, D]
+  const void* cos; const void* sin; int64_t cs_b, cs_s;  // RoPE tables [B or 1, N, D]
+  void* k_rot; int64_t rs_b, rs_h, rs_s;          // rotated keys out
+  int32_t* keep; int64_t km_b, km_h, km_s;        // keep mask out (may be null)
+  void* kp; void* vp; int64_t ps_b, ps_h, ps_s;   // packed K / V [B, H, cap, D]
+  int32_t* ts; int32_t* cnt; float* cnt_f; int64_t ms_b, ms_h;  // packed metadata [B, H, cap]
+  int32_t* anchors;                               // [B * H] kept count per head
+  uint8_t* ws;                                    // workspace: header, then a status word per chunk
+  float thr;                                      // squared-distance (or cosine) threshold
+  int H, N, chunk, nch, cap;
+  unsigned total_chunks, total_warps;
 };
 
 }  // namespace dab

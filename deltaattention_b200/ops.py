@@ -8,8 +8,9 @@ GQA expansion, two-phase attention) with these B200-specific changes:
   of modeling_llama.py:700-708 are gone;
 * periodic packing is a strided view of the rotated keys / values (row stride x period), so
   nothing is copied; timestamps and counts come from one tiny kernel;
-* delta / explicit keep masks pack on the device; the only host sync is the reference's
-  own read of the packed length (modeling_llama.py:656);
+* delta selection, with RoPE(k) and packing, is one launch whose packed length stays on the
+  device (no host sync); explicit keep masks pack on the device with the reference's one read
+  of the packed length (modeling_llama.py:656);
 * the output can be written straight into the ``[B, N, H, d]`` layout ``o_proj`` consumes.
 """
 from __future__ import annotations
@@ -48,18 +49,45 @@ def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: Optional[to
 
 @dataclass
 class Packed:
-    """Packed history of one layer: K/V rows, anchor timestamps and run-length counts."""
-    k: torch.Tensor          # [B, Hkv, M, d] (possibly a strided view)
+    """Packed history of one layer: K/V rows, anchor timestamps and run-length counts.
+
+    With ``anchors`` set (device packing without a host sync) the tensors have a capacity of
+    rows per head and ``anchors`` [B * Hkv] int32 holds each head's kept count on the device;
+    the reference's packed length is their maximum (``packed_length()`` reads it back)."""
+    k: torch.Tensor          # [B, Hkv, M, d] (possibly a strided view), or [B, Hkv, capacity, d]
     v: torch.Tensor
     timestamps: torch.Tensor  # [B, Hkv, M] int32
     counts: torch.Tensor      # [B, Hkv, M] int32 (the reference's format)
     keep_mask: Optional[torch.Tensor] = None
     counts_f32: Optional[torch.Tensor] = None  # the same counts as fp32 (what attention weights with)
+    anchors: Optional[torch.Tensor] = None     # [B * Hkv] int32 kept count per head (device length)
 
     def weights(self) -> torch.Tensor:
         if self.counts_f32 is None:
             self.counts_f32 = self.counts.float()
         return self.counts_f32
+
+    def packed_length(self) -> int:
+        """The reference's packed length M (a host read when the length lives on the device)."""
+        if self.anchors is None:
+            return self.k.shape[2]
+        return int(self.anchors.max().item())
+
+    def materialize(self) -> "Packed":
+        """The reference's packed tensors (modeling_llama.py:655-685): every head cut to the
+        packed length M, slots past its own anchors zero (K, V, timestamp, count). The packing
+        itself when the length is already on the host; otherwise one host read of M."""
+        if self.anchors is None:
+            return self
+        M = self.packed_length()
+        B, H = self.k.shape[:2]
+        valid = torch.arange(M, device=self.k.device)[None, None, :] < self.anchors.view(B, H, 1)
+        zero = torch.zeros((), dtype=self.k.dtype, device=self.k.device)
+        k = torch.where(valid[..., None], self.k[:, :, :M], zero)
+        v = torch.where(valid[..., None], self.v[:, :, :M], zero)
+        ts = torch.where(valid, self.timestamps[:, :, :M], 0).to(torch.int32)
+        cnt = torch.where(valid, self.counts[:, :, :M], 0).to(torch.int32)
+        return Packed(k, v, ts, cnt, self.keep_mask)
 
 
 def pack_periodic(k_rot: torch.Tensor, v: torch.Tensor, period: int) -> Packed:
@@ -130,6 +158,57 @@ def pack_from_keep(k_rot: torch.Tensor, v: torch.Tensor, keep: torch.Tensor, num
     return p
 
 
+def delta_compress(k, v, cos, sin, threshold: float, similarity: str = "euclidean", chunk_size: int = 512,
+                   capacity: Optional[int] = None, want_keep_mask: bool = True):
+    """RoPE, delta selection and packing of one layer's keys in one launch, with no host sync
+    (modeling_llama.py:555 + :600-685; the reference reads the packed length back at :656).
+
+    k / v [B, Hkv, N, d] pre-RoPE keys and values (any 16-byte-aligned row layout, e.g. the
+    projection layout); cos / sin [1 or B, N, d]. ``threshold`` is the raw threshold as in
+    ``delta_keep_mask`` (squared for Euclidean). Returns (rotated keys [B, Hkv, N, d], Packed
+    with ``anchors`` on the device and ``capacity`` rows per head, default N rounded up to 128).
+    """
+    L.require_cuda(k, v, cos, sin)
+    B, H, N, D = k.shape
+    cap = int(capacity) if capacity is not None else max(128, -(-N // 128) * 128)
+    dev = k.device
+    use_cos = similarity == "cosine"
+    thr = threshold if use_cos else threshold ** 2
+    cs = min(chunk_size, N) if chunk_size > 0 else N
+    k_rot = torch.empty((B, H, N, D), dtype=k.dtype, device=dev)
+    kp = torch.empty((B, H, cap, D), dtype=k.dtype, device=dev)
+    vp = torch.empty_like(kp)
+    ts = torch.empty((B, H, cap), dtype=torch.int32, device=dev)
+    cnt = torch.empty_like(ts)
+    cnt_f = torch.empty((B, H, cap), dtype=torch.float32, device=dev)
+    anchors = torch.empty((B * H,), dtype=torch.int32, device=dev)
+    keep = torch.empty((B, H, N), dtype=torch.int32, device=dev) if want_keep_mask else None
+    if cos.stride() != sin.stride():
+        cos, sin = cos.contiguous(), sin.contiguous()
+    cb = cos.stride(0) if cos.shape[0] > 1 else 0
+    lib = L.load()
+    st = L.stream_of(k)
+    ws = L.workspace(dev, st.value, lib.dab_delta_compress_workspace_size(B, H, N, cs), tag="compress")
+    L.check(lib.dab_delta_compress(
+        L.ptr(k), L.strides(k.stride()), L.ptr(v), L.strides(v.stride()), L.ptr(cos), L.ptr(sin),
+        L.strides([cb, cos.stride(1), cos.stride(2)]), L.ptr(k_rot), L.strides(k_rot.stride()), L.ptr(keep),
+        L.strides(keep.stride() if keep is not None else (0, 0, 0)), L.ptr(kp), L.ptr(vp), L.strides(kp.stride()),
+        L.ptr(ts), L.ptr(cnt), L.ptr(cnt_f), L.strides(ts.stride()), L.ptr(anchors), L.dtype_code(k), B, H, N, D,
+        float(thr), 1 if use_cos else 0, cs, cap, L.ptr(ws), ws.numel(), st), "delta_compress")
+    return k_rot, Packed(kp, vp, ts, cnt, keep, counts_f32=cnt_f, anchors=anchors)
+
+
+def fused_delta_ok(k, v, cos) -> bool:
+    """Whether ``delta_compress`` and the device-length attention take these tensors (bf16 /
+    fp16, head_dim 64 / 128, contiguous 16-byte-aligned rows)."""
+    if k.dtype not in (torch.bfloat16, torch.float16) or k.shape[-1] not in (64, 128):
+        return False
+    for t in (k, v, cos):
+        if t.stride(-1) != 1 or t.data_ptr() % 16 or any((st * 2) % 16 for st in t.stride()[:-1]):
+            return False
+    return True
+
+
 def attention(q_rot, k_rot, v, packed: Optional[Packed], *, sm_scale=None, dense_window=128,
               variant="hybrid", out=None, force_simt=False):
     """Two-phase count-weighted attention (deltaFlashAttention.py:9-357) with GQA by index.
@@ -158,6 +237,16 @@ def attention(q_rot, k_rot, v, packed: Optional[Packed], *, sm_scale=None, dense
     bd = 1 << max(4, (D - 1).bit_length())
     strides = [*q_rot.stride(), *k_rot.stride(), *v.stride(), *kp.stride(), *vp.stride(), *ts.stride(),
                *cnt.stride(), *out.stride()]
+    if packed is not None and packed.anchors is not None:
+        # packed length on the device (capacity rows per head; M = max of the anchors)
+        if force_simt:
+            raise ValueError("attention: a device packed length runs on the tcgen05 kernel only")
+        L.check(lib.dab_hybrid_flash_devlen(
+            VARIANTS[variant], L.ptr(q_rot), L.ptr(k_rot), L.ptr(v), L.ptr(kp), L.ptr(vp), L.ptr(ts), L.ptr(cnt),
+            1 if cnt.dtype == torch.int32 else 0, L.ptr(packed.anchors), L.ptr(out), L.dtype_code(q_rot),
+            L.strides(strides), float(sm_scale), N, k_rot.shape[2], M, D, Hq, int(dense_window), -(-N // 128),
+            B * Hq, 128, 128, bd, Hq // Hkv, L.ptr(ws), ws.numel(), st), "attention")
+        return out
     L.check(lib.dab_hybrid_flash(
         VARIANTS[variant], L.ptr(q_rot), L.ptr(k_rot), L.ptr(v), L.ptr(kp), L.ptr(vp), L.ptr(ts), L.ptr(cnt),
         1 if cnt.dtype == torch.int32 else 0, L.ptr(out), L.dtype_code(q_rot), L.strides(strides), float(sm_scale),
@@ -189,25 +278,34 @@ def flash(q_rot, k_rot, v, *, causal=True, sm_scale=None, out=None, force_simt=F
 
 def delta_prefill(q, k, v, cos, sin, *, mode="periodic", keep_rate=0.25, threshold=None,
                   similarity="euclidean", chunk_size=512, dense_window=128, variant="hybrid", sm_scale=None,
-                  out=None, keep_mask=None, return_packed=False):
+                  out=None, keep_mask=None, return_packed=False, fused=True):
     """The whole delta-attention prefill layer-op on pre-RoPE q / k and v.
 
     q [B, Hq, N, d], k / v [B, Hkv, N, d] (any strides, e.g. the [B, N, H, d] projection
     layout viewed with transpose(1, 2)). mode: 'periodic' (keep t % round(1/keep_rate) == 0),
     'delta' (threshold selection in chunks of ``chunk_size``) or 'mask' (``keep_mask``).
+    In delta mode with bf16 / fp16 keys of head_dim 64 / 128 (and ``fused``), RoPE(k),
+    selection and packing are one launch (``delta_compress``) and the packed length stays on
+    the device, so the layer-op makes no host sync; otherwise they run as separate kernels and
+    the packed length is read back as the reference does (modeling_llama.py:656).
     Returns the attention output [B, Hq, N, d] (and the packed history when requested).
     """
     L.require_cuda(q, k, v, cos, sin)
     q_rot = rope(q, cos, sin)
-    k_rot = rope(k, cos, sin)
+    fused_delta = mode == "delta" and fused and fused_delta_ok(k, v, cos)
+    k_rot = None if fused_delta else rope(k, cos, sin)
     if mode == "periodic":
         period = max(1, round(1.0 / keep_rate))
         packed = pack_periodic(k_rot, v, period)
     elif mode == "delta":
         if threshold is None:
             raise ValueError("delta mode needs a threshold")
-        keep, _ = delta_keep_mask(k_rot, threshold, similarity, chunk_size)
-        packed = pack_from_keep(k_rot, v, keep)
+        if fused_delta:
+            # one launch for RoPE(k), selection and packing; the packed length stays on the device
+            k_rot, packed = delta_compress(k, v, cos, sin, threshold, similarity, chunk_size)
+        else:
+            keep, _ = delta_keep_mask(k_rot, threshold, similarity, chunk_size)
+            packed = pack_from_keep(k_rot, v, keep)
     elif mode == "mask":
         packed = pack_from_keep(k_rot, v, keep_mask.to(torch.int32))
     else:

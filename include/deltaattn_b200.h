@@ -91,6 +91,25 @@ int dab_hybrid_flash(int variant, const void* q, const void* k_dense, const void
                      int64_t grid_m, int64_t grid_bh, int64_t block_m, int64_t block_n, int64_t block_d,
                      int64_t kv_group, void* workspace, size_t workspace_bytes, int force_simt, void* stream);
 
+/* dab_hybrid_flash with the packed length kept on the device (native: the reference reads it
+ * back to size the packed tensors, modeling_llama.py:655-656). `anchors_per_head` [B * Hts]
+ * int32 holds every (batch, kv-head)'s kept count; the packed length M is their maximum,
+ * taken on the device, and results equal dab_hybrid_flash on the same tensors cut to M rows.
+ * The packed tensors (K/V, timestamps, counts) have `capacity` rows, a multiple of 128 and at
+ * least M. For each head, rows [anchors, ceil(anchors / 128) * 128) must hold zero K / V,
+ * timestamp 0 and count 0 (dab_delta_compress writes them); later rows are not read: rows
+ * [anchors, M) are the reference's zero padding, scheduled (their zero timestamps enter the
+ * phase-1 stop rule) but not loaded. The workspace is sized with num_packed = capacity.
+ * tcgen05 path only (bf16 / fp16, head_dim 64 / 128, 128 x 128 blocks); other calls return 1. */
+int dab_hybrid_flash_devlen(int variant, const void* q, const void* k_dense, const void* v_dense,
+                            const void* k_packed, const void* v_packed, const int32_t* packed_ts,
+                            const void* packed_counts, int counts_is_int, const int32_t* anchors_per_head,
+                            void* out, int dtype, const int64_t* strides, float sm_scale, int64_t seq_len_q,
+                            int64_t seq_len_k, int64_t capacity, int64_t head_dim, int64_t num_heads,
+                            int64_t dense_window, int64_t grid_m, int64_t grid_bh, int64_t block_m, int64_t block_n,
+                            int64_t block_d, int64_t kv_group, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
 /* Bytes of the library's static device scratch behind dab_hybrid_flash_noalloc. */
 #define DAB_NOALLOC_SCRATCH_BYTES (1u << 20)
 
@@ -224,6 +243,35 @@ int dab_pack_from_keep(const int32_t* keep_mask, const int64_t* km_strides, cons
                        const int64_t* meta_strides, int32_t* index_map, int dtype, int64_t batch, int64_t heads,
                        int64_t seq_len, int64_t head_dim, int64_t capacity, int32_t* anchors_per_head,
                        int32_t* max_anchors, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scratch bytes dab_delta_compress needs (a 256-byte header, then 8 bytes per chunk). The
+ * scratch must be zeroed once before its first use; the kernel leaves it ready for the next
+ * call, so one scratch serves successive calls on one stream (not concurrent calls). */
+size_t dab_delta_compress_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t chunk_size);
+
+/* Threshold ("row" delta) key compression in one launch: apply_rotary_pos_emb on the raw keys
+ * (modeling_llama.py:180-204, eager rounding, bit-identical to dab_rope) written to k_rot;
+ * chunked_eval_kernel's selection on the rotated keys (tritonModules.py:7-69: squared Euclidean
+ * distance > threshold_sq, or cosine < threshold_sq with use_cosine; bit-exact keep decisions,
+ * written to keep_mask when it is not NULL); and the packing of modeling_llama.py:655-685 (K rows
+ * from the rotated keys, V rows, timestamps, run-length counts as int32 and, when not NULL,
+ * fp32), with the packed length left on the device: anchors_per_head[B * H] receives every
+ * head's kept count (the reference's M = their maximum, modeling_llama.py:656, is taken by
+ * dab_hybrid_flash_devlen on the device). Packed buffers have `capacity` rows per head (keep
+ * it >= seq_len); for each head, rows [anchors, min(capacity, ceil(anchors / 128) * 128))
+ * are written as zero K / V, timestamp 0 and count 0; later rows are left untouched.
+ * Strides: k, v, k_rot, packed K / V (b, h, s, d); cos / sin (b, s, d), b-stride 0 broadcasts;
+ * keep mask and packed metadata (b, h, s). Rows must be contiguous and 16-byte aligned,
+ * bf16 / fp16, head_dim 64 or 128, chunk_size <= 1024. A bounded wait that times out or a
+ * capacity overflow sets the workspace's first word (dab_workspace_error reads it). */
+int dab_delta_compress(const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                       const void* cos_t, const void* sin_t, const int64_t* cs_strides, void* k_rot,
+                       const int64_t* rot_strides, int32_t* keep_mask, const int64_t* km_strides, void* k_packed,
+                       void* v_packed, const int64_t* pack_strides, int32_t* packed_ts, int32_t* packed_counts,
+                       float* packed_counts_f32, const int64_t* meta_strides, int32_t* anchors_per_head, int dtype,
+                       int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, float threshold_sq,
+                       int use_cosine, int64_t chunk_size, int64_t capacity, void* workspace,
+                       size_t workspace_bytes, void* stream);
 
 /* N:M structured anchor selection (nmDeltaFlashAttention; the reference ships only a
  * compiled module for it, so the semantics are this library's own): candidates are the

@@ -94,9 +94,12 @@ def test_delta_mode_cfg2_length_matches_oracle(threshold):
     cos, sin = synth.rope_tables(N, D, 5e5, torch.bfloat16)
     out, packed, k_rot = ops.delta_prefill(q.cuda(), k.cuda(), v.cuda(), cos.cuda(), sin.cuda(), mode="delta",
                                            threshold=threshold, chunk_size=512, return_packed=True)
+    assert packed.anchors is not None  # the fused, device-length path
+    packed = packed.materialize()
     heads = [0, 5]
     q_ref = O.apply_rope(q[:, heads].contiguous(), cos, sin)
     k_ref = O.apply_rope(k.contiguous(), cos, sin)
+    assert torch.equal(k_rot.cpu().view(torch.int16), k_ref.view(torch.int16))
     keep, _ = O.delta_keep_mask(k_ref, threshold ** 2, False, 512, N // 512)
     np.testing.assert_array_equal(packed.keep_mask.cpu().numpy(), keep.numpy())
     _, kp, vp, ts, cnt = O.pack_from_keep(k_ref, v.contiguous(), keep)

@@ -403,6 +403,7 @@ def test_native_gqa_prefill_matches_oracle(mode):
                                                                           chunk_size=512)
     out, packed, k_rot = ops.delta_prefill(q.cuda(), k.cuda(), v.cuda(), cos.cuda(), sin.cuda(), return_packed=True,
                                            **kw)
+    packed = packed.materialize()
     q_ref = O.apply_rope(q.contiguous(), cos, sin)
     k_ref = O.apply_rope(k.contiguous(), cos, sin)
     np.testing.assert_array_equal(k_rot.float().cpu().numpy(), k_ref.float().numpy())
@@ -421,20 +422,45 @@ def test_native_gqa_prefill_matches_oracle(mode):
 
 
 @pytest.mark.parametrize("threshold", [8.0, 11.0, 14.0])
-def test_delta_mode_tc_matches_simt(threshold):
-    """Threshold-selected anchors carry different run-length counts within a block (the
-    tcgen05 kernel's per-key-count path); it agrees with the CUDA-core kernel within the bf16
-    tolerance at N=4096, GQA 4:1."""
+def test_delta_mode_fused_matches_separate_kernels_and_oracle(threshold):
+    """The fused key compression (RoPE + scan + packing in one launch, packed length on the
+    device) against the separate RoPE / scan / pack kernels with the host length: rotated keys,
+    keep mask, anchors and every packed row bit-identical, rows past each head's anchors zero up
+    to its block end; the device-length attention equals the host-length call on the same
+    packing, and both match the oracle within the bf16 tolerance (N = 4096, GQA 4:1)."""
     from deltaattention_b200 import ops, synth
     B, Hq, Hkv, N, D = 1, 8, 2, 4096, 128
     q, k, v = synth.layer_inputs(B, Hq, Hkv, N, D, torch.bfloat16, seed=33, device="cuda")
     cos, sin = synth.rope_tables(N, D, 5e5, torch.bfloat16, device="cuda")
-    out, packed, k_rot = ops.delta_prefill(q, k, v, cos, sin, mode="delta", threshold=threshold, return_packed=True)
-    c = packed.counts
+    out, pk, k_rot = ops.delta_prefill(q, k, v, cos, sin, mode="delta", threshold=threshold, return_packed=True)
+    out2, pk2, k_rot2 = ops.delta_prefill(q, k, v, cos, sin, mode="delta", threshold=threshold, return_packed=True,
+                                          fused=False)
+    assert pk.anchors is not None and pk2.anchors is None
+    assert torch.equal(k_rot.view(torch.int16), k_rot2.view(torch.int16))
+    assert torch.equal(pk.keep_mask, pk2.keep_mask)
+    A = pk.anchors.view(B, Hkv).cpu()
+    assert torch.equal(A, pk2.keep_mask.sum(-1).cpu().int())
+    for h in range(Hkv):
+        a = int(A[0, h])
+        z = min(pk.k.shape[2], -(-a // 128) * 128)
+        assert torch.equal(pk.k[0, h, :a].view(torch.int16), pk2.k[0, h, :a].view(torch.int16))
+        assert torch.equal(pk.v[0, h, :a].view(torch.int16), pk2.v[0, h, :a].view(torch.int16))
+        assert torch.equal(pk.timestamps[0, h, :a], pk2.timestamps[0, h, :a])
+        assert torch.equal(pk.counts[0, h, :a], pk2.counts[0, h, :a])
+        assert (pk.k[0, h, a:z] == 0).all() and (pk.v[0, h, a:z] == 0).all()
+        assert (pk.timestamps[0, h, a:z] == 0).all() and (pk.counts[0, h, a:z] == 0).all()
+    m = pk.materialize()
+    assert torch.equal(m.timestamps, pk2.timestamps) and torch.equal(m.counts, pk2.counts)
+    c = m.counts
     assert (c[:, :, :128].amax(-1) != c[:, :, :128].amin(-1)).any(), "counts should differ within a block"
-    q_rot = ops.rope(q, cos, sin)
-    ref = ops.attention(q_rot, k_rot, v, packed, force_simt=True)
-    _cmp(out, ref, torch.bfloat16, f"delta tc vs simt, threshold {threshold}")
+    # the device-length attention reads only what the host-length call reads
+    assert torch.equal(out.view(torch.int16), out2.view(torch.int16))
+    q_ref = O.apply_rope(q.cpu().contiguous(), cos.cpu(), sin.cpu())
+    k_ref = k_rot.cpu()
+    ref = O.hybrid_attention(q_ref, k_ref, v.cpu().contiguous(), m.k.cpu(), m.v.cpu(), m.timestamps.cpu(),
+                             m.counts.cpu().float(), D ** -0.5, 128, n_rep=Hq // Hkv, heads=[0, 7])
+    for h in (0, 7):
+        _cmp(out[:, h], ref[:, h], torch.bfloat16, f"delta fused vs oracle, threshold {threshold}, head {h}")
     _check_ws_clean()
 
 
