@@ -401,13 +401,41 @@ def traffic_per_launch():
         return None
 
 
+_SAMPLER = r"""
+import sys, time
+import pynvml
+pynvml.nvmlInit()
+hs = []
+for key in sys.argv[2:]:
+    try:
+        hs.append(pynvml.nvmlDeviceGetHandleByUUID(key))
+    except Exception:
+        hs.append(pynvml.nvmlDeviceGetHandleByIndex(int(key.split(":")[-1])))
+mx = [pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM) for h in hs]
+pw = [0.0] * len(hs)
+out = open(sys.argv[1], "w", buffering=1)
+n = 0
+while True:
+    for i, h in enumerate(hs):
+        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+        if n % 16 == 0:
+            pw[i] = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+        out.write(f"{time.time():.6f},{i},{sm},{mx[i]},{pw[i]:.1f},{rs}\n")
+    n += 1
+    time.sleep(0.0002)
+"""
+
+
 class ClockSampler:
     """SM clock, power and clock-event reasons sampled DURING the timed region.
 
-    NVML is polled every `period_s` (0.5 ms plus the query time) from a background thread, so
-    a timed region of a few tens of milliseconds still gets ten or more samples; ``nvidia-smi -lms 200`` is the
-    fallback when NVML cannot be loaded. GPUs are matched to NVML by UUID (the CUDA ordinals
-    of `gpus`), so CUDA_VISIBLE_DEVICES remapping does not confuse them."""
+    A separate process polls NVML (every ~0.3 ms; two queries per sample, the power every 16th)
+    and timestamps each sample, so the sampling neither waits on this process's interpreter
+    lock nor perturbs the launches; ``mark_start`` / ``mark_end`` bracket the timed region and
+    the summary keeps the samples inside it. ``nvidia-smi -lms 200`` is the fallback when
+    NVML cannot be loaded. GPUs are matched to NVML by UUID (CUDA ordinals `gpus`), so
+    CUDA_VISIBLE_DEVICES remapping does not confuse them."""
 
     REASONS = (("sw_power_cap", 0x4), ("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
                ("hw_thermal_slowdown", 0x40), ("hw_power_brake_slowdown", 0x80))
@@ -415,88 +443,86 @@ class ClockSampler:
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpus, period_s=0.0005):
+    def __init__(self, gpus):
         self.gpus = list(gpus)
-        self.period = period_s
-        self.samples = []  # (sm_mhz, max_mhz, power_w, reasons bitmask)
         self.proc = None
-        self.thread = None
-        self.nvml = None
+        self.kind = None
+        self.t0 = self.t1 = None
         self.path = os.path.join("/tmp", f"dab_clocks_{os.getpid()}.csv")
 
-    def _handles(self):
-        import pynvml
-        pynvml.nvmlInit()
-        hs = []
+    def _keys(self):
+        keys = []
         for i in self.gpus:
             try:
                 uid = str(torch.cuda.get_device_properties(i).uuid)
-                hs.append(pynvml.nvmlDeviceGetHandleByUUID(uid if uid.startswith("GPU-") else "GPU-" + uid))
+                keys.append(uid if uid.startswith("GPU-") else "GPU-" + uid)
             except Exception:
-                hs.append(pynvml.nvmlDeviceGetHandleByIndex(i))
-        return pynvml, hs
-
-    def _poll(self, pynvml, hs):
-        # two queries per sample (SM clock, event reasons); the maximum clock is read once and
-        # the power every eighth sample, so that a sample takes well under a millisecond
-        mxs = [float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)) for h in hs]
-        pws = [0.0] * len(hs)
-        n = 0
-        while not self.stop:
-            for i, h in enumerate(hs):
-                try:
-                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
-                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-                    if n % 8 == 0:
-                        pws[i] = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
-                    self.samples.append((float(sm), mxs[i], pws[i], int(rs)))
-                except Exception:
-                    pass
-            n += 1
-            time.sleep(self.period)
+                keys.append(f"index:{i}")
+        return keys
 
     def __enter__(self):
-        self.stop = False
+        if os.path.exists(self.path):
+            os.remove(self.path)
         try:
-            import threading
-            pynvml, hs = self._handles()
-            self.nvml = pynvml
-            self.thread = threading.Thread(target=self._poll, args=(pynvml, hs), daemon=True)
-            self.thread.start()
+            import pynvml  # noqa: F401  (the sampler process needs it)
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, self.path, *self._keys()],
+                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            self.kind = "nvml"
+            t_end = time.time() + 20.0
+            while time.time() < t_end and self.proc.poll() is None:  # wait for the first sample
+                if os.path.exists(self.path) and os.path.getsize(self.path) > 0:
+                    break
+                time.sleep(0.01)
+            if self.proc.poll() is not None:
+                raise RuntimeError("NVML sampler exited")
             return self
         except Exception:
-            self.nvml = None
+            self.proc = None
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+            self.kind = "nvidia-smi"
         except Exception:
             self.proc = None
         return self
 
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
     def __exit__(self, *a):
-        self.stop = True
-        if self.thread is not None:
-            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-            self.fh.close()
+            if self.kind == "nvidia-smi":
+                self.fh.close()
 
     def summary(self):
         sm, mx, reasons = [], [], set()
-        src = "nvml (~1 ms)"
-        if self.nvml is not None:
-            for s, m, _, rs in self.samples:
-                sm.append(s)
-                mx.append(m)
-                for name, bit in self.REASONS:
-                    if rs & bit:
-                        reasons.add(name)
-        elif self.proc is not None:
+        if self.kind == "nvml":
+            src = "nvml sampler process (~0.3 ms)"
+            try:
+                for line in open(self.path):
+                    f = line.strip().split(",")
+                    if len(f) != 6:
+                        continue
+                    t = float(f[0])
+                    if (self.t0 is not None and t < self.t0) or (self.t1 is not None and t > self.t1):
+                        continue
+                    sm.append(float(f[2]))
+                    mx.append(float(f[3]))
+                    for name, bit in self.REASONS:
+                        if int(f[5]) & bit:
+                            reasons.add(name)
+            except Exception:
+                pass
+        elif self.kind == "nvidia-smi":
             src = "nvidia-smi (200 ms)"
             try:
                 for line in open(self.path):
@@ -749,7 +775,9 @@ def run_ours(args, world, rank, local):
     with ClockSampler(range(world) if rank == 0 else [local]) as clk:
         torch.cuda.synchronize()
         barrier(world)
+        clk.mark_start()
         total_ms = _timed_steps(step, args.steps, stream, flush)
+        clk.mark_end()
         barrier(world)
     clocks = clk.summary()
     ms = max_over_ranks(total_ms / args.steps, world)

@@ -43,7 +43,8 @@ template <int D> struct TcCfg {
   static constexpr int OFF_V = OFF_K + NK * KVBYTES;
   static constexpr int OFF_AUXC = OFF_V + NV * KVBYTES;
   static constexpr int OFF_AUXT = OFF_AUXC + NV * TC_BN * 4;
-  static constexpr int OFF_BAR = OFF_AUXT + NV * TC_BN * 4;
+  static constexpr int OFF_ONES = OFF_AUXT + NV * TC_BN * 4;  // 128 unit weights (dense blocks, KEYED)
+  static constexpr int OFF_BAR = OFF_ONES + TC_BN * 4;
   static constexpr int NBAR = 2 + 2 * NK + 2 * NV + 2 * 6 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 64 + 1024;  // + alignment slack
@@ -191,6 +192,10 @@ __device__ __forceinline__ int unit_of(int iter, int cta, int G) {
   return (iter & 1) ? base + (G - 1 - cta) : base + cta;
 }
 
+// the packed length: the host value, or (device packed length) the maximum of the heads' anchors
+// that the schedule pre-pass, the previous launch on this stream, wrote to the workspace
+__device__ __forceinline__ int packed_len(const TcParams& p) { return p.anchors ? *p.len_dev : p.num_packed; }
+
 struct TileInfo {
   int packed;   // 1: packed block, 0: dense block
   int idx;      // block index (in 128-key blocks)
@@ -205,14 +210,8 @@ struct TileSeq {
   int pmax, dlo, dhi;
   int state, cur;  // state 0: packed, 1: dense, 2: done
   int mb_lo[2];
-  int vblk;  // packed blocks of the unit's kv-head holding rows (later ones are zero padding)
-
-  // `num_packed`: the packed length (the host value, or the device maximum of the heads' anchors)
-  __device__ __forceinline__ void init(const TcParams& p, const Unit& U, int num_packed) {
-    // with a device packed length, blocks past the head's own anchors are the reference's zero
-    // padding: K = V = 0 and count 0 add nothing to O or l, so they are not loaded or computed
-    // (the schedule pre-pass still counts their zero timestamps in the phase-1 stop rule)
-    vblk = p.anchors ? (p.anchors[U.b * p.Hts + U.hts[0]] + TC_BN - 1) / TC_BN : INT32_MAX;
+  __device__ __forceinline__ void init(const TcParams& p, const Unit& U) {
+    const int num_packed = packed_len(p);
     #pragma unroll
     for (int x = 0; x < 2; ++x) {
       n1[x] = 0; ds[x] = 0; de[x] = 0;
@@ -234,6 +233,10 @@ struct TileSeq {
     }
     const bool v0 = U.valid[0], v1 = U.valid[1];
     pmax = max(v0 ? n1[0] : 0, v1 ? n1[1] : 0);
+    // with a device packed length, blocks past the head's own anchors are the reference's zero
+    // padding: K = V = 0 and count 0 add nothing to O or l, so they are not loaded or computed
+    // (the schedule pre-pass still counts their zero timestamps in the phase-1 stop rule)
+    if (p.anchors) pmax = min(pmax, (p.anchors[U.b * p.Hts + U.hts[0]] + TC_BN - 1) / TC_BN);
     dlo = INT32_MAX; dhi = 0;
     #pragma unroll
     for (int x = 0; x < 2; ++x)
@@ -247,7 +250,6 @@ struct TileSeq {
     while (state == 0) {
       if (cur >= pmax) { state = 1; cur = dlo; break; }
       const int j = cur++;
-      if (j >= vblk) continue;  // zero padding of this head (device packed length)
       int use = 0;
       #pragma unroll
       for (int x = 0; x < 2; ++x) {
@@ -287,7 +289,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t par, const Abo
 }
 
 
-template <int D, bool BF16>
+// KEYED: the launch's packed blocks carry per-key counts that differ inside a block (the
+// threshold selection's run lengths), given as fp32. The streaming fast path then weights each
+// probability by its key's count (a multiply by the count staged with the V tile) instead of
+// one per-block exponent offset, so such blocks stay off the exact two-pass path; one copy of
+// the unrolled exponential loop either way (dense blocks read unit weights).
+template <int D, bool BF16, bool KEYED>
 __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_constant__ TcParams p) {
   using C = TcCfg<D>;
   constexpr int NK = C::NK, NV = C::NV;
@@ -311,6 +318,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
   float* auxc = reinterpret_cast<float*>(smem + C::OFF_AUXC);
   int32_t* auxt = reinterpret_cast<int32_t*>(smem + C::OFF_AUXT);
+  float* ones = reinterpret_cast<float*>(smem + C::OFF_ONES);
+  if (KEYED && threadIdx.x < TC_BN) ones[threadIdx.x] = 1.f;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -354,9 +363,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
   tc_fence_after();
   const uint32_t tmem = *tmem_base_smem;
   const Abort ab{abort_flag, p.err};
-  // the packed length: the host's, or the maximum of the heads' anchors that the schedule
-  // pre-pass (the previous launch on this stream) wrote to the workspace
-  const int num_packed = p.anchors ? *p.len_dev : p.num_packed;
   const int G = gridDim.x;
   const int n_iter = (p.num_units + G - 1) / G;
 
@@ -383,7 +389,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       }
       ++q_issued;
       TileSeq seq;
-      seq.init(p, U, num_packed);
+      seq.init(p, U);
       TileInfo t;
       while (seq.next(p, U, t)) {
         const int slot = kpos % NK;
@@ -416,7 +422,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       const Unit U = decode_unit(p, u);
       const int hk = U.hts[0];  // both tiles of a unit share the K/V head
       TileSeq seq;
-      seq.init(p, U, num_packed);
+      seq.init(p, U);
       TileInfo t;
       while (seq.next(p, U, t)) {
         if (!t.needs_v) continue;
@@ -430,7 +436,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           int32_t* tt = auxt + slot * TC_BN;
           // with a device packed length every row of a block the head holds is written (rows
           // past its anchors up to the block end are zeros), so the whole block is copied
-          const int nkeys = p.anchors ? TC_BN : min(TC_BN, num_packed - t.idx * TC_BN);
+          const int nkeys = p.anchors ? TC_BN : min(TC_BN, p.num_packed - t.idx * TC_BN);
           if (p.meta_bulk) {
             meta_bytes = static_cast<uint32_t>(nkeys) * 4u * (p.variant == TC_PURE ? 2u : 1u);
             if (lane == 0) {
@@ -446,7 +452,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
               const int key = t.idx * TC_BN + e;
               uint32_t cv = 0;
               int32_t tv2 = 0;
-              if (p.anchors || key < num_packed) {
+              if (p.anchors || key < p.num_packed) {
                 const int64_t off = U.b * p.cs_b + static_cast<int64_t>(hk) * p.cs_h + static_cast<int64_t>(key) * p.cs_n;
                 cv = static_cast<const uint32_t*>(p.counts)[off];
                 if (p.variant == TC_PURE)
@@ -554,7 +560,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         auto uses = [&](const TileInfo& t) { return mine && (t.use >> x & 1); };
 
         TileSeq seq;
-        seq.init(p, U, num_packed);
+        seq.init(p, U);
         TileInfo cur, nxt;
         bool have_cur = seq.next(p, U, cur);
         int cur_v = -1;
@@ -653,7 +659,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       float m_used = -INFINITY, l = 0.f;
       bool o_has = false;
       TileSeq seq;
-      seq.init(p, U, num_packed);
+      seq.init(p, U);
       const float* wrow = p.blkw + (static_cast<int64_t>(U.b) * p.Hts + U.hts[x]) * p.nblk;
       TileInfo t;
       bool ok = true;
@@ -672,7 +678,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         // a packed block with one common count is weighted through the exponent (no per-key work)
         const bool perkey = t.packed && !(lw == lw);  // NaN: counts differ inside the block
         const int32_t* tsv = auxt + vs * TC_BN;
-        if (perkey || (t.packed && p.variant == TC_PURE)) {
+        // per-key weights of the streaming path (KEYED): the block's counts, or unit weights
+        const float* wts = KEYED ? (t.packed ? auxc + vs * TC_BN : ones) : nullptr;
+        if (perkey || (t.packed && (KEYED || p.variant == TC_PURE))) {
           // per-key counts (and timestamps) arrive with the block's V tile
           if (!warp_wait(v_full + vs, vfp, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
         }
@@ -689,7 +697,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             for (int e = 0; e < 32; ++e) {
               const int j = w * 32 + e;
               const float cj = cint ? static_cast<float>(static_cast<int32_t>(cnt[j])) : __uint_as_float(cnt[j]);
-              const bool v = (n0 + j < num_packed) && cj > 0.f && tsv[j] <= row;
+              const bool v = (n0 + j < packed_len(p)) && cj > 0.f && tsv[j] <= row;
               bits |= (v ? 1u : 0u) << e;
             }
             if (w == 0) vm[0] = bits; else if (w == 1) vm[1] = bits; else if (w == 2) vm[2] = bits; else vm[3] = bits;
@@ -698,7 +706,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         int lim = TC_BN;
         if (p.variant != TC_PURE) {
           if (t.packed) {
-            lim = num_packed - n0;
+            lim = packed_len(p) - n0;
           } else {
             lim = p.seq_k - n0;
             if (p.variant != TC_DENSE || p.causal) lim = min(lim, row - n0 + 1);
@@ -762,6 +770,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             out[e / 2 + 1] = pack2(pe[2], pe[3], BF16);
           }
         };
+        // probabilities weighted by per-key counts (KEYED streaming path): 2^(s*scale + nb) * w
+        auto exp_keyed = [&](int c, const uint32_t* sc, float nb, uint32_t* out) {
+          const float2 s2 = make_float2(sl2, sl2), n2 = make_float2(nb, nb);
+          const float* w = wts + c * 32;
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            const float4 w4 = *reinterpret_cast<const float4*>(w + e);
+            const float2 a01 = ffma2(make_float2(__uint_as_float(sc[e]), __uint_as_float(sc[e + 1])), s2, n2);
+            const float2 a23 = ffma2(make_float2(__uint_as_float(sc[e + 2]), __uint_as_float(sc[e + 3])), s2, n2);
+            const float2 p01 = fmul2(make_float2(ex2(a01.x), ex2(a01.y)), make_float2(w4.x, w4.y));
+            const float2 p23 = fmul2(make_float2(ex2(a23.x), ex2(a23.y)), make_float2(w4.z, w4.w));
+            la = fadd2(la, p01);
+            lb = fadd2(lb, p23);
+            out[e / 2] = pack2(p01.x, p01.y, BF16);
+            out[e / 2 + 1] = pack2(p23.x, p23.y, BF16);
+          }
+        };
+        // one chunk of the streaming path
+        auto exp_stream = [&](int c, const uint32_t* sc, float nb, uint32_t* out) {
+          if constexpr (KEYED) exp_keyed(c, sc, nb, out);
+          else exp_plain(sc, nb, out);
+        };
         // fast path (warp-uniform; bf16, unmasked tile, one weight per block, every row already
         // holding a finite reference): S streams through two register buffers (the load of chunk
         // c+1 is in flight while chunk c is exponentiated against the running reference) and
@@ -770,14 +800,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         // more than 2^8 above its reference stops the stream: the repair path below takes over
         // from that chunk. P of keys 0..63 (chunks 0 and 1) is released to the MMA warp (p_lo)
         // only after chunks 2 and 3 have passed the same check, so released P is final.
-        const bool fast = BF16 && !perkey && !any_mask && !__any_sync(0xFFFFFFFFu, m_used == -INFINITY);
+        // (KEYED: per-key weights are fine too)
+        const bool fast = BF16 && (KEYED || !perkey) && !any_mask &&
+                          !__any_sync(0xFFFFFFFFu, m_used == -INFINITY);
         if (!warp_wait(s_full + x, s_par, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
         s_par ^= 1;
         tc_fence_after();
         int stop = 0;  // first chunk the fast path did not finish
         bool lo_sent = false;  // p_lo arrived (P of keys 0..63 final)
         if (fast) {
-          const float nb = lw - m_used;
+          const float nb = KEYED ? -m_used : lw - m_used;
           const float lim_raise = m_used + 8.f;
           uint32_t sa[32], sb[32];
           tmem_ld32_async(tS, sa);
@@ -792,7 +824,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
               return false;
             }
             uint32_t pc[16];
-            exp_plain(sc, nb, pc);
+            exp_stream(c, sc, nb, pc);
             tmem_st16(tS + c * 16, pc);
             tmem_ld32_wait(sn);
             tmem_ld32_async(tS + (c + 2) * 32, sc);
@@ -811,9 +843,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
               if (lane == 0) mbar_arrive(p_lo + x);
               lo_sent = true;
               uint32_t pc[16];
-              exp_plain(sa, nb, pc);
+              exp_stream(2, sa, nb, pc);
               tmem_st16(tS + 32, pc);
-              exp_plain(sb, nb, pc);
+              exp_stream(3, sb, nb, pc);
               tmem_st16(tS + 48, pc);
               stop = 4;
             }
@@ -948,10 +980,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
   if (warp == 2) tmem_dealloc(tmem, 512);
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool KEYED>
 static cudaError_t launch_tc_t(const TcParams& p, int num_sms, cudaStream_t st) {
   using C = TcCfg<D>;
-  auto kfn = attn_tc_kernel<D, BF16>;
+  auto kfn = attn_tc_kernel<D, BF16, KEYED>;
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int grid = p.num_units < num_sms ? p.num_units : num_sms;
@@ -961,8 +993,14 @@ static cudaError_t launch_tc_t(const TcParams& p, int num_sms, cudaStream_t st) 
 }
 
 cudaError_t launch_attn_tc(int head_dim, bool bf16, const TcParams& p, int num_sms, cudaStream_t st) {
-  if (head_dim == 128) return bf16 ? launch_tc_t<128, true>(p, num_sms, st) : launch_tc_t<128, false>(p, num_sms, st);
-  if (head_dim == 64) return bf16 ? launch_tc_t<64, true>(p, num_sms, st) : launch_tc_t<64, false>(p, num_sms, st);
+  // per-key weights on the streaming path only where it runs (bf16) and the counts are fp32
+  const bool keyed = p.keyed && bf16 && !p.counts_is_int;
+  if (head_dim == 128)
+    return keyed ? launch_tc_t<128, true, true>(p, num_sms, st)
+                 : bf16 ? launch_tc_t<128, true, false>(p, num_sms, st) : launch_tc_t<128, false, false>(p, num_sms, st);
+  if (head_dim == 64)
+    return keyed ? launch_tc_t<64, true, true>(p, num_sms, st)
+                 : bf16 ? launch_tc_t<64, true, false>(p, num_sms, st) : launch_tc_t<64, false, false>(p, num_sms, st);
   return cudaErrorInvalidValue;
 }
 

@@ -259,6 +259,8 @@ static int run_attention(int variant, int causal, const void* q, const void* kd,
       // counts (and timestamps) rows: contiguous along keys with 16-byte aligned block starts
       p.anchors = anchors;
       p.len_dev = reinterpret_cast<const int*>(ws + 4);  // header word 1: the device packed length
+      // device-packed (threshold) histories carry run-length counts that differ inside blocks
+      p.keyed = anchors != nullptr;
       p.meta_bulk = needs_packed && num_packed > 0 && counts && cs && cs[2] == 1 && num_packed % 4 == 0 &&
                     aligned16(counts) && (cs[0] * 4) % 16 == 0 && (cs[1] * 4) % 16 == 0 &&
                     (variant != 2 || (ts && tss && tss[2] == 1 && aligned16(ts) && (tss[0] * 4) % 16 == 0 &&

@@ -46,6 +46,7 @@ struct TcParams {
   // written by the schedule pre-pass); num_packed / nblk then give the buffers' capacity.
   const int32_t* anchors;
   const int* len_dev;
+  int keyed;               // packed blocks' counts differ inside blocks: weight per key on the fast path
 };
 
 // fused key compression (compress.cu): strides in elements

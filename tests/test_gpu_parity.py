@@ -426,8 +426,9 @@ def test_delta_mode_fused_matches_separate_kernels_and_oracle(threshold):
     """The fused key compression (RoPE + scan + packing in one launch, packed length on the
     device) against the separate RoPE / scan / pack kernels with the host length: rotated keys,
     keep mask, anchors and every packed row bit-identical, rows past each head's anchors zero up
-    to its block end; the device-length attention equals the host-length call on the same
-    packing, and both match the oracle within the bf16 tolerance (N = 4096, GQA 4:1)."""
+    to its block end; the device-length attention (per-key count weights on the streaming path)
+    agrees with the host-length call on the same packing, and both match the oracle within the
+    bf16 tolerance (N = 4096, GQA 4:1)."""
     from deltaattention_b200 import ops, synth
     B, Hq, Hkv, N, D = 1, 8, 2, 4096, 128
     q, k, v = synth.layer_inputs(B, Hq, Hkv, N, D, torch.bfloat16, seed=33, device="cuda")
@@ -453,8 +454,9 @@ def test_delta_mode_fused_matches_separate_kernels_and_oracle(threshold):
     assert torch.equal(m.timestamps, pk2.timestamps) and torch.equal(m.counts, pk2.counts)
     c = m.counts
     assert (c[:, :, :128].amax(-1) != c[:, :, :128].amin(-1)).any(), "counts should differ within a block"
-    # the device-length attention reads only what the host-length call reads
-    assert torch.equal(out.view(torch.int16), out2.view(torch.int16))
+    # the device-length attention weights each key by its count on the streaming path; the
+    # host-length call takes the exact two-pass path for those blocks: equal within rounding
+    _cmp(out, out2, torch.bfloat16, f"delta fused vs separate kernels, threshold {threshold}")
     q_ref = O.apply_rope(q.cpu().contiguous(), cos.cpu(), sin.cpu())
     k_ref = k_rot.cpu()
     ref = O.hybrid_attention(q_ref, k_ref, v.cpu().contiguous(), m.k.cpu(), m.v.cpu(), m.timestamps.cpu(),
