@@ -10,9 +10,11 @@ interpreter goldens in ``tests/golden``):
   strided fp32 accumulators combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)); fp16
   vectors are accumulated the same way in fp32 and rounded to fp16 once.
 * fp16 elementwise arithmetic is computed in fp32 and rounded to fp16 (numpy half
-  semantics). bf16 follows the same structure with bf16 rounding; the interpreter
-  cannot pin bf16 (it operates on raw uint16 bit patterns), so bf16 parity rests on
-  this shared structure.
+  semantics). bf16 follows the same structure with bf16 rounding (nearest even). The
+  stock interpreter operates on raw uint16 bit patterns for bf16, so the bf16 fixtures
+  come from the reference kernels run on the interpreter with IEEE bf16 arithmetic
+  (``tests/golden/bf16_interp.py``): selection, packing and decode state match them bit
+  for bit, attention outputs to within one bf16 ulp.
 * Attention dot products accumulate in fp32; the count-weighted probabilities are
   rounded to the value dtype before the PV product (deltaFlashAttention.py:98,137).
 """

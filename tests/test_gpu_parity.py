@@ -61,6 +61,8 @@ SEL = [
     ("keep_cosine_fp32", torch.float32, 1, 2, 1000, 64, 256, True, 1e4, 3),
     ("keep_cosine_bf16", torch.bfloat16, 1, 2, 1000, 128, 300, True, 5e5, 4),
     ("keep_cosine_fp16", torch.float16, 1, 2, 700, 96, 512, True, 5e5, 5),
+    ("keep_euclid_bf16", torch.bfloat16, 1, 2, 1000, 128, 300, False, 5e5, 6),
+    ("keep_euclid_bf16_d64", torch.bfloat16, 2, 2, 777, 64, 256, False, 1e4, 7),
 ]
 
 
@@ -217,6 +219,37 @@ def test_scatter_pack_layouts_match_oracle(dt, D, layout):
     assert torch.equal(ts.cpu(), ts_ref)
 
 
+def test_scatter_pack_bf16_matches_reference(golden):
+    """bf16 Euclidean selection, the reference's cumsum index map and the scatter pack on
+    the GPU against the reference kernels' bf16 fixture, bit for bit."""
+    import tritonModules as tm
+    g = golden("pack_bf16")
+    k = I.post_rope_keys(1, 2, 1000, 128, 5e5, torch.bfloat16, seed=6).cuda()
+    v = torch.from_numpy(I.normal((1, 2, 1000, 128), seed=106)).to(torch.bfloat16).cuda()
+    keep = torch.zeros((1, 2, 1000), dtype=torch.int32, device="cuda")
+    cc = torch.zeros((1, 2, 4), dtype=torch.int32, device="cuda")
+    thr = I.median_threshold(k.cpu(), False)
+    tm.chunked_eval_kernel[(2, 4)](k, keep, cc, thr, *k.stride(), *keep.stride(), *cc.stride(),
+                                   1000, 128, 300, num_heads=2, BLOCK_D=128, USE_COSINE=False)
+    np.testing.assert_array_equal(keep.cpu().numpy(), g["keep"])
+    im = (torch.cumsum(keep, -1) - 1).to(torch.int32)
+    M = int(keep.sum(-1).max())
+    kp = torch.zeros((1, 2, M, 128), dtype=torch.bfloat16, device="cuda")
+    vp = torch.zeros_like(kp)
+    ts = torch.zeros((1, 2, M), dtype=torch.int32, device="cuda")
+    tm.parallel_scatter_pack_kv_kernel[(2, -(-1000 // 64))](
+        k, v, kp, vp, ts, keep, im, *k.stride(), *v.stride(), *kp.stride(), *vp.stride(), *ts.stride(),
+        *keep.stride(), *im.stride(), 1000, 128, 2, BLOCK_S=64, BLOCK_D=128)
+    np.testing.assert_array_equal(im.cpu().numpy(), g["index_map"])
+    np.testing.assert_array_equal(kp.float().cpu().numpy(), g["k_packed"])
+    np.testing.assert_array_equal(vp.float().cpu().numpy(), g["v_packed"])
+    np.testing.assert_array_equal(ts.cpu().numpy(), g["timestamps"])
+    from deltaattention_b200 import ops
+    p = ops.pack_from_keep(k, v, keep, want_index_map=True)
+    np.testing.assert_array_equal(p.k.float().cpu().numpy(), g["k_packed"])
+    np.testing.assert_array_equal(p.counts.cpu().numpy(), g["counts"])
+
+
 def test_device_pack_from_keep_matches_reference(golden):
     from deltaattention_b200 import ops
     g = golden("pack_fp32")
@@ -300,6 +333,9 @@ ATTN = [
     ("attn_fp16_periodic", torch.float16, 2, 600, 128, "periodic", 24),
     ("attn_fp16_delta", torch.float16, 2, 520, 128, "delta", 25),
     ("attn_fp32_quirk", torch.float32, 2, 600, 64, "quirk", 26),
+    ("attn_bf16_periodic", torch.bfloat16, 2, 600, 128, "periodic", 27),
+    ("attn_bf16_delta", torch.bfloat16, 2, 520, 128, "delta", 28),
+    ("attn_bf16_d64_w0", torch.bfloat16, 2, 400, 64, "periodic", 29),
 ]
 VARIANT_KERNEL = {"hybrid": "hybrid_compressed_flash_kernel", "sanity": "hybrid_compressed_flash_kernel_sanity",
                   "pure_phase1": "pure_phase1_flash_kernel"}
@@ -340,7 +376,8 @@ def test_hybrid_variants_match_reference(golden, case, variant):
     _check_ws_clean()
 
 
-@pytest.mark.parametrize("case", [ATTN[0], ATTN[3]], ids=[ATTN[0][0], ATTN[3][0]])
+@pytest.mark.parametrize("case", [ATTN[0], ATTN[3], ATTN[6], ATTN[8]],
+                         ids=[ATTN[0][0], ATTN[3][0], ATTN[6][0], ATTN[8][0]])
 @pytest.mark.parametrize("causal", [True, False])
 def test_flash_matches_reference(golden, case, causal):
     import flashAttention as fa
@@ -597,7 +634,8 @@ def test_dense_r1_matches_flash_kernel():
 
 # ------------------------------------------------------------------ decoding
 @pytest.mark.parametrize("name,dt,use_cos", [("decode_fp32_euclid", torch.float32, False),
-                                             ("decode_fp16_cosine", torch.float16, True)])
+                                             ("decode_fp16_cosine", torch.float16, True),
+                                             ("decode_bf16_euclid", torch.bfloat16, False)])
 def test_decode_replay_matches_reference(golden, name, dt, use_cos):
     import deltaDecoding as dd
     g = golden(name)

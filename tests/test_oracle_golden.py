@@ -1,8 +1,9 @@
 """Pin the CPU oracle against golden vectors produced by the reference's own kernels.
 
 The fixtures in tests/golden were produced by ``gen_golden.py`` running the reference
-Triton kernels under TRITON_INTERPRET=1. Selection / packing / decode-cache state must
-match bit for bit; attention outputs within the tolerances below.
+Triton kernels under TRITON_INTERPRET=1 (the bf16 ones on the interpreter with IEEE bf16
+arithmetic, ``bf16_interp``). Selection / packing / decode-cache state must match bit for
+bit; attention outputs within the tolerances below.
 """
 import numpy as np
 import pytest
@@ -16,6 +17,24 @@ def test_interpreter_bf16_arithmetic_is_bitwise(golden):
     g = golden("bf16_interp_probe")
     # the interpreter subtracts raw bit patterns: not the bf16 difference
     assert not np.array_equal(g["interp"], g["true"])
+
+
+def test_patched_interpreter_bf16_arithmetic_is_ieee(golden):
+    g = golden("bf16_interp_ieee_probe")
+    # with bf16_interp installed the same kernel gives the correctly rounded difference,
+    # including a tie (1 - 2^-8 rounds to even), overflow to +inf and a signed zero
+    np.testing.assert_array_equal(g["interp"], g["true"])
+
+
+def test_bf16_rounding_helpers_agree_with_torch():
+    import bf16_interp as BI
+    x = np.random.default_rng(0).standard_normal(4096).astype(np.float32) * 10.0 ** np.arange(-20, 20, 10 / 1024)[:4096].astype(np.float32)
+    x = np.concatenate([x, np.float32([0.0, -0.0, np.inf, -np.inf, 3.4e38, 1.0 + 2.0 ** -8,
+                                      1.0 + 3 * 2.0 ** -8])])
+    ours = BI.f32_to_bf16_bits(x)
+    ref = torch.from_numpy(x).bfloat16().view(torch.int16).numpy().view(np.uint16)
+    np.testing.assert_array_equal(ours, ref)
+    np.testing.assert_array_equal(BI.bf16_bits_to_f32(ours), torch.from_numpy(ref.view(np.int16)).view(torch.bfloat16).float().numpy())
 
 
 @pytest.mark.parametrize("dt_name,dt", [("bf16", torch.bfloat16), ("fp32", torch.float32)])
@@ -35,6 +54,8 @@ SEL = [
     ("keep_cosine_fp32", torch.float32, 1, 2, 1000, 64, 256, True, 1e4, 3),
     ("keep_cosine_bf16", torch.bfloat16, 1, 2, 1000, 128, 300, True, 5e5, 4),
     ("keep_cosine_fp16", torch.float16, 1, 2, 700, 96, 512, True, 5e5, 5),
+    ("keep_euclid_bf16", torch.bfloat16, 1, 2, 1000, 128, 300, False, 5e5, 6),
+    ("keep_euclid_bf16_d64", torch.bfloat16, 2, 2, 777, 64, 256, False, 1e4, 7),
 ]
 
 
@@ -73,6 +94,21 @@ def test_pack_bit_exact(golden):
     np.testing.assert_array_equal(counts.numpy(), g["counts"])
 
 
+def test_pack_bf16_bit_exact(golden):
+    g = golden("pack_bf16")
+    k = I.post_rope_keys(1, 2, 1000, 128, 5e5, torch.bfloat16, seed=6)
+    v = torch.from_numpy(I.normal((1, 2, 1000, 128), seed=106)).to(torch.bfloat16)
+    assert float(v.double().sum()) == pytest.approx(float(g["v_sum"]), rel=1e-12)
+    keep, _ = O.delta_keep_mask(k, I.median_threshold(k, False), False, 300, 4)
+    np.testing.assert_array_equal(keep.numpy(), g["keep"])
+    im, kp, vp, ts, counts = O.pack_from_keep(k, v, keep)
+    np.testing.assert_array_equal(im.numpy(), g["index_map"])
+    np.testing.assert_array_equal(kp.float().numpy(), g["k_packed"])
+    np.testing.assert_array_equal(vp.float().numpy(), g["v_packed"])
+    np.testing.assert_array_equal(ts.numpy(), g["timestamps"])
+    np.testing.assert_array_equal(counts.numpy(), g["counts"])
+
+
 ATTN = [
     ("attn_fp32_periodic", torch.float32, 2, 600, 64, "periodic", 21),
     ("attn_fp32_delta", torch.float32, 2, 600, 64, "delta", 22),
@@ -80,8 +116,11 @@ ATTN = [
     ("attn_fp16_periodic", torch.float16, 2, 600, 128, "periodic", 24),
     ("attn_fp16_delta", torch.float16, 2, 520, 128, "delta", 25),
     ("attn_fp32_quirk", torch.float32, 2, 600, 64, "quirk", 26),
+    ("attn_bf16_periodic", torch.bfloat16, 2, 600, 128, "periodic", 27),
+    ("attn_bf16_delta", torch.bfloat16, 2, 520, 128, "delta", 28),
+    ("attn_bf16_d64_w0", torch.bfloat16, 2, 400, 64, "periodic", 29),
 ]
-TOL = {torch.float32: (2e-5, 2e-6), torch.float16: (4e-3, 2e-4)}
+TOL = {torch.float32: (2e-5, 2e-6), torch.float16: (4e-3, 2e-4), torch.bfloat16: (4e-3, 4e-5)}  # one bf16 ulp at |o| < 1
 
 
 def attn_case(golden, case):
@@ -106,7 +145,7 @@ def test_hybrid_attention_matches_reference(golden, case, variant):
     assert err.max() <= mx and err.mean() <= mean, (err.max(), err.mean())
 
 
-@pytest.mark.parametrize("case", ATTN[:1] + ATTN[3:4], ids=[ATTN[0][0], ATTN[3][0]])
+@pytest.mark.parametrize("case", ATTN[:1] + ATTN[3:4] + ATTN[6:7], ids=[ATTN[0][0], ATTN[3][0], ATTN[6][0]])
 @pytest.mark.parametrize("causal", [True, False])
 def test_flash_matches_reference(golden, case, causal):
     g, q, k, v, *_ = attn_case(golden, case)
@@ -132,7 +171,8 @@ def test_delta_padding_block_restarts_dense_window(golden):
 
 
 @pytest.mark.parametrize("name,dt,use_cos", [("decode_fp32_euclid", torch.float32, False),
-                                             ("decode_fp16_cosine", torch.float16, True)])
+                                             ("decode_fp16_cosine", torch.float16, True),
+                                             ("decode_bf16_euclid", torch.bfloat16, False)])
 def test_decode_replay_matches_reference(golden, name, dt, use_cos):
     g = golden(name)
     st = I.decode_setup(dt, seed=31)
