@@ -53,6 +53,7 @@ SIGNATURES = {
                                        P, SZ, P]),
     "dab_decode_advance": (I32, [P, I64, P]),
     "dab_rope": (I32, [P, PI64, P, PI64, P, P, PI64, I32, I64, I64, I64, I64, P]),
+    "dab_proj_rope": (I32, [P, I64, P, I64, P, P, I64, P, I64, I32, I64, I64, I64, I64, I64, I64, P, SZ, P]),
     "dab_periodic_meta": (I32, [P, P, P, I64, I64, I64, I64, P]),
     "dab_pack_from_keep_workspace_size": (SZ, [I64, I64, I64]),
     "dab_nm_select": (I32, [P, PI64, P, PI64, I32, I64, I64, I64, I64, I64, I64, I64, P]),
@@ -148,11 +149,11 @@ def workspace(device: torch.device, stream: int, nbytes: int, tag: str = "attn")
 
 
 def workspace_errors() -> list:
-    """Read and clear the error word of every attention and key-compression workspace
-    (synchronises)."""
+    """Read and clear the error word of every attention, key-compression and projection
+    workspace (synchronises)."""
     codes = []
     for (tag, dev, st), buf in list(_ws_cache.items()):
-        if tag not in ("attn", "compress"):
+        if tag not in ("attn", "compress", "proj"):
             continue
         code = ctypes.c_int(0)
         check(load().dab_workspace_error(ptr(buf), ctypes.byref(code), ctypes.c_void_p(st)), "workspace_error")

@@ -196,6 +196,22 @@ __device__ __forceinline__ int unit_of(int iter, int cta, int G) {
 // that the schedule pre-pass, the previous launch on this stream, wrote to the workspace
 __device__ __forceinline__ int packed_len(const TcParams& p) { return p.anchors ? *p.len_dev : p.num_packed; }
 
+// the two query tiles' (phase-1 blocks, dense start block) entries of the schedule, fetched one
+// unit ahead by the MMA and softmax warps so a unit boundary does not wait on the load
+struct UnitSched {
+  int2 s[2];
+};
+__device__ __forceinline__ UnitSched fetch_sched(const TcParams& p, const Unit& U) {
+  UnitSched us;
+  #pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    us.s[x] = make_int2(0, 0);
+    if (U.valid[x] && (p.variant == TC_HYBRID || p.variant == TC_SANITY))
+      us.s[x] = __ldg(&p.sched[(static_cast<int64_t>(U.b) * p.Hts + U.hts[x]) * p.nmb + U.mb[x]]);
+  }
+  return us;
+}
+
 struct TileInfo {
   int packed;   // 1: packed block, 0: dense block
   int idx;      // block index (in 128-key blocks)
@@ -210,7 +226,8 @@ struct TileSeq {
   int pmax, dlo, dhi;
   int state, cur;  // state 0: packed, 1: dense, 2: done
   int mb_lo[2];
-  __device__ __forceinline__ void init(const TcParams& p, const Unit& U) {
+  __device__ __forceinline__ void init(const TcParams& p, const Unit& U) { init(p, U, fetch_sched(p, U)); }
+  __device__ __forceinline__ void init(const TcParams& p, const Unit& U, const UnitSched& us) {
     const int num_packed = packed_len(p);
     #pragma unroll
     for (int x = 0; x < 2; ++x) {
@@ -220,7 +237,7 @@ struct TileSeq {
       const int m0 = U.mb[x] * TC_BM;
       const int hi = min(p.seq_k, m0 + TC_BM);
       if (p.variant == TC_HYBRID || p.variant == TC_SANITY) {
-        const int2 s = p.sched[(static_cast<int64_t>(U.b) * p.Hts + U.hts[x]) * p.nmb + U.mb[x]];
+        const int2 s = us.s[x];
         n1[x] = s.x;
         ds[x] = s.y;
         de[x] = (hi + TC_BN - 1) / TC_BN;
@@ -521,11 +538,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         if (lane == 0) mbar_arrive(turn + x);
         ++nbatch;
       };
+      UnitSched us_next{};
+      bool us_have = false;
       for (int it = 0; it < n_iter && !aborted; ++it) {
         const int u = unit_of(it, blockIdx.x, G);
         if (u >= p.num_units) continue;
         const Unit U = decode_unit(p, u);
-        const bool mine = U.valid[x];
+        const UnitSched us = us_have ? us_next : fetch_sched(p, U);
+        {
+          const int un = unit_of(it + 1, blockIdx.x, G);
+          us_have = it + 1 < n_iter && un < p.num_units;
+          if (us_have) us_next = fetch_sched(p, decode_unit(p, un));
+        }
+        const bool mine = x ? U.valid[1] : U.valid[0];
         if (!warp_wait(q_full, q_par, ab, ERR_TIMEOUT_MMA)) { aborted = true; break; }
         q_par ^= 1;
         tc_fence_after();
@@ -560,7 +585,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         auto uses = [&](const TileInfo& t) { return mine && (t.use >> x & 1); };
 
         TileSeq seq;
-        seq.init(p, U);
+        seq.init(p, U, us);
         TileInfo cur, nxt;
         bool have_cur = seq.next(p, U, cur);
         int cur_v = -1;
@@ -651,16 +676,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
     const float sl2 = p.scale_log2;
     int vpos = 0;  // V ring position (the packed block's counts travel with its V tile)
     uint32_t s_par = 0, o_par = 0;
+    UnitSched us_next{};
+    bool us_have = false;
     for (int it = 0; it < n_iter; ++it) {
       const int u = unit_of(it, blockIdx.x, G);
       if (u >= p.num_units) continue;
       const Unit U = decode_unit(p, u);
-      const int row = U.mb[x] * TC_BM + r;
+      const UnitSched us = us_have ? us_next : fetch_sched(p, U);
+      {
+        const int un = unit_of(it + 1, blockIdx.x, G);
+        us_have = it + 1 < n_iter && un < p.num_units;
+        if (us_have) us_next = fetch_sched(p, decode_unit(p, un));
+      }
+      const bool my_valid = x ? U.valid[1] : U.valid[0];
+      const int my_hts = x ? U.hts[1] : U.hts[0];
+      const int my_hq = x ? U.hq[1] : U.hq[0];
+      const int row = (x ? U.mb[1] : U.mb[0]) * TC_BM + r;
       float m_used = -INFINITY, l = 0.f;
       bool o_has = false;
       TileSeq seq;
-      seq.init(p, U);
-      const float* wrow = p.blkw + (static_cast<int64_t>(U.b) * p.Hts + U.hts[x]) * p.nblk;
+      seq.init(p, U, us);
+      const float* wrow = p.blkw + (static_cast<int64_t>(U.b) * p.Hts + my_hts) * p.nblk;
       TileInfo t;
       bool ok = true;
       while (seq.next(p, U, t)) {
@@ -670,7 +706,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         const int vs = vpos % NV;
         const uint32_t vfp = (vpos / NV) & 1;
         ++vpos;
-        if (!U.valid[x] || !(t.use >> x & 1)) continue;
+        if (!my_valid || !(t.use >> x & 1)) continue;
         // everything up to the first read of S depends only on the block: it is done before
         // waiting for S, off the softmax -> PV -> QK^T -> softmax chain
         const uint32_t* cnt = reinterpret_cast<const uint32_t*>(auxc + vs * TC_BN);
@@ -927,14 +963,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         o_has = true;
       }
       if (!ok) break;
-      if (!U.valid[x]) continue;  // invalid tiles take no part in the o_full / tile_free handshake
+      if (!my_valid) continue;  // invalid tiles take no part in the o_full / tile_free handshake
       // ---------------- epilogue: O / l -> out
       float lf = l;
       if (p.variant == TC_PURE && !(lf > 0.f)) lf = 1.f;
       const float inv = 1.f / lf;
       const bool row_ok = row < p.seq_q;
       using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-      T* orow = static_cast<T*>(p.out) + U.b * p.os_b + static_cast<int64_t>(U.hq[x]) * p.os_h +
+      T* orow = static_cast<T*>(p.out) + U.b * p.os_b + static_cast<int64_t>(my_hq) * p.os_h +
                 static_cast<int64_t>(row) * p.os_m;
       if (!warp_wait(o_full + x, o_par, ab, ERR_TIMEOUT_EPILOGUE)) break;
       o_par ^= 1;

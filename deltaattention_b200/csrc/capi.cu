@@ -47,6 +47,7 @@ cudaError_t launch_nm_select(int, const void*, const int64_t*, int32_t*, const i
                              int64_t, int, int, int64_t, cudaStream_t);
 cudaError_t launch_key_compress(int, int, bool, CompressParams, cudaStream_t);
 size_t key_compress_workspace(int64_t, int64_t, int64_t, int64_t);
+cudaError_t launch_proj_rope(const ProjParams&, int, cudaStream_t);
 }  // namespace dab
 
 using namespace dab;
@@ -87,9 +88,9 @@ int num_sms() {
   return n > 0 ? n : 148;
 }
 
-// 4-D map over (d, rows, heads, batch) with a 64 x 128 box and 128-byte swizzle.
+// 4-D map over (d, rows, heads, batch) with a 64 x box_rows box and 128-byte swizzle.
 bool encode_rows(CUtensorMap* m, const void* base, int dtype, int64_t d, int64_t rows, int64_t heads,
-                 int64_t batch, int64_t s_row, int64_t s_head, int64_t s_batch) {
+                 int64_t batch, int64_t s_row, int64_t s_head, int64_t s_batch, uint32_t box_rows = 128) {
   EncodeTiledFn enc = get_encode();
   if (!enc) return false;
   const int es = elem_size(dtype);
@@ -105,7 +106,7 @@ bool encode_rows(CUtensorMap* m, const void* base, int dtype, int64_t d, int64_t
                            static_cast<cuuint64_t>(sb * es)};
   for (auto s : strides)
     if (s % 16 != 0 || s == 0 || s >= (1ull << 40)) return false;
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t box[4] = {64, box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUtensorMapDataType dt = dtype == BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -547,6 +548,47 @@ int dab_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* y_
   return cuda_status(launch_rope(dtype, x, x_strides, y, y_strides, cos_t, sin_t, cs_strides, batch, heads, seq_len,
                                  head_dim, static_cast<cudaStream_t>(stream)),
                      "rope");
+}
+
+int dab_proj_rope(const void* x, int64_t x_row_stride, const void* w, int64_t w_row_stride, const void* cos_t,
+                  const void* sin_t, int64_t cs_row_stride, void* out, int64_t out_row_stride, int dtype,
+                  int64_t rows, int64_t in_features, int64_t out_features, int64_t head_dim, int64_t rope_lo,
+                  int64_t rope_hi, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x || !w || !out || !workspace) return fail(1, "dab_proj_rope: null pointer");
+  if (dtype != BF16) return fail(1, "dab_proj_rope: bf16 only");
+  if (head_dim != 128) return fail(1, "dab_proj_rope: head_dim must be 128");
+  if (rows < 1 || in_features < 1 || out_features < 1) return fail(1, "dab_proj_rope: empty problem");
+  if (out_features % 128 != 0) return fail(1, "dab_proj_rope: out_features must be a multiple of 128");
+  if (rope_lo < 0 || rope_hi < rope_lo || rope_hi > out_features || rope_lo % 128 || rope_hi % 128)
+    return fail(1, "dab_proj_rope: RoPE column range must be head-aligned inside [0, out_features]");
+  if (rope_hi > rope_lo && (!cos_t || !sin_t)) return fail(1, "dab_proj_rope: RoPE tables missing");
+  if (workspace_bytes < WS_HEADER) return fail(1, "dab_proj_rope: workspace smaller than 256 bytes");
+  if (rows > INT32_MAX / 2 || in_features > INT32_MAX / 2 || out_features > INT32_MAX / 2)
+    return fail(1, "dab_proj_rope: size too large");
+  // TMA: 16-byte aligned bases and row strides; the epilogue: 16-byte output and table rows
+  if (!aligned16(x) || !aligned16(w) || !aligned16(out) || x_row_stride % 8 || w_row_stride % 8 ||
+      out_row_stride % 8 || (rope_hi > rope_lo && (!aligned16(cos_t) || !aligned16(sin_t) || cs_row_stride % 8)))
+    return fail(1, "dab_proj_rope: pointers and row strides must be 16-byte aligned");
+  ProjParams p{};
+  if (!encode_rows(&p.tm_x, x, BF16, in_features, rows, 1, 1, x_row_stride, 0, 0, 128) ||
+      !encode_rows(&p.tm_w, w, BF16, in_features, out_features, 1, 1, w_row_stride, 0, 0, 256))
+    return fail(1, "dab_proj_rope: tensor map encoding failed (layout not TMA-compatible)");
+  p.cos = cos_t;
+  p.sin = sin_t;
+  p.cs_row = cs_row_stride;
+  p.out = out;
+  p.os_row = out_row_stride;
+  p.err = static_cast<int*>(workspace);
+  p.rows = static_cast<int>(rows);
+  p.K = static_cast<int>(in_features);
+  p.Ho = static_cast<int>(out_features);
+  p.rope_lo = static_cast<int>(rope_lo);
+  p.rope_hi = static_cast<int>(rope_hi);
+  p.n_tiles_n = static_cast<int>((out_features + 255) / 256);
+  const int64_t tiles = ((rows + 127) / 128) * p.n_tiles_n;
+  if (tiles > INT32_MAX) return fail(1, "dab_proj_rope: too many tiles");
+  p.num_tiles = static_cast<int>(tiles);
+  return cuda_status(launch_proj_rope(p, num_sms(), static_cast<cudaStream_t>(stream)), "proj_rope");
 }
 
 int dab_periodic_meta(int32_t* packed_ts, int32_t* packed_counts, float* packed_counts_f32, int64_t batch_heads,

@@ -65,4 +65,17 @@ struct CompressParams {
   unsigned total_chunks, total_warps;
 };
 
+// projection GEMM with a RoPE epilogue (proj.cu): out = RoPE(round(X W^T)) on [rope_lo, rope_hi)
+struct ProjParams {
+  CUtensorMap tm_x;                     // X [rows, K] bf16, box 64 x 128, 128-byte swizzle
+  CUtensorMap tm_w;                     // W [Ho, K] bf16 (nn.Linear weight), box 64 x 256
+  const void* cos; const void* sin;     // RoPE tables [rows, head_dim] bf16
+  int64_t cs_row;                       // table row stride (elements)
+  void* out; int64_t os_row;            // out [rows, Ho] bf16, row stride (elements)
+  int* err;                             // device error word (bounded waits)
+  int rows, K, Ho;
+  int rope_lo, rope_hi;                 // output columns that get RoPE (multiples of 128)
+  int n_tiles_n, num_tiles;             // 256-column tiles per row block; total tiles
+};
+
 }  // namespace dab

@@ -47,6 +47,45 @@ def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: Optional[to
     return out
 
 
+def proj_rope(x: torch.Tensor, w: torch.Tensor, cos: Optional[torch.Tensor] = None,
+              sin: Optional[torch.Tensor] = None, rope_cols: Optional[tuple] = None,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q / k / v projection with RoPE as the GEMM epilogue (modeling_llama.py:550-555).
+
+    ``x`` [rows, in] (the hidden states, rows = B*N), ``w`` [out, in] (nn.Linear weight, no
+    bias), bf16. Returns [rows, out] = x @ w.T rounded to bf16, with RoPE (eager bf16
+    rounding, table row r of ``cos`` / ``sin`` [rows, 128]) applied to the output columns in
+    ``rope_cols`` = (lo, hi), by default all of them when tables are given. Viewed as
+    [B, N, H, 128] and transposed, this is the reference's rotated ``key_states`` (or
+    ``query_states``) in the projection layout the attention kernels read through strides.
+    """
+    L.require_cuda(x, w)
+    rows, kin = x.shape
+    nout = w.shape[0]
+    if w.shape[1] != kin:
+        raise ValueError(f"proj_rope: x has {kin} features, w expects {w.shape[1]}")
+    if rope_cols is None:
+        rope_cols = (0, nout) if cos is not None else (0, 0)
+    lo, hi = rope_cols
+    if hi > lo:
+        if cos is None or sin is None:
+            raise ValueError("proj_rope: RoPE columns given without cos / sin tables")
+        L.require_cuda(cos, sin)
+        cos = cos.reshape(-1, cos.shape[-1])
+        sin = sin.reshape(-1, sin.shape[-1])
+        if cos.shape[0] != rows or cos.stride() != sin.stride() or cos.stride(1) != 1:
+            raise ValueError("proj_rope: cos / sin must be [rows, 128] with unit column stride and equal strides")
+    if out is None:
+        out = torch.empty((rows, nout), dtype=x.dtype, device=x.device)
+    st = L.stream_of(x)
+    ws = L.workspace(x.device, st.value, 256, tag="proj")
+    L.check(L.load().dab_proj_rope(L.ptr(x), x.stride(0), L.ptr(w), w.stride(0),
+                                   L.ptr(cos) if hi > lo else None, L.ptr(sin) if hi > lo else None,
+                                   cos.stride(0) if hi > lo else 0, L.ptr(out), out.stride(0), L.dtype_code(x),
+                                   rows, kin, nout, 128, lo, hi, L.ptr(ws), ws.numel(), st), "proj_rope")
+    return out
+
+
 @dataclass
 class Packed:
     """Packed history of one layer: K/V rows, anchor timestamps and run-length counts.

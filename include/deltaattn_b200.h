@@ -218,6 +218,19 @@ int dab_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* y_
              const void* sin_t, const int64_t* cs_strides, int dtype, int64_t batch, int64_t heads,
              int64_t seq_len, int64_t head_dim, void* stream);
 
+/* q/k/v projection with RoPE as the GEMM epilogue (modeling_llama.py:550-555:
+ * `k_proj(hidden_states).view(B, N, H, d).transpose(1, 2)` then apply_rotary_pos_emb at
+ * :180-204). out[r, c] = x[r, :] . w[c, :] (nn.Linear, no bias), rounded to bf16; columns in
+ * [rope_lo, rope_hi) (head-aligned) then get RoPE with eager bf16 rounding, using table row r
+ * of cos / sin ([rows, 128]). x [rows, in_features], w [out_features, in_features], out
+ * [rows, out_features]: unit column stride, 16-byte aligned row strides (elements). bf16,
+ * head_dim 128, out_features a multiple of 128. `workspace` holds the 256-byte error header
+ * (dab_workspace_error). */
+int dab_proj_rope(const void* x, int64_t x_row_stride, const void* w, int64_t w_row_stride, const void* cos_t,
+                  const void* sin_t, int64_t cs_row_stride, void* out, int64_t out_row_stride, int dtype,
+                  int64_t rows, int64_t in_features, int64_t out_features, int64_t head_dim, int64_t rope_lo,
+                  int64_t rope_hi, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Packed timestamps / counts of periodic packing (modeling_llama.py:626-632 followed by
  * :655-685): anchor j at j*period covering min(period, seq_len - j*period) tokens.
  * Buffers are [batch_heads][num_packed] contiguous; num_packed must be ceil(seq_len/period).

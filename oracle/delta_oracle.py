@@ -31,7 +31,7 @@ __all__ = [
     "delta_keep_mask", "periodic_keep_mask", "random_keep_mask", "nm_keep_mask",
     "pack_from_keep", "hybrid_schedule", "tile_count", "hybrid_attention",
     "flash_attention", "decode_update", "decode_attention", "sq_dist_f32",
-    "eager_attention",
+    "eager_attention", "proj_rope",
 ]
 
 # ---------------------------------------------------------------------------
@@ -110,6 +110,26 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
 # ---------------------------------------------------------------------------
 # anchor selection
 # ---------------------------------------------------------------------------
+
+def proj_rope(x: torch.Tensor, w: torch.Tensor, cos: Optional[torch.Tensor], sin: Optional[torch.Tensor],
+              rope_lo: int, rope_hi: int, head_dim: int = 128) -> torch.Tensor:
+    """``k_proj(hidden_states).view(B, N, H, d)`` then ``apply_rotary_pos_emb``
+    (modeling_llama.py:550-555, :180-204), kept in the projection layout [rows, out].
+
+    The Linear's product is accumulated in fp64 here and rounded to the input dtype once (a
+    GEMM's fp32 accumulation order is implementation-defined, so parity with it is to
+    within rounding); RoPE then follows eager rounding on columns [rope_lo, rope_hi).
+    """
+    y = (x.double() @ w.double().t()).to(x.dtype)
+    if rope_hi <= rope_lo:
+        return y
+    rows = y.shape[0]
+    part = y[:, rope_lo:rope_hi].reshape(rows, -1, head_dim).transpose(0, 1)   # [H, rows, d]
+    rot = apply_rope(part.unsqueeze(0), cos.reshape(1, rows, head_dim), sin.reshape(1, rows, head_dim))[0]
+    y = y.clone()
+    y[:, rope_lo:rope_hi] = rot.transpose(0, 1).reshape(rows, -1)
+    return y
+
 
 def delta_keep_mask(k: torch.Tensor, threshold: float, use_cosine: bool,
                     chunk_size: int, num_chunks: int):
