@@ -392,6 +392,52 @@ def sweep(dev, seed, reps=3):
     return out
 
 
+def proj_rope_bench(dev, seed, reps=5):
+    """The k_proj / fused QKV projection with RoPE as the GEMM epilogue (modeling_llama.py:
+    550-555) at cfg2 sizes (32768 tokens, hidden 4096), against the unfused path it replaces:
+    torch's bf16 GEMM (cuBLAS) followed by the library's RoPE kernel. Inputs are larger than
+    L2; CUDA events, median of `reps` launches after a warm-up launch."""
+    from deltaattention_b200 import ops, synth
+    burst, _, _ = peaks()
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    rows, kin = CFG["N"], 4096
+    x = torch.randn(rows, kin, device=dev, dtype=torch.bfloat16, generator=g)
+    cos, sin = synth.rope_tables(rows, CFG["D"], CFG["theta"], torch.bfloat16, device=dev)
+    cos, sin = cos.reshape(rows, CFG["D"]), sin.reshape(rows, CFG["D"])
+
+    def timed(fn):
+        fn()
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+    out = {}
+    for name, nout, rope_hi in (("k_proj", 1024, 1024), ("qkv_proj", 6144, 5120)):
+        w = torch.randn(nout, kin, device=dev, dtype=torch.bfloat16, generator=g) * kin ** -0.5
+        fused = timed(lambda: ops.proj_rope(x, w, cos, sin, rope_cols=(0, rope_hi)))
+        gemm = timed(lambda: x @ w.t())
+
+        def unfused():
+            y = x @ w.t()
+            h = rope_hi // CFG["D"]
+            yr = y[:, :rope_hi].view(1, rows, h, CFG["D"]).transpose(1, 2)
+            ops.rope(yr, cos[None], sin[None], out=yr)
+            return y
+        unf = timed(unfused)
+        flops = 2 * rows * kin * nout
+        out[name] = {"out_features": nout, "rope_columns": rope_hi, "fused_ms": fused, "cublas_gemm_ms": gemm,
+                     "cublas_gemm_plus_rope_ms": unf, "fused_tflops": flops / fused / 1e9,
+                     "frac_of_burst": flops / fused / 1e9 / burst, "speedup_vs_unfused": unf / fused}
+        del w
+    return out
+
+
 def traffic_per_launch():
     """DRAM bytes per attention launch from the committed ncu summary, if present."""
     try:
@@ -930,6 +976,7 @@ def run_ours(args, world, rank, local):
         hk_ = hbm_kernels(dev, 2000 + rank)
         line["hbm_kernels"] = {"peak_gbs": hbm_peak()[0], "peak_kind": hbm_peak()[1], **hk_}
     if world == 1 and not args.no_sweep:
+        line["proj_rope"] = proj_rope_bench(dev, 6000 + rank)
         line["decode_step"] = decode_step(dev, 4000 + rank)
         line["serving_cfg5"] = serving(dev, 5000 + rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
