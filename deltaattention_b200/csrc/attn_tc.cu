@@ -828,29 +828,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           if constexpr (KEYED) exp_keyed(c, sc, nb, out);
           else exp_plain(sc, nb, out);
         };
-        // fast path (warp-uniform; bf16, unmasked tile, one weight per block, every row already
-        // holding a finite reference): S streams through two register buffers (the load of chunk
-        // c+1 is in flight while chunk c is exponentiated against the running reference) and
+        // fast path (warp-uniform; bf16, unmasked tile, one weight per block): S streams through
+        // two register buffers (the load of chunk c+1 is in flight while chunk c is
+        // exponentiated against the running reference) and
         // each P chunk is stored as soon as it is computed. P chunk c covers columns
         // 16c..16c+15, below every S chunk not yet read. A chunk that raises some row's maximum
         // more than 2^8 above its reference stops the stream: the repair path below takes over
         // from that chunk. P of keys 0..63 (chunks 0 and 1) is released to the MMA warp (p_lo)
         // only after chunks 2 and 3 have passed the same check, so released P is final.
         // (KEYED: per-key weights are fine too)
-        const bool fast = BF16 && (KEYED || !perkey) && !any_mask &&
-                          !__any_sync(0xFFFFFFFFu, m_used == -INFINITY);
+        const bool fast = BF16 && (KEYED || !perkey) && !any_mask;
         if (!warp_wait(s_full + x, s_par, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
         s_par ^= 1;
         tc_fence_after();
         int stop = 0;  // first chunk the fast path did not finish
         bool lo_sent = false;  // p_lo arrived (P of keys 0..63 final)
         if (fast) {
-          const float nb = KEYED ? -m_used : lw - m_used;
-          const float lim_raise = m_used + 8.f;
           uint32_t sa[32], sb[32];
           tmem_ld32_async(tS, sa);
           tmem_ld32_wait(sa);
           tmem_ld32_async(tS + 32, sb);
+          // a row without a reference yet (the unit's first block) takes chunk 0's maximum: any
+          // finite reference is exact once O / l divides it out, and a later chunk more than 2^8
+          // above it takes the repair path like any other jump
+          if (m_used == -INFINITY) {
+            const float m0 = chunk_max(sa) * sl2;
+            m_used = (m0 == -INFINITY) ? 0.f : m0;
+          }
+          const float nb = KEYED ? -m_used : lw - m_used;
+          const float lim_raise = m_used + 8.f;
           // chunk c (0 or 1); false when it stops the stream (no load is left in flight then). On
           // success chunk c+1 has landed in sn and chunk c+2 is loading into sc.
           auto step = [&](int c, uint32_t(&sc)[32], uint32_t(&sn)[32]) -> bool {
