@@ -149,11 +149,11 @@ def workspace(device: torch.device, stream: int, nbytes: int, tag: str = "attn")
 
 
 def workspace_errors() -> list:
-    """Read and clear the error word of every attention, key-compression and projection
-    workspace (synchronises)."""
+    """Read and clear the error word of every attention, key-compression, projection and
+    packing workspace (synchronises)."""
     codes = []
     for (tag, dev, st), buf in list(_ws_cache.items()):
-        if tag not in ("attn", "compress", "proj"):
+        if tag not in ("attn", "compress", "proj", "pack"):
             continue
         code = ctypes.c_int(0)
         check(load().dab_workspace_error(ptr(buf), ctypes.byref(code), ctypes.c_void_p(st)), "workspace_error")

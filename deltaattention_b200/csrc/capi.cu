@@ -26,8 +26,9 @@ cudaError_t launch_rope(int, const void*, const int64_t*, void*, const int64_t*,
 cudaError_t launch_periodic_meta(int32_t*, int32_t*, float*, int64_t, int64_t, int64_t, int64_t, cudaStream_t);
 cudaError_t launch_pack_from_keep(int, const int32_t*, const int64_t*, const void*, const int64_t*, const void*,
                                   const int64_t*, void*, void*, const int64_t*, int32_t*, int32_t*, const int64_t*,
-                                  int32_t*, int64_t, int64_t, int64_t, int64_t, int64_t, int32_t*, int32_t*,
+                                  int32_t*, int64_t, int64_t, int64_t, int64_t, int64_t, uint8_t*, int32_t*,
                                   int32_t*, cudaStream_t);
+size_t pack_from_keep_workspace(int64_t, int64_t);
 cudaError_t launch_attn_simt(int, const SimtParams&, cudaStream_t);
 cudaError_t launch_attn_tc(int, bool, const TcParams&, int, cudaStream_t);
 cudaError_t launch_schedule(const int32_t*, const int64_t*, const void*, const int64_t*, int, int, int, int, int,
@@ -603,8 +604,7 @@ int dab_periodic_meta(int32_t* packed_ts, int32_t* packed_counts, float* packed_
 }
 
 size_t dab_pack_from_keep_workspace_size(int64_t batch, int64_t heads, int64_t seq_len) {
-  const int64_t ntile = (seq_len + 1023) / 1024;
-  return static_cast<size_t>(4 * batch * heads * (ntile > 0 ? ntile : 1)) * sizeof(int32_t);
+  return pack_from_keep_workspace(batch * heads, seq_len);
 }
 
 int dab_pack_from_keep(const int32_t* keep_mask, const int64_t* km_strides, const void* k, const int64_t* k_strides,
@@ -620,10 +620,12 @@ int dab_pack_from_keep(const int32_t* keep_mask, const int64_t* km_strides, cons
     return fail(1, "dab_pack_from_keep: workspace too small");
   if (k_strides[3] != 1 || v_strides[3] != 1 || pack_strides[3] != 1 || meta_strides[2] != 1)
     return fail(1, "dab_pack_from_keep: innermost strides must be 1");
+  if (seq_len >= (int64_t{1} << 30) || capacity >= (int64_t{1} << 31))
+    return fail(1, "dab_pack_from_keep: seq_len must be below 2^30 and capacity below 2^31");
   return cuda_status(launch_pack_from_keep(dtype, keep_mask, km_strides, k, k_strides, v, v_strides, k_packed,
                                            v_packed, pack_strides, packed_ts, packed_counts, meta_strides, index_map,
                                            batch, heads, seq_len, head_dim, capacity,
-                                           static_cast<int32_t*>(workspace), anchors_per_head, max_anchors,
+                                           static_cast<uint8_t*>(workspace), anchors_per_head, max_anchors,
                                            static_cast<cudaStream_t>(stream)),
                      "pack_from_keep");
 }

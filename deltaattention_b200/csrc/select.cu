@@ -616,218 +616,321 @@ cudaError_t launch_periodic_meta(int32_t* ts, int32_t* counts, float* counts_f, 
 }
 
 // ---------------------------------------------------------------------------------------
-// device-side packing from a keep mask (native path: no host sync, no repeat_kv)
-//   pass 1: per (head, 1024-token tile) kept counts
-//   pass 2: per head exclusive scan over tiles, anchors per head, first kept per tile
-//   pass 3: per tile local scan -> index map, scatter K/V/ts, run-length counts
+// device-side packing from a keep mask (native path: no host sync, no repeat_kv), one launch
+// (modeling_llama.py:655-685: index_map = cumsum(keep) - 1, the scatter of kept K / V rows and
+// timestamps, run-length counts, zero padding up to the packed length).
+// One CTA per 1024-token tile of one (batch, head). A CTA takes a ticket (head-major order),
+// counts its tile's kept tokens, publishes that count, and finds its packed offset by a
+// decoupled look-back over the head's earlier tiles: every tile publishes its own count before
+// it waits on anything, and it waits only on tiles with smaller tickets (already running), so
+// every wait ends. The run length of a tile's last anchor reaches the first kept token after
+// the tile, found by scanning the keep mask forward 32 tokens at a time. The head's last tile
+// writes the head's anchor count and zeroes the padding rows up to the capacity; the launch's
+// last CTA writes the maximum anchor count, resets the ticket / done counters and advances the
+// epoch that tags the status words, so the workspace is cleared once and then reused.
 // ---------------------------------------------------------------------------------------
-constexpr int PACK_TILE = 1024;
+constexpr int PACK_TILE = 1024;    // tokens per tile (one CTA)
+constexpr int PACK_THREADS = 256;  // threads per CTA: four consecutive tokens each
+constexpr int PACK_HDR = 64;  // workspace header bytes; then one uint64 status word per tile
+constexpr int PACK_PADDERS = 128;  // CTAs after the tiles that zero the padding rows
 
-__global__ void __launch_bounds__(PACK_TILE) keep_tile_count_kernel(const int32_t* __restrict__ keep,
-                                                                    int64_t kb, int64_t kh, int64_t ks,
-                                                                    int64_t H, int64_t N, int32_t* tile_cnt,
-                                                                    int32_t* tile_first, int64_t ntile) {
-  const int64_t bh = blockIdx.y, t = blockIdx.x;
-  const int64_t b = static_cast<int>(bh) / static_cast<int>(H), h = bh - b * H;  // bh: a grid index
-  const int64_t s = t * PACK_TILE + threadIdx.x;
-  const int kv = (s < N) ? (keep[b * kb + h * kh + s * ks] == 1) : 0;
-  const int c = __syncthreads_count(kv);
-  __shared__ int first;
-  if (threadIdx.x == 0) first = INT32_MAX;
-  __syncthreads();
-  if (kv) atomicMin(&first, static_cast<int>(s));
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    tile_cnt[bh * ntile + t] = c;
-    tile_first[bh * ntile + t] = first;
-  }
+struct PackHdr {
+  int err;  // first word: the error word dab_workspace_error reads
+  unsigned ticket, done, epoch;
+};
+enum : int { ERR_PACK_LOOKBACK = 0x201 };
+
+__device__ __forceinline__ uint64_t pk_ld(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
-
-// one block per head: exclusive scan of tile counts; next_first[t] = first kept position
-// strictly after tile t (or N); anchors[bh] = total kept; atomicMax into *max_anchors
-__global__ void __launch_bounds__(1024) keep_tile_scan_kernel(int32_t* tile_cnt, int32_t* tile_first,
-                                                              int32_t* tile_off, int32_t* next_first,
-                                                              int32_t* anchors, int32_t* max_anchors,
-                                                              int64_t ntile, int64_t N) {
-  const int64_t bh = blockIdx.x;
-  if (threadIdx.x == 0) {
-    int32_t run = 0;
-    for (int64_t t = 0; t < ntile; ++t) {
-      tile_off[bh * ntile + t] = run;
-      run += tile_cnt[bh * ntile + t];
-    }
-    int32_t nf = static_cast<int32_t>(N);
-    for (int64_t t = ntile - 1; t >= 0; --t) {
-      next_first[bh * ntile + t] = nf;
-      const int32_t f = tile_first[bh * ntile + t];
-      if (f != INT32_MAX) nf = f;
-    }
-    anchors[bh] = run;
-    atomicMax(max_anchors, run);
-  }
+__device__ __forceinline__ void pk_st(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// status word: epoch (32 bits) | flag (2 bits: 1 = the tile's count, 2 = inclusive prefix) | value
+__device__ __forceinline__ uint64_t pk_word(unsigned ep, unsigned flag, unsigned val) {
+  return (static_cast<uint64_t>(ep) << 32) | (static_cast<uint64_t>(flag) << 30) | val;
 }
 
 template <typename T>
-__global__ void __launch_bounds__(PACK_TILE) keep_pack_kernel(
+__global__ void __launch_bounds__(PACK_THREADS) keep_pack_kernel(
     const int32_t* __restrict__ keep, int64_t kb, int64_t kh, int64_t ks, const T* __restrict__ k, int64_t xb,
     int64_t xh, int64_t xs, const T* __restrict__ v, int64_t vb, int64_t vh, int64_t vs, T* __restrict__ kp,
     T* __restrict__ vp, int64_t pb, int64_t ph, int64_t ps, int32_t* __restrict__ ts, int32_t* __restrict__ counts,
-    int64_t mb, int64_t mh, int32_t* __restrict__ index_map, const int32_t* tile_off, const int32_t* next_first,
-    int64_t H, int64_t N, int64_t D, int64_t ntile, int64_t capacity, int vec16) {
-  __shared__ int32_t warp_off[PACK_TILE / 32];
+    int64_t mb, int64_t mh, int32_t* __restrict__ index_map, uint8_t* __restrict__ ws, int32_t* __restrict__ anchors,
+    int32_t* __restrict__ max_anchors, int64_t H, int64_t N, int64_t D, int64_t ntile, int64_t capacity, int vec16) {
+  constexpr int NW = PACK_THREADS / 32;
+  constexpr int TPT = PACK_TILE / PACK_THREADS;  // consecutive tokens per thread
+  __shared__ int32_t warp_tot[NW];
   __shared__ int32_t pos_of[PACK_TILE];
-  __shared__ int32_t total;
-  const int64_t bh = blockIdx.y, t = blockIdx.x;
-  const int64_t b = static_cast<int>(bh) / static_cast<int>(H), h = bh - b * H;  // bh: a grid index
-  const int64_t s = t * PACK_TILE + threadIdx.x;
-  const int kv = (s < N) ? (keep[b * kb + h * kh + s * ks] == 1) : 0;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const unsigned bal = __ballot_sync(0xFFFFFFFFu, kv);
-  const int in_warp = __popc(bal & ((1u << lane) - 1));
-  if (lane == 0) warp_off[warp] = __popc(bal);
+  __shared__ int32_t total, s_base, s_next;
+  __shared__ unsigned s_ticket, s_ep;
+  __shared__ int s_last;
+  PackHdr* hdr = reinterpret_cast<PackHdr*>(ws);
+  uint64_t* status = reinterpret_cast<uint64_t*>(ws + PACK_HDR);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    s_ticket = atomicAdd(&hdr->ticket, 1u);
+    s_ep = *reinterpret_cast<volatile unsigned*>(&hdr->epoch) + 1u;
+  }
   __syncthreads();
-  if (warp == 0) {
-    const int v0 = warp_off[lane];
-    int incl = v0;
+  const unsigned L = s_ticket, ep = s_ep;
+  const int64_t BHt = (static_cast<int64_t>(gridDim.x) - PACK_PADDERS) / ntile;  // batch * heads
+  const int nv = vec16 ? static_cast<int>(D * static_cast<int64_t>(sizeof(T)) / 16) : 0;
+  if (static_cast<int64_t>(L) >= BHt * ntile) {
+    // a padder: once every head's anchor count is out (the inclusive prefix of its last tile,
+    // a smaller ticket), zero slice (L - tiles) of each head's padding rows [anchors, capacity)
+    const int e = static_cast<int>(static_cast<int64_t>(L) - BHt * ntile);
+    for (int64_t bh = 0; bh < BHt; ++bh) {
+      if (tid == 0) {
+        const uint64_t* sw = status + bh * ntile + ntile - 1;
+        uint64_t w = pk_ld(sw);
+        if ((w >> 32) != ep || ((w >> 30) & 3u) != 2u) {
+          const uint64_t t0 = globaltimer();
+          while ((w >> 32) != ep || ((w >> 30) & 3u) != 2u) {
+            if (globaltimer() - t0 > DAB_WAIT_TIMEOUT_NS) {
+              atomicCAS(&hdr->err, 0, static_cast<int>(ERR_PACK_LOOKBACK));
+              w = pk_word(ep, 2u, static_cast<unsigned>(capacity < 0x3FFFFFFF ? capacity : 0x3FFFFFFF));
+              break;
+            }
+            w = pk_ld(sw);
+          }
+        }
+        s_base = static_cast<int32_t>(w & 0x3FFFFFFFu);
+      }
+      __syncthreads();
+      const int64_t A = s_base;
+      __syncthreads();
+      if (A >= capacity) continue;
+      const int64_t b = static_cast<int>(bh) / static_cast<int>(H), h = bh - b * H;
+      const int64_t per = (capacity - A + PACK_PADDERS - 1) / PACK_PADDERS;
+      const int64_t r0 = A + e * per, r1 = min(capacity, r0 + per);
+      for (int64_t jj = r0 + tid; jj < r1; jj += PACK_THREADS) {
+        ts[b * mb + h * mh + jj] = 0;
+        counts[b * mb + h * mh + jj] = 0;
+      }
+      if (vec16) {
+        for (int64_t i = tid; i < (r1 - r0) * nv; i += PACK_THREADS) {
+          const int64_t off = (b * pb + h * ph + (r0 + i / nv) * ps) * static_cast<int64_t>(sizeof(T)) + (i % nv) * 16;
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(kp) + off) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(vp) + off) = make_uint4(0, 0, 0, 0);
+        }
+      } else {
+        for (int64_t i = tid; i < (r1 - r0) * D; i += PACK_THREADS) {
+          const int64_t off = b * pb + h * ph + (r0 + i / D) * ps + i % D;
+          kp[off] = from_f32<T>(0.f);
+          vp[off] = from_f32<T>(0.f);
+        }
+      }
+    }
+  } else {
+    const int64_t bh = static_cast<int64_t>(L) / ntile, t = static_cast<int64_t>(L) - bh * ntile;
+    const int64_t b = static_cast<int>(bh) / static_cast<int>(H), h = bh - b * H;
+    const int32_t* krow = keep + b * kb + h * kh;
+    // this thread's TPT consecutive tokens, their kept count and the block-wide exclusive scan
+    const int64_t s0 = t * PACK_TILE + static_cast<int64_t>(tid) * TPT;
+    int kv[TPT];
+    int cnt = 0;
+#pragma unroll
+    for (int e = 0; e < TPT; ++e) {
+      kv[e] = (s0 + e < N) ? (krow[(s0 + e) * ks] == 1) : 0;
+      cnt += kv[e];
+    }
+    int incl = cnt;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int n = __shfl_up_sync(0xFFFFFFFFu, incl, o);
       if (lane >= o) incl += n;
     }
-    warp_off[lane] = incl - v0;
-    if (lane == 31) total = incl;
-  }
-  __syncthreads();
-  const int local = warp_off[warp] + in_warp;  // exclusive index of s among kept positions of the tile
-  const int32_t base = tile_off[bh * ntile + t];
-  const int32_t j = base + local;               // packed slot of s when kept
-  if (s < N && index_map) index_map[bh * N + s] = j + kv - 1;  // cumsum(keep) - 1
-  if (kv) pos_of[local] = static_cast<int32_t>(s);
-  __syncthreads();
-  if (kv && j < capacity) {
-    // run length: distance to the next anchor (or to N after the last one)
-    const int32_t nxt = (local + 1 < total) ? pos_of[local + 1] : next_first[bh * ntile + t];
-    ts[b * mb + h * mh + j] = static_cast<int32_t>(s);
-    counts[b * mb + h * mh + j] = nxt - static_cast<int32_t>(s);
-  }
-  if (vec16) {
-    // 16-byte rows: the warp's kept rows are flattened into (row, 16-byte piece) work items,
-    // lane i takes items i, i+32, ...; four items' loads are issued before their stores
-    const int nv = static_cast<int>(D * static_cast<int64_t>(sizeof(T)) / 16);
-    const int nrows = __popc(bal);
-    const int items = nrows * nv;
-    const int lbase = warp_off[warp];
-    for (int i0 = lane; i0 < items; i0 += 4 * 32) {
-      uint4 kr4[4], vr4[4];
-      int64_t dst[4];
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      const int v0 = lane < NW ? warp_tot[lane] : 0;
+      int wi = v0;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int idx = i0 + u * 32;
-        dst[u] = -1;
-        if (idx < items) {
-          const int r = idx / nv, c = idx % nv;
-          const int loc = lbase + r;
-          const int32_t jj = base + loc;
-          if (jj < capacity) {
-            const int64_t ss = pos_of[loc];
-            kr4[u] = *(reinterpret_cast<const uint4*>(k + b * xb + h * xh + ss * xs) + c);
-            vr4[u] = *(reinterpret_cast<const uint4*>(v + b * vb + h * vh + ss * vs) + c);
-            dst[u] = (b * pb + h * ph + static_cast<int64_t>(jj) * ps) * static_cast<int64_t>(sizeof(T)) + c * 16;
+      for (int o = 1; o < NW; o <<= 1) {
+        const int n = __shfl_up_sync(0xFFFFFFFFu, wi, o);
+        if (lane >= o) wi += n;
+      }
+      if (lane < NW) warp_tot[lane] = wi - v0;  // exclusive offset of warp `lane`
+      if (lane == NW - 1) total = wi;
+    }
+    __syncthreads();
+    const int tbase = warp_tot[warp] + incl - cnt;  // kept tokens of the tile before this thread's
+    if (warp == 0) {
+      // publish this tile's count, then look back over the head's earlier tiles for the offset:
+      // the warp reads 32 predecessors' status words at once, waits until each holds at least a
+      // count, and adds counts up to the nearest one that holds an inclusive prefix
+      if (lane == 0) pk_st(status + L, pk_word(ep, t == 0 ? 2u : 1u, static_cast<unsigned>(total)));
+      int32_t base = 0;
+      bool found = t == 0;
+      for (int64_t i0 = static_cast<int64_t>(L) - 1; !found; i0 -= 32) {
+        const int64_t i = i0 - lane;                          // lane l: predecessor i0 - l
+        const bool mine = i >= static_cast<int64_t>(L) - t;  // within this head
+        uint64_t w = mine ? pk_ld(status + i) : pk_word(ep, 2u, 0u);
+        if (mine && ((w >> 32) != ep || ((w >> 30) & 3u) == 0)) {
+          const uint64_t t0 = globaltimer();
+          while ((w >> 32) != ep || ((w >> 30) & 3u) == 0) {
+            if (globaltimer() - t0 > DAB_WAIT_TIMEOUT_NS) {
+              atomicCAS(&hdr->err, 0, static_cast<int>(ERR_PACK_LOOKBACK));
+              w = pk_word(ep, 2u, 0u);
+              break;
+            }
+            w = pk_ld(status + i);
           }
         }
-      }
+        const unsigned fl = __ballot_sync(0xFFFFFFFFu, ((w >> 30) & 3u) == 2u);  // lanes past the head count too
+        const int stop = __ffs(fl) - 1;  // nearest predecessor with an inclusive prefix (-1: none)
+        int32_t vsum = (stop < 0 || lane <= stop) ? static_cast<int32_t>(w & 0x3FFFFFFFu) : 0;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (dst[u] < 0) continue;
-        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(kp) + dst[u]) = kr4[u];
-        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(vp) + dst[u]) = vr4[u];
+        for (int o = 16; o; o >>= 1) vsum += __shfl_xor_sync(0xFFFFFFFFu, vsum, o);
+        base += vsum;
+        found = stop >= 0;
+      }
+      if (lane == 0) {
+        if (t != 0) pk_st(status + L, pk_word(ep, 2u, static_cast<unsigned>(base + total)));
+        s_base = base;
+      }
+    } else if (warp == 1) {
+      // first kept token after the tile (the run length of the tile's last anchor ends there)
+      int64_t nf = N;
+      for (int64_t q0 = (t + 1) * PACK_TILE; q0 < N; q0 += 32) {
+        const int64_t sl = q0 + lane;
+        const unsigned bb = __ballot_sync(0xFFFFFFFFu, sl < N && krow[sl * ks] == 1);
+        if (bb) {
+          nf = q0 + __ffs(bb) - 1;
+          break;
+        }
+      }
+      if (lane == 0) s_next = static_cast<int32_t>(nf);
+    }
+    __syncthreads();
+    const int32_t base = s_base;
+    int loc = tbase;
+#pragma unroll
+    for (int e = 0; e < TPT; ++e) {
+      const int64_t s = s0 + e;
+      if (s < N && index_map) index_map[bh * N + s] = base + loc + kv[e] - 1;  // cumsum(keep) - 1
+      if (kv[e]) pos_of[loc++] = static_cast<int32_t>(s);
+    }
+    __syncthreads();
+    const int tot = total;
+    int32_t* tsr = ts + b * mb + h * mh;
+    int32_t* cnr = counts + b * mb + h * mh;
+    for (int i = tid; i < tot; i += PACK_THREADS) {
+      const int32_t j = base + i;
+      if (j >= capacity) break;
+      // run length: distance to the next anchor (or to N after the last one)
+      const int32_t sp = pos_of[i];
+      const int32_t nxt = (i + 1 < tot) ? pos_of[i + 1] : s_next;
+      tsr[j] = sp;
+      cnr[j] = nxt - sp;
+    }
+    if (t == ntile - 1 && tid == 0) anchors[bh] = base + tot;
+    if (vec16) {
+      // 16-byte rows: the tile's kept rows as (row, 16-byte piece) items, thread i takes items
+      // i, i + PACK_THREADS, ...; four items' loads are issued before their stores
+      const int items = tot * nv;
+      const T* kh0 = k + b * xb + h * xh;
+      const T* vh0 = v + b * vb + h * vh;
+      uint8_t* kd0 = reinterpret_cast<uint8_t*>(kp + b * pb + h * ph);
+      uint8_t* vd0 = reinterpret_cast<uint8_t*>(vp + b * pb + h * ph);
+      for (int i0 = tid; i0 < items; i0 += 4 * PACK_THREADS) {
+        uint4 kr4[4], vr4[4];
+        int64_t dst[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int idx = i0 + u * PACK_THREADS;
+          dst[u] = -1;
+          if (idx < items) {
+            const int r = idx / nv, c = idx % nv;
+            const int32_t jj = base + r;
+            if (jj < capacity) {
+              const int64_t ss = pos_of[r];
+              kr4[u] = *(reinterpret_cast<const uint4*>(kh0 + ss * xs) + c);
+              vr4[u] = *(reinterpret_cast<const uint4*>(vh0 + ss * vs) + c);
+              dst[u] = static_cast<int64_t>(jj) * ps * static_cast<int64_t>(sizeof(T)) + c * 16;
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (dst[u] < 0) continue;
+          *reinterpret_cast<uint4*>(kd0 + dst[u]) = kr4[u];
+          *reinterpret_cast<uint4*>(vd0 + dst[u]) = vr4[u];
+        }
+      }
+    } else {
+      // element copies: warp w takes kept rows w, w + NW, ...
+      for (int r = warp; r < tot; r += NW) {
+        const int32_t jj = base + r;
+        if (jj >= capacity) break;
+        const int64_t ss = pos_of[r];
+        const T* kr = k + b * xb + h * xh + ss * xs;
+        const T* vr = v + b * vb + h * vh + ss * vs;
+        T* kd = kp + b * pb + h * ph + static_cast<int64_t>(jj) * ps;
+        T* vd = vp + b * pb + h * ph + static_cast<int64_t>(jj) * ps;
+        for (int64_t d = lane; d < D; d += 32) {
+          kd[d] = kr[d];
+          vd[d] = vr[d];
+        }
       }
     }
-    return;
+  }  // tile CTAs
+  // the launch's last CTA: the maximum anchor count, then the counters for the next launch
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const unsigned d = atomicAdd(&hdr->done, 1u);
+    s_last = d == gridDim.x - 1;
   }
-  // each warp copies the K/V rows of its kept lanes
-  for (unsigned m = bal; m; m &= m - 1) {
-    const int src = __ffs(m) - 1;
-    const int64_t ss = t * PACK_TILE + warp * 32 + src;
-    const int32_t jj = __shfl_sync(0xFFFFFFFFu, j, src);
-    if (jj >= capacity) continue;
-    const T* kr = k + b * xb + h * xh + ss * xs;
-    const T* vr = v + b * vb + h * vh + ss * vs;
-    T* kd = kp + b * pb + h * ph + static_cast<int64_t>(jj) * ps;
-    T* vd = vp + b * pb + h * ph + static_cast<int64_t>(jj) * ps;
-    for (int64_t d = lane; d < D; d += 32) {
-      kd[d] = kr[d];
-      vd[d] = vr[d];
+  __syncthreads();
+  if (s_last) {
+    __threadfence();
+    int32_t mx = 0;
+    for (int64_t i = tid; i < BHt; i += PACK_THREADS) mx = max(mx, *reinterpret_cast<volatile int32_t*>(anchors + i));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if (lane == 0) warp_tot[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+      for (int w = 1; w < NW; ++w) mx = max(mx, warp_tot[w]);
+      *max_anchors = mx;
+      hdr->ticket = 0u;
+      hdr->done = 0u;
+      hdr->epoch = ep;
+      __threadfence();
     }
   }
 }
 
-// slots [anchors[bh], capacity) of every head: zero K / V rows, timestamps and counts (the
-// reference packs into zero-initialised tensors; writing the padding here spares the caller a
-// memset of the whole packed history)
-template <typename T>
-__global__ void __launch_bounds__(256) pack_pad_kernel(T* __restrict__ kp, T* __restrict__ vp, int64_t pb, int64_t ph,
-                                                       int64_t ps, int32_t* __restrict__ ts,
-                                                       int32_t* __restrict__ counts, int64_t mb, int64_t mh,
-                                                       const int32_t* __restrict__ anchors, int64_t H, int64_t D,
-                                                       int64_t capacity, int vec16) {
-  const int64_t bh = blockIdx.y;
-  const int64_t b = static_cast<int>(bh) / static_cast<int>(H), h = bh - b * H;  // bh: a grid index
-  const int64_t j0 = anchors[bh] + static_cast<int64_t>(blockIdx.x) * 32;
-  if (j0 >= capacity) return;
-  const int64_t rows = (capacity - j0) < 32 ? (capacity - j0) : 32;
-  if (threadIdx.x < rows) {
-    ts[b * mb + h * mh + j0 + threadIdx.x] = 0;
-    counts[b * mb + h * mh + j0 + threadIdx.x] = 0;
-  }
-  if (vec16) {
-    const int nv = static_cast<int>(D * static_cast<int64_t>(sizeof(T)) / 16);
-    for (int64_t i = threadIdx.x; i < rows * nv; i += blockDim.x) {
-      const int64_t off = (b * pb + h * ph + (j0 + i / nv) * ps) * static_cast<int64_t>(sizeof(T)) + (i % nv) * 16;
-      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(kp) + off) = make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(vp) + off) = make_uint4(0, 0, 0, 0);
-    }
-  } else {
-    for (int64_t i = threadIdx.x; i < rows * D; i += blockDim.x) {
-      const int64_t off = b * pb + h * ph + (j0 + i / D) * ps + i % D;
-      kp[off] = from_f32<T>(0.f);
-      vp[off] = from_f32<T>(0.f);
-    }
-  }
+size_t pack_from_keep_workspace(int64_t BH, int64_t N) {
+  const int64_t ntile = (N + PACK_TILE - 1) / PACK_TILE;
+  return static_cast<size_t>(PACK_HDR + 8 * (BH > 0 ? BH : 1) * (ntile > 0 ? ntile : 1));
 }
 
 cudaError_t launch_pack_from_keep(int dtype, const int32_t* keep, const int64_t* kms, const void* k,
                                   const int64_t* xs, const void* v, const int64_t* vs, void* kp, void* vp,
                                   const int64_t* ps, int32_t* ts, int32_t* counts, const int64_t* ms,
                                   int32_t* index_map, int64_t B, int64_t H, int64_t N, int64_t D,
-                                  int64_t capacity, int32_t* ws, int32_t* anchors, int32_t* max_anchors,
+                                  int64_t capacity, uint8_t* ws, int32_t* anchors, int32_t* max_anchors,
                                   cudaStream_t st) {
   const int64_t ntile = (N + PACK_TILE - 1) / PACK_TILE;
   const int64_t BH = B * H;
   if (BH == 0 || N == 0) return cudaSuccess;
-  int32_t* tile_cnt = ws;
-  int32_t* tile_first = ws + BH * ntile;
-  int32_t* tile_off = ws + 2 * BH * ntile;
-  int32_t* next_first = ws + 3 * BH * ntile;
-  cudaMemsetAsync(max_anchors, 0, sizeof(int32_t), st);
-  keep_tile_count_kernel<<<dim3(static_cast<unsigned>(ntile), static_cast<unsigned>(BH)), PACK_TILE, 0, st>>>(
-      keep, kms[0], kms[1], kms[2], H, N, tile_cnt, tile_first, ntile);
-  keep_tile_scan_kernel<<<static_cast<unsigned>(BH), 32, 0, st>>>(tile_cnt, tile_first, tile_off, next_first,
-                                                                  anchors, max_anchors, ntile, N);
+  if (BH * ntile + PACK_PADDERS > (int64_t{1} << 31) - 1) return cudaErrorInvalidValue;
   const size_t es = dtype == F32 ? 4 : 2;
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   const int vec16 = al16(k) && al16(v) && al16(kp) && al16(vp) && (D * es) % 16 == 0 &&
                     ((xs[0] | xs[1] | xs[2] | vs[0] | vs[1] | vs[2] | ps[0] | ps[1] | ps[2]) * es) % 16 == 0;
-  const unsigned pad_blocks = static_cast<unsigned>((capacity + 31) / 32);
+  const unsigned grid = static_cast<unsigned>(BH * ntile + PACK_PADDERS);
 #define DAB_KP(TY)                                                                                               \
-  keep_pack_kernel<TY><<<dim3(static_cast<unsigned>(ntile), static_cast<unsigned>(BH)), PACK_TILE, 0, st>>>(     \
+  keep_pack_kernel<TY><<<grid, PACK_THREADS, 0, st>>>(                                                              \
       keep, kms[0], kms[1], kms[2], static_cast<const TY*>(k), xs[0], xs[1], xs[2],                             \
       static_cast<const TY*>(v), vs[0], vs[1], vs[2], static_cast<TY*>(kp), static_cast<TY*>(vp), ps[0],         \
-      ps[1], ps[2], ts, counts, ms[0], ms[1], index_map, tile_off, next_first, H, N, D, ntile, capacity, vec16); \
-  if (capacity > 0)                                                                                              \
-    pack_pad_kernel<TY><<<dim3(pad_blocks, static_cast<unsigned>(BH)), 256, 0, st>>>(                           \
-        static_cast<TY*>(kp), static_cast<TY*>(vp), ps[0], ps[1], ps[2], ts, counts, ms[0], ms[1], anchors, H, D, \
-        capacity, vec16);                                                                                        \
+      ps[1], ps[2], ts, counts, ms[0], ms[1], index_map, ws, anchors, max_anchors, H, N, D, ntile, capacity,     \
+      vec16);                                                                                                    \
   return cudaGetLastError();
   switch (dtype) {
     case F32: DAB_KP(float)

@@ -185,8 +185,7 @@ def pack_from_keep(k_rot: torch.Tensor, v: torch.Tensor, keep: torch.Tensor, num
     im = torch.empty((B, H, N), dtype=torch.int32, device=dev) if want_index_map else None
     lib = L.load()
     st = L.stream_of(k_rot)
-    wsb = lib.dab_pack_from_keep_workspace_size(B, H, N)
-    ws = torch.empty(max(int(wsb), 16), dtype=torch.uint8, device=dev)
+    ws = L.workspace(dev, st.value, int(lib.dab_pack_from_keep_workspace_size(B, H, N)), tag="pack")
     L.check(lib.dab_pack_from_keep(
         L.ptr(keep), L.strides(keep.stride()), L.ptr(k_rot), L.strides(k_rot.stride()), L.ptr(v),
         L.strides(v.stride()), L.ptr(kp), L.ptr(vp), L.strides(kp.stride()), L.ptr(ts), L.ptr(cnt),

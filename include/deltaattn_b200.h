@@ -241,7 +241,10 @@ int dab_proj_rope(const void* x, int64_t x_row_stride, const void* w, int64_t w_
 int dab_periodic_meta(int32_t* packed_ts, int32_t* packed_counts, float* packed_counts_f32, int64_t batch_heads,
                       int64_t num_packed, int64_t seq_len, int64_t period, void* stream);
 
-/* Scratch bytes dab_pack_from_keep needs. */
+/* Scratch bytes dab_pack_from_keep needs: a 64-byte header (error word first, then the
+ * launch's ticket / done counters and epoch) and one status word per 1024-token tile. The
+ * workspace must be zero-filled before its first use and is then reused as is, one
+ * workspace per stream (each launch leaves the counters reset). */
 size_t dab_pack_from_keep_workspace_size(int64_t batch, int64_t heads, int64_t seq_len);
 
 /* Device-side packing from a keep mask (modeling_llama.py:655-685 without the host sync at
@@ -249,7 +252,8 @@ size_t dab_pack_from_keep_workspace_size(int64_t batch, int64_t heads, int64_t s
  * timestamps and run-length counts into buffers of `capacity` rows, anchors per head and
  * their maximum (the reference's M). Rows beyond a head's anchors are written with zero
  * K / V, timestamp 0 and count 0: the reference's zero-initialised padding, so the caller
- * need not clear the buffers. */
+ * need not clear the buffers. One launch: tiles find their packed offsets by a look-back
+ * over the head's earlier tiles (bounded waits; a timeout sets the workspace's error word). */
 int dab_pack_from_keep(const int32_t* keep_mask, const int64_t* km_strides, const void* k, const int64_t* k_strides,
                        const void* v, const int64_t* v_strides, void* k_packed, void* v_packed,
                        const int64_t* pack_strides, int32_t* packed_ts, int32_t* packed_counts,

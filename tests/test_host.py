@@ -52,7 +52,7 @@ def test_host_only_entry_points(lib_path):
         nmb, nblk = -(-N // 128), max(1, -(-M // 128))
         want = 256 + r256(B * H * nmb * 8) + 2 * r256(B * H * nblk * 4)
         assert lib.dab_hybrid_flash_workspace_size(B, H, N, M) == want
-    assert lib.dab_pack_from_keep_workspace_size(2, 3, 5000) == 4 * 2 * 3 * 5 * 4
+    assert lib.dab_pack_from_keep_workspace_size(2, 3, 5000) == 64 + 8 * 2 * 3 * 5  # header + a word per tile
 
 
 def test_device_length_entries_reject_null_state(lib_path):
