@@ -438,6 +438,57 @@ def proj_rope_bench(dev, seed, reps=5):
     return out
 
 
+def dpxa_bench(dev, seed, reps=3):
+    """DPXA (delta-based tile scoring, Paper/src/methodology.tex:89-135) at cfg2 sizes: the
+    selection (anchor masks of Q and K per 128-token block, compaction, sampled tile scores,
+    top-p with p = 0.9) and the block-sparse attention over the selected tiles, against the
+    same kernel dense. Queries correlated with the keys at their own position (so attention
+    is local, as in a real layer) over AR(1) keys; thresholds keep about half the rows."""
+    from deltaattention_b200 import ops, synth
+    burst, _, _ = peaks()
+    stream = torch.cuda.current_stream(dev)
+    B, Hq, Hkv, N, D = 1, CFG["Hq"], CFG["Hkv"], CFG["N"], CFG["D"]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    k = synth.ar1((B, Hkv, N, D), g, dev).to(torch.bfloat16)
+    q = (0.5 * k.repeat_interleave(Hq // Hkv, 1).float()
+         + 0.2 * synth.ar1((B, Hq, N, D), g, dev)).to(torch.bfloat16)
+    v = (0.5 * torch.randn((B, Hkv, N, D), device=dev, generator=g)).to(torch.bfloat16)
+    cos, sin = synth.rope_tables(N, D, CFG["theta"], torch.bfloat16, device=dev)
+    qr, kr = ops.rope(q, cos, sin), ops.rope(k, cos, sin)
+    del q, k
+    dq = (qr[:, :, 1:].float() - qr[:, :, :-1].float()).pow(2).sum(-1).flatten()
+    dk = (kr[:, :, 1:].float() - kr[:, :, :-1].float()).pow(2).sum(-1).flatten()
+    tq = float(torch.quantile(dq[:: max(1, dq.numel() // 1000000)], 0.9)) ** 0.5
+    tk = float(torch.quantile(dk[:: max(1, dk.numel() // 1000000)], 0.9)) ** 0.5
+    del dq, dk
+
+    def timed(fn):
+        fn()
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+    p = 0.9
+    sel_ms = timed(lambda: ops.dpxa_select(qr, kr, tq, tk, p))
+    sel, (kq, kk, _, _) = ops.dpxa_select(qr, kr, tq, tk, p, return_stats=True)
+    nb = N // 128
+    mask = ops.selection_to_mask(sel, nb)
+    tiles = int(mask.sum()) * (Hq // Hkv)        # q-head tiles the sparse attention runs
+    attn_ms = timed(lambda: ops.block_sparse_attention(qr, kr, v, sel))
+    dense_ms = timed(lambda: ops.flash(qr, kr, v))
+    flops = tiles * 4 * 128 * 128 * D
+    return {"top_p": p, "anchor_fraction_q": float(kq.float().mean()), "anchor_fraction_k": float(kk.float().mean()),
+            "selected_tile_fraction": tiles / (Hq * nb * (nb + 1) / 2), "selection_ms": sel_ms,
+            "sparse_attention_ms": attn_ms, "dense_r1_ms": dense_ms,
+            "sparse_attention_tflops": flops / attn_ms / 1e9, "frac_of_burst": flops / attn_ms / 1e9 / burst,
+            "speedup_vs_dense": dense_ms / (attn_ms + sel_ms)}
+
+
 def traffic_per_launch():
     """DRAM bytes per attention launch from the committed ncu summary, if present."""
     try:
@@ -977,6 +1028,7 @@ def run_ours(args, world, rank, local):
         line["hbm_kernels"] = {"peak_gbs": hbm_peak()[0], "peak_kind": hbm_peak()[1], **hk_}
     if world == 1 and not args.no_sweep:
         line["proj_rope"] = proj_rope_bench(dev, 6000 + rank)
+        line["dpxa"] = dpxa_bench(dev, 7000 + rank)
         line["decode_step"] = decode_step(dev, 4000 + rank)
         line["serving_cfg5"] = serving(dev, 5000 + rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

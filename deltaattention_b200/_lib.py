@@ -54,6 +54,10 @@ SIGNATURES = {
     "dab_decode_advance": (I32, [P, I64, P]),
     "dab_rope": (I32, [P, PI64, P, PI64, P, P, PI64, I32, I64, I64, I64, I64, P]),
     "dab_proj_rope": (I32, [P, I64, P, I64, P, P, I64, P, I64, I32, I64, I64, I64, I64, I64, I64, P, SZ, P]),
+    "dab_dpxa_compact": (I32, [P, PI64, P, PI64, P, P, P, I32, I64, I64, I64, I64, P]),
+    "dab_dpxa_score": (I32, [P, P, P, P, P, P, P, P, F32, I32, I64, I64, I64, I64, I64, P]),
+    "dab_dpxa_select": (I32, [P, P, P, F32, I64, I64, I64, I64, P]),
+    "dab_block_sparse_attention": (I32, [P, P, P, P, P, I32, PI64, F32, I64, I64, I64, I64, I64, P, SZ, P]),
     "dab_periodic_meta": (I32, [P, P, P, I64, I64, I64, I64, P]),
     "dab_pack_from_keep_workspace_size": (SZ, [I64, I64, I64]),
     "dab_nm_select": (I32, [P, PI64, P, PI64, I32, I64, I64, I64, I64, I64, I64, I64, P]),

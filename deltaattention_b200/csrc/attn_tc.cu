@@ -24,7 +24,7 @@
 
 namespace dab {
 
-enum TcVariant : int { TC_HYBRID = 0, TC_SANITY = 1, TC_PURE = 2, TC_DENSE = 3 };
+enum TcVariant : int { TC_HYBRID = 0, TC_SANITY = 1, TC_PURE = 2, TC_DENSE = 3, TC_SPARSE = 4 };
 
 constexpr int TC_THREADS = 384;
 constexpr int TC_BM = 128;
@@ -221,13 +221,35 @@ struct TileInfo {
 
 // Enumerates the union of both query tiles' block lists in reference order (all packed
 // blocks first, then dense blocks ascending). Every role walks the same sequence.
-struct TileSeq {
+// SPARSE (DPXA block-sparse attention): the dense key blocks set in each tile's bitmask, up to
+// and including its diagonal block, ascending.
+template <bool SPARSE>
+struct TileSeqT {
   int n1[2], ds[2], de[2];
   int pmax, dlo, dhi;
   int state, cur;  // state 0: packed, 1: dense, 2: done
   int mb_lo[2];
+  const uint32_t* mrow[2];  // SPARSE: the tiles' bitmask rows
+  int widx;                 // SPARSE: index of the mask word held in wrd
+  uint32_t wrd[2];
   __device__ __forceinline__ void init(const TcParams& p, const Unit& U) { init(p, U, fetch_sched(p, U)); }
   __device__ __forceinline__ void init(const TcParams& p, const Unit& U, const UnitSched& us) {
+    if constexpr (SPARSE) {
+      dlo = 0;
+      dhi = 0;
+      #pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        mb_lo[x] = U.mb[x];
+        mrow[x] = U.valid[x] ? p.sel + (static_cast<int64_t>(U.b * p.Hts + U.hts[x]) * p.nmb + U.mb[x]) * p.sel_words
+                             : nullptr;
+        if (U.valid[x]) dhi = max(dhi, U.mb[x] + 1);
+      }
+      widx = -1;
+      wrd[0] = wrd[1] = 0u;
+      state = 1;
+      cur = 0;
+      return;
+    }
     const int num_packed = packed_len(p);
     #pragma unroll
     for (int x = 0; x < 2; ++x) {
@@ -264,6 +286,30 @@ struct TileSeq {
   }
 
   __device__ __forceinline__ bool next(const TcParams& p, const Unit& U, TileInfo& t) {
+    if constexpr (SPARSE) {
+      // blocks up to each tile's diagonal (mb_lo holds the query block here), in mask order
+      while (cur < dhi) {
+        const int w = cur >> 5;
+        if (w != widx) {
+          widx = w;
+          #pragma unroll
+          for (int x = 0; x < 2; ++x) wrd[x] = mrow[x] ? __ldg(mrow[x] + w) : 0u;
+        }
+        const uint32_t any = (wrd[0] | wrd[1]) >> (cur & 31);
+        if (!any) { cur = (w + 1) << 5; continue; }
+        const int j = cur + __ffs(any) - 1;
+        cur = j + 1;
+        int use = 0;
+        #pragma unroll
+        for (int x = 0; x < 2; ++x)
+          if (mrow[x] && j <= mb_lo[x] && ((wrd[x] >> (j & 31)) & 1u)) use |= 1 << x;
+        if (!use) continue;
+        t.packed = 0; t.idx = j; t.use = use; t.needs_v = 1;
+        return true;
+      }
+      state = 2;
+      return false;
+    }
     while (state == 0) {
       if (cur >= pmax) { state = 1; cur = dlo; break; }
       const int j = cur++;
@@ -311,9 +357,10 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t par, const Abo
 // probability by its key's count (a multiply by the count staged with the V tile) instead of
 // one per-block exponent offset, so such blocks stay off the exact two-pass path; one copy of
 // the unrolled exponential loop either way (dense blocks read unit weights).
-template <int D, bool BF16, bool KEYED>
+template <int D, bool BF16, bool KEYED, bool SPARSE>
 __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_constant__ TcParams p) {
   using C = TcCfg<D>;
+  using TileSeq = TileSeqT<SPARSE>;
   constexpr int NK = C::NK, NV = C::NV;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1022,10 +1069,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
   if (warp == 2) tmem_dealloc(tmem, 512);
 }
 
-template <int D, bool BF16, bool KEYED>
+template <int D, bool BF16, bool KEYED, bool SPARSE = false>
 static cudaError_t launch_tc_t(const TcParams& p, int num_sms, cudaStream_t st) {
   using C = TcCfg<D>;
-  auto kfn = attn_tc_kernel<D, BF16, KEYED>;
+  auto kfn = attn_tc_kernel<D, BF16, KEYED, SPARSE>;
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int grid = p.num_units < num_sms ? p.num_units : num_sms;
@@ -1035,6 +1082,13 @@ static cudaError_t launch_tc_t(const TcParams& p, int num_sms, cudaStream_t st) 
 }
 
 cudaError_t launch_attn_tc(int head_dim, bool bf16, const TcParams& p, int num_sms, cudaStream_t st) {
+  if (p.variant == TC_SPARSE) {
+    if (head_dim == 128)
+      return bf16 ? launch_tc_t<128, true, false, true>(p, num_sms, st) : launch_tc_t<128, false, false, true>(p, num_sms, st);
+    if (head_dim == 64)
+      return bf16 ? launch_tc_t<64, true, false, true>(p, num_sms, st) : launch_tc_t<64, false, false, true>(p, num_sms, st);
+    return cudaErrorInvalidValue;
+  }
   // per-key weights on the streaming path only where it runs (bf16) and the counts are fp32
   const bool keyed = p.keyed && bf16 && !p.counts_is_int;
   if (head_dim == 128)

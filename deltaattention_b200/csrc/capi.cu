@@ -49,6 +49,11 @@ cudaError_t launch_nm_select(int, const void*, const int64_t*, int32_t*, const i
 cudaError_t launch_key_compress(int, int, bool, CompressParams, cudaStream_t);
 size_t key_compress_workspace(int64_t, int64_t, int64_t, int64_t);
 cudaError_t launch_proj_rope(const ProjParams&, int, cudaStream_t);
+cudaError_t launch_dpxa_compact(int, const void*, const int64_t*, const int32_t*, const int64_t*, void*, int32_t*,
+                                int32_t*, int, int, int, int, cudaStream_t);
+cudaError_t launch_dpxa_score(int, const void*, const int32_t*, const int32_t*, const void*, const int32_t*,
+                              const int32_t*, float*, float*, float, int, int, int, int, int, cudaStream_t);
+cudaError_t launch_dpxa_select(const float*, const float*, uint32_t*, float, int, int, int, int, cudaStream_t);
 }  // namespace dab
 
 using namespace dab;
@@ -590,6 +595,99 @@ int dab_proj_rope(const void* x, int64_t x_row_stride, const void* w, int64_t w_
   if (tiles > INT32_MAX) return fail(1, "dab_proj_rope: too many tiles");
   p.num_tiles = static_cast<int>(tiles);
   return cuda_status(launch_proj_rope(p, num_sms(), static_cast<cudaStream_t>(stream)), "proj_rope");
+}
+
+// ------------------------------------------------------------------------- DPXA
+int dab_dpxa_compact(const void* x, const int64_t* x_strides, const int32_t* keep_mask, const int64_t* km_strides,
+                     void* compact, int32_t* positions, int32_t* counts, int dtype, int64_t batch, int64_t heads,
+                     int64_t seq_len, int64_t head_dim, void* stream) {
+  if (!x || !x_strides || !keep_mask || !km_strides || !compact || !positions || !counts)
+    return fail(1, "dab_dpxa_compact: null pointer");
+  if (dtype != BF16 && dtype != F16) return fail(1, "dab_dpxa_compact: bf16 or fp16 only");
+  if (head_dim != 64 && head_dim != 128) return fail(1, "dab_dpxa_compact: head_dim must be 64 or 128");
+  if (x_strides[3] != 1 || x_strides[2] % 8 || !aligned16(x) || !aligned16(compact))
+    return fail(1, "dab_dpxa_compact: rows must be contiguous and 16-byte aligned");
+  if (batch * heads > 65535 || seq_len >= (int64_t{1} << 30)) return fail(1, "dab_dpxa_compact: size too large");
+  return cuda_status(launch_dpxa_compact(dtype, x, x_strides, keep_mask, km_strides, compact, positions, counts,
+                                         static_cast<int>(batch), static_cast<int>(heads), static_cast<int>(seq_len),
+                                         static_cast<int>(head_dim), static_cast<cudaStream_t>(stream)),
+                     "dpxa_compact");
+}
+
+int dab_dpxa_score(const void* q_compact, const int32_t* q_positions, const int32_t* q_counts,
+                   const void* k_compact, const int32_t* k_positions, const int32_t* k_counts, float* tile_max,
+                   float* tile_sum, float sm_scale, int dtype, int64_t batch, int64_t num_q_heads, int64_t kv_group,
+                   int64_t seq_len, int64_t head_dim, void* stream) {
+  if (!q_compact || !q_positions || !q_counts || !k_compact || !k_positions || !k_counts || !tile_max || !tile_sum)
+    return fail(1, "dab_dpxa_score: null pointer");
+  if (dtype != BF16 && dtype != F16) return fail(1, "dab_dpxa_score: bf16 or fp16 only");
+  if (head_dim != 64 && head_dim != 128) return fail(1, "dab_dpxa_score: head_dim must be 64 or 128");
+  if (kv_group < 1 || num_q_heads % kv_group) return fail(1, "dab_dpxa_score: bad kv_group");
+  if (batch * num_q_heads > 65535 || seq_len >= (int64_t{1} << 30)) return fail(1, "dab_dpxa_score: size too large");
+  return cuda_status(launch_dpxa_score(dtype, q_compact, q_positions, q_counts, k_compact, k_positions, k_counts,
+                                       tile_max, tile_sum, sm_scale, static_cast<int>(batch),
+                                       static_cast<int>(num_q_heads), static_cast<int>(kv_group),
+                                       static_cast<int>(seq_len), static_cast<int>(head_dim),
+                                       static_cast<cudaStream_t>(stream)),
+                     "dpxa_score");
+}
+
+int dab_dpxa_select(const float* tile_max, const float* tile_sum, uint32_t* selection, float top_p, int64_t batch,
+                    int64_t num_kv_heads, int64_t kv_group, int64_t seq_len, void* stream) {
+  if (!tile_max || !tile_sum || !selection) return fail(1, "dab_dpxa_select: null pointer");
+  if (kv_group < 1 || batch * num_kv_heads > 65535) return fail(1, "dab_dpxa_select: bad sizes");
+  if ((seq_len + 127) / 128 > 2048) return fail(1, "dab_dpxa_select: at most 2048 key blocks (256 k tokens)");
+  return cuda_status(launch_dpxa_select(tile_max, tile_sum, selection, top_p, static_cast<int>(batch),
+                                        static_cast<int>(num_kv_heads), static_cast<int>(kv_group),
+                                        static_cast<int>(seq_len), static_cast<cudaStream_t>(stream)),
+                     "dpxa_select");
+}
+
+int dab_block_sparse_attention(const void* q, const void* k, const void* v, const uint32_t* selection, void* out,
+                               int dtype, const int64_t* strides, float sm_scale, int64_t batch, int64_t num_q_heads,
+                               int64_t kv_group, int64_t seq_len, int64_t head_dim, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  const char* nm = "dab_block_sparse_attention";
+  if (!q || !k || !v || !selection || !out || !strides || !workspace) return fail(1, std::string(nm) + ": null pointer");
+  if (dtype != BF16 && dtype != F16) return fail(1, std::string(nm) + ": bf16 or fp16 only");
+  if (head_dim != 64 && head_dim != 128) return fail(1, std::string(nm) + ": head_dim must be 64 or 128");
+  if (kv_group < 1 || num_q_heads % kv_group || batch < 1 || seq_len < 1 || seq_len >= (int64_t{1} << 31))
+    return fail(1, std::string(nm) + ": bad sizes");
+  if (workspace_bytes < WS_HEADER) return fail(1, std::string(nm) + ": workspace smaller than 256 bytes");
+  const int64_t* qs = strides;
+  const int64_t* ks = strides + 4;
+  const int64_t* vs = strides + 8;
+  const int64_t* os = strides + 12;
+  if (qs[3] != 1 || ks[3] != 1 || vs[3] != 1 || os[3] != 1 || !aligned16(q) || !aligned16(k) || !aligned16(v))
+    return fail(1, std::string(nm) + ": unit head-dim strides and 16-byte aligned rows required");
+  const int64_t Hts = num_q_heads / kv_group;
+  const int64_t nmb = (seq_len + 127) / 128;
+  TcParams p;
+  std::memset(&p, 0, sizeof(p));
+  bool ok = encode_rows(&p.tm_q, q, dtype, head_dim, seq_len, num_q_heads, batch, qs[2], qs[1], qs[0]);
+  ok = ok && encode_rows(&p.tm_kd, k, dtype, head_dim, seq_len, Hts, batch, ks[2], ks[1], ks[0]);
+  ok = ok && encode_rows(&p.tm_vd, v, dtype, head_dim, seq_len, Hts, batch, vs[2], vs[1], vs[0]);
+  if (!ok) return fail(1, std::string(nm) + ": tensor map encoding failed (layout not TMA-compatible)");
+  p.tm_kp = p.tm_kd;
+  p.tm_vp = p.tm_vd;
+  p.err = static_cast<int*>(workspace);
+  p.out = out;
+  p.os_b = os[0]; p.os_h = os[1]; p.os_m = os[2];
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.seq_q = static_cast<int>(seq_len); p.seq_k = static_cast<int>(seq_len);
+  p.B = static_cast<int>(batch); p.Hq = static_cast<int>(num_q_heads); p.kv_group = static_cast<int>(kv_group);
+  p.Hts = static_cast<int>(Hts);
+  p.nmb = static_cast<int>(nmb);
+  p.variant = 4;  // TC_SPARSE
+  p.causal = 1;
+  p.pair_heads = (kv_group % 2 == 0) ? 1 : 0;
+  p.num_units = static_cast<int>(p.pair_heads ? nmb * batch * Hts * (kv_group / 2) : ((nmb + 1) / 2) * batch * num_q_heads);
+  p.out_vec_ok = aligned16(out) && (os[0] * 2) % 16 == 0 && (os[1] * 2) % 16 == 0 && (os[2] * 2) % 16 == 0;
+  p.len_dev = reinterpret_cast<const int*>(static_cast<uint8_t*>(workspace) + 4);
+  p.sel = selection;
+  p.sel_words = static_cast<int>((nmb + 31) / 32);
+  return cuda_status(launch_attn_tc(static_cast<int>(head_dim), dtype == BF16, p, num_sms(), static_cast<cudaStream_t>(stream)),
+                     nm);
 }
 
 int dab_periodic_meta(int32_t* packed_ts, int32_t* packed_counts, float* packed_counts_f32, int64_t batch_heads,

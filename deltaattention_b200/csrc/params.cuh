@@ -47,6 +47,10 @@ struct TcParams {
   const int32_t* anchors;
   const int* len_dev;
   int keyed;               // packed blocks' counts differ inside blocks: weight per key on the fast path
+  // block-sparse variant (DPXA): bitmask of the key blocks each (batch, kv-head, query block)
+  // attends, `sel_words` 32-bit words per query block
+  const uint32_t* sel;
+  int sel_words;
 };
 
 // fused key compression (compress.cu): strides in elements

@@ -47,6 +47,91 @@ def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: Optional[to
     return out
 
 
+def dpxa_select(q_rot: torch.Tensor, k_rot: torch.Tensor, tau_q: float, tau_k: float, top_p: float,
+                sm_scale: Optional[float] = None, return_stats: bool = False):
+    """DPXA tile selection (Paper/src/methodology.tex:89-135, as the library specifies it).
+
+    q_rot [B, Hq, N, d], k_rot [B, Hkv, N, d] post-RoPE, bf16 / fp16, d 64 or 128. Steps: the
+    delta selection (Euclidean, thresholds tau_q / tau_k, squared inside as the reference) on
+    every 128-token block of Q and K; each block's anchors compacted; sampled tile scores
+    Q^d K^d^T (causal on the diagonal) reduced to a tile importance; per query block the
+    tiles taken by decreasing weight (the weights of a GQA group's q-heads averaged) until the
+    cumulative weight exceeds ``top_p``, the diagonal always. Returns the selection bitmask
+    [B, Hkv, nb, ceil(nb/32)] int32 (bit j of query block i: key block j attended), and with
+    ``return_stats`` also (keep_q, keep_k, tile_max, tile_sum) [B, Hq, nb, nb].
+    """
+    L.require_cuda(q_rot, k_rot)
+    B, Hq, N, D = q_rot.shape
+    Hkv = k_rot.shape[1]
+    if Hq % Hkv:
+        raise ValueError("query heads must be a multiple of kv heads")
+    if sm_scale is None:
+        sm_scale = D ** -0.5
+    nb = -(-N // 128)
+    dev = q_rot.device
+    lib = L.load()
+    st = L.stream_of(q_rot)
+    keep_q, _ = delta_keep_mask(q_rot, tau_q, "euclidean", 128)
+    keep_k, _ = delta_keep_mask(k_rot, tau_k, "euclidean", 128)
+    out = {}
+    for name, x, keep, H in (("q", q_rot, keep_q, Hq), ("k", k_rot, keep_k, Hkv)):
+        cx = torch.empty((B, H, nb, 128, D), dtype=x.dtype, device=dev)
+        pos = torch.empty((B, H, nb, 128), dtype=torch.int32, device=dev)
+        cnt = torch.empty((B, H, nb), dtype=torch.int32, device=dev)
+        L.check(lib.dab_dpxa_compact(L.ptr(x), L.strides(x.stride()), L.ptr(keep), L.strides(keep.stride()), L.ptr(cx),
+                                     L.ptr(pos), L.ptr(cnt), L.dtype_code(x), B, H, N, D, st), "dpxa_compact")
+        out[name] = (cx, pos, cnt)
+    tmax = torch.full((B, Hq, nb, nb), float("-inf"), dtype=torch.float32, device=dev)
+    tsum = torch.zeros((B, Hq, nb, nb), dtype=torch.float32, device=dev)
+    (cq, qp, qc), (ck, kp_, kc) = out["q"], out["k"]
+    L.check(lib.dab_dpxa_score(L.ptr(cq), L.ptr(qp), L.ptr(qc), L.ptr(ck), L.ptr(kp_), L.ptr(kc), L.ptr(tmax),
+                               L.ptr(tsum), float(sm_scale), L.dtype_code(q_rot), B, Hq, Hq // Hkv, N, D, st),
+            "dpxa_score")
+    sel = torch.empty((B, Hkv, nb, -(-nb // 32)), dtype=torch.int32, device=dev)
+    L.check(lib.dab_dpxa_select(L.ptr(tmax), L.ptr(tsum), L.ptr(sel), float(top_p), B, Hkv, Hq // Hkv, N, st),
+            "dpxa_select")
+    if return_stats:
+        return sel, (keep_q, keep_k, tmax, tsum)
+    return sel
+
+
+def selection_to_mask(sel: torch.Tensor, nb: int) -> torch.Tensor:
+    """The bitmask of ``dpxa_select`` as bool [B, Hkv, nb, nb]."""
+    j = torch.arange(nb, device=sel.device)
+    words = sel.to(torch.int64) & 0xFFFFFFFF
+    return ((words[..., j // 32] >> (j % 32)) & 1).bool()
+
+
+def block_sparse_attention(q_rot, k_rot, v, sel, *, sm_scale=None, out=None):
+    """Causal attention over the selected 128-key blocks only (DPXA step 5) on the tcgen05
+    kernel: q_rot [B, Hq, N, d], k_rot / v [B, Hkv, N, d], ``sel`` from ``dpxa_select``."""
+    L.require_cuda(q_rot, k_rot, v, sel, out)
+    B, Hq, N, D = q_rot.shape
+    Hkv = k_rot.shape[1]
+    if sm_scale is None:
+        sm_scale = D ** -0.5
+    if out is None:
+        out = torch.empty((B, Hq, N, D), dtype=q_rot.dtype, device=q_rot.device)
+    nb = -(-N // 128)
+    if tuple(sel.shape) != (B, Hkv, nb, -(-nb // 32)) or not sel.is_contiguous():
+        raise ValueError("block_sparse_attention: selection must be a contiguous [B, Hkv, nb, words] bitmask")
+    lib = L.load()
+    st = L.stream_of(q_rot)
+    ws = L.workspace(q_rot.device, st.value, 256)
+    strides = [*q_rot.stride(), *k_rot.stride(), *v.stride(), *out.stride()]
+    L.check(lib.dab_block_sparse_attention(L.ptr(q_rot), L.ptr(k_rot), L.ptr(v), L.ptr(sel), L.ptr(out),
+                                           L.dtype_code(q_rot), L.strides(strides), float(sm_scale), B, Hq, Hq // Hkv,
+                                           N, D, L.ptr(ws), ws.numel(), st), "block_sparse_attention")
+    return out
+
+
+def dpxa_prefill(q, k, v, cos, sin, *, tau_q: float, tau_k: float, top_p: float, sm_scale=None):
+    """One DPXA attention layer-op: RoPE(q, k), tile selection, block-sparse attention."""
+    q_rot, k_rot = rope(q, cos, sin), rope(k, cos, sin)
+    sel = dpxa_select(q_rot, k_rot, tau_q, tau_k, top_p, sm_scale)
+    return block_sparse_attention(q_rot, k_rot, v, sel, sm_scale=sm_scale)
+
+
 def proj_rope(x: torch.Tensor, w: torch.Tensor, cos: Optional[torch.Tensor] = None,
               sin: Optional[torch.Tensor] = None, rope_cols: Optional[tuple] = None,
               out: Optional[torch.Tensor] = None) -> torch.Tensor:

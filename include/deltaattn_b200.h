@@ -231,6 +231,39 @@ int dab_proj_rope(const void* x, int64_t x_row_stride, const void* w, int64_t w_
                   int64_t rows, int64_t in_features, int64_t out_features, int64_t head_dim, int64_t rope_lo,
                   int64_t rope_hi, void* workspace, size_t workspace_bytes, void* stream);
 
+/* DPXA: delta-based tile scoring for block-sparse prefill (Paper/src/methodology.tex:89-135;
+ * the paper ships no code, so these entries implement the library's specification of it).
+ *
+ * dab_dpxa_compact: the anchors of every 128-token block (keep_mask from the delta selection
+ * with chunk 128, e.g. dab_chunked_eval) gathered to the front of the block: `compact`
+ * [B][H][nb][128][head_dim], their positions [B][H][nb][128] and counts [B][H][nb] int32.
+ * x [B, H, N, d] with unit d-stride and 16-byte aligned rows; bf16 / fp16, d 64 or 128. */
+int dab_dpxa_compact(const void* x, const int64_t* x_strides, const int32_t* keep_mask, const int64_t* km_strides,
+                     void* compact, int32_t* positions, int32_t* counts, int dtype, int64_t batch, int64_t heads,
+                     int64_t seq_len, int64_t head_dim, void* stream);
+/* dab_dpxa_score: for every (batch, q-head, query block i, key block j <= i) the sampled tile
+ * scores S = sm_scale * Q^d_i K^d_j^T over the compacted anchors (K of kv-head h / kv_group),
+ * causal by anchor position on the diagonal tile, reduced to tile_max = max S and
+ * tile_sum = sum exp(S - tile_max), fp32 [B][Hq][nb][nb]; entries j > i are not written. */
+int dab_dpxa_score(const void* q_compact, const int32_t* q_positions, const int32_t* q_counts,
+                   const void* k_compact, const int32_t* k_positions, const int32_t* k_counts, float* tile_max,
+                   float* tile_sum, float sm_scale, int dtype, int64_t batch, int64_t num_q_heads, int64_t kv_group,
+                   int64_t seq_len, int64_t head_dim, void* stream);
+/* dab_dpxa_select: per (batch, kv-head, query block) the tiles' sampled attention mass
+ * averaged over the group's q-heads, taken by decreasing weight (ties to the lower block)
+ * until the cumulative weight exceeds top_p, plus the diagonal: bitmask `selection`
+ * [B][Hkv][nb][ceil(nb / 32)] (bit j of word j / 32). nb <= 2048. */
+int dab_dpxa_select(const float* tile_max, const float* tile_sum, uint32_t* selection, float top_p, int64_t batch,
+                    int64_t num_kv_heads, int64_t kv_group, int64_t seq_len, void* stream);
+/* Causal attention over the selected 128-key blocks only (the tcgen05 kernel walking the
+ * bitmask), full K / V: q [B, Hq, N, d], k / v [B, Hq / kv_group, N, d], out [B, Hq, N, d];
+ * `strides` q, k, v, out (4 each, elements). bf16 / fp16, d 64 or 128, unit d-stride,
+ * 16-byte aligned rows. `workspace` holds the 256-byte error header. */
+int dab_block_sparse_attention(const void* q, const void* k, const void* v, const uint32_t* selection, void* out,
+                               int dtype, const int64_t* strides, float sm_scale, int64_t batch, int64_t num_q_heads,
+                               int64_t kv_group, int64_t seq_len, int64_t head_dim, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* Packed timestamps / counts of periodic packing (modeling_llama.py:626-632 followed by
  * :655-685): anchor j at j*period covering min(period, seq_len - j*period) tokens.
  * Buffers are [batch_heads][num_packed] contiguous; num_packed must be ceil(seq_len/period).

@@ -31,7 +31,8 @@ __all__ = [
     "delta_keep_mask", "periodic_keep_mask", "random_keep_mask", "nm_keep_mask",
     "pack_from_keep", "hybrid_schedule", "tile_count", "hybrid_attention",
     "flash_attention", "decode_update", "decode_attention", "sq_dist_f32",
-    "eager_attention", "proj_rope",
+    "eager_attention", "proj_rope", "dpxa_keep", "dpxa_tile_stats", "dpxa_weights", "dpxa_select",
+    "block_sparse_attention",
 ]
 
 # ---------------------------------------------------------------------------
@@ -505,6 +506,129 @@ def eager_attention(q, k, v, sm_scale: float, n_rep: int = 1, query_rows: Option
     w = w + mask
     w = torch.softmax(w, dim=-1, dtype=torch.float32).to(q.dtype)
     return torch.matmul(w, v)
+
+
+# ---------------------------------------------------------------------------
+# DPXA: delta-based tile scoring for block-sparse prefill (Paper/src/methodology.tex:89-135)
+#
+# The paper describes the method without code; this is the builder's specification, which
+# the CUDA path implements and these functions restate:
+#   1. Compaction: Stage-1 delta selection (the chunked_eval_kernel rule, Euclidean, squared
+#      threshold) over every 128-token block of post-RoPE Q (threshold tau_q) and of
+#      post-RoPE K (tau_k); each block's first row is an anchor; anchors keep their order.
+#   2. Sampled scores per tile (query block i of q-head h, key block j <= i of its kv-head):
+#      S = scale * Q^d_i K^d_j^T over the anchors only, causal inside the diagonal tile
+#      (anchor key position <= anchor query position).
+#   3. Tile importance: the sum of exp(S) over the tile's valid cells, kept as (max, sum of
+#      exp(S - max)) per tile so no exponential overflows.
+#   4. Top-p selection: per q-head the tile weights of a query block are its tiles'
+#      importance over their total (the sampled attention mass); the q-heads of a GQA group
+#      share one selection (their weights averaged), so the group's K / V blocks are read
+#      once. Tiles are taken in decreasing weight (ties to the lower block) until the
+#      cumulative weight exceeds p; the diagonal tile is always taken.
+#   5. Attention: causal softmax attention of the full Q against the full K / V of the
+#      selected key blocks only.
+# ---------------------------------------------------------------------------
+
+def dpxa_keep(x: torch.Tensor, threshold: float, block: int = 128) -> torch.Tensor:
+    """Step 1: anchor mask of every ``block``-token block (chunked_eval_kernel with chunk =
+    block, Euclidean; ``threshold`` is the squared distance threshold)."""
+    N = x.shape[2]
+    keep, _ = delta_keep_mask(x, threshold, False, block, -(-N // block))
+    return keep
+
+
+def dpxa_tile_stats(q, k, keep_q, keep_k, sm_scale: float, n_rep: int, block: int = 128):
+    """Steps 2-3: per (b, q-head, query block i, key block j <= i) the tile's maximum scaled
+    sampled score and the sum of exp(S - max) over its valid cells (fp64 here). Tiles with
+    j > i, or without a valid cell, hold (-inf, 0). Returns (tmax, tsum) [B, Hq, nb, nb]."""
+    B, Hq, N, D = q.shape
+    nb = -(-N // block)
+    tmax = torch.full((B, Hq, nb, nb), float("-inf"), dtype=torch.float64)
+    tsum = torch.zeros((B, Hq, nb, nb), dtype=torch.float64)
+    qf, kf = q.double(), k.double()
+    for b in range(B):
+        for h in range(Hq):
+            hk = h // n_rep
+            kblocks = []
+            for j in range(nb):
+                idx = torch.nonzero(keep_k[b, hk, j * block:(j + 1) * block]).flatten() + j * block
+                kblocks.append((idx, kf[b, hk, idx]))
+            for i in range(nb):
+                qi = torch.nonzero(keep_q[b, h, i * block:(i + 1) * block]).flatten() + i * block
+                qa = qf[b, h, qi]
+                for j in range(i + 1):
+                    kj, ka = kblocks[j]
+                    sc = (qa @ ka.T) * sm_scale
+                    if j == i:
+                        sc = torch.where(kj[None, :] <= qi[:, None], sc, torch.tensor(float("-inf"), dtype=sc.dtype))
+                    m = sc.max() if sc.numel() else torch.tensor(float("-inf"))
+                    if torch.isfinite(m):
+                        tmax[b, h, i, j] = m
+                        tsum[b, h, i, j] = torch.exp(sc - m).sum()
+    return tmax, tsum
+
+
+def dpxa_weights(tmax, tsum, n_rep: int):
+    """Step 4 (weights): per q-head, tile importance over the query block's total; then the
+    mean over each GQA group's q-heads. Returns [B, Hkv, nb, nb] (zero for j > i)."""
+    B, Hq, nb, _ = tmax.shape
+    M = tmax.max(dim=-1, keepdim=True).values
+    M = torch.where(torch.isfinite(M), M, torch.zeros_like(M))
+    imp = torch.where(torch.isfinite(tmax), torch.exp(tmax - M) * tsum, torch.zeros_like(tsum))
+    tot = imp.sum(-1, keepdim=True)
+    w = torch.where(tot > 0, imp / torch.where(tot > 0, tot, torch.ones_like(tot)), torch.zeros_like(imp))
+    return w.view(B, Hq // n_rep, n_rep, nb, nb).mean(2)
+
+
+def dpxa_select(w, p: float) -> torch.Tensor:
+    """Step 4 (top-p): bool [B, Hkv, nb, nb], causal, the diagonal always selected."""
+    B, Hk, nb, _ = w.shape
+    sel = torch.zeros((B, Hk, nb, nb), dtype=torch.bool)
+    for b in range(B):
+        for h in range(Hk):
+            for i in range(nb):
+                wi = w[b, h, i, : i + 1]
+                order = sorted(range(i + 1), key=lambda j: (-float(wi[j]), j))
+                cum = 0.0
+                for j in order:
+                    sel[b, h, i, j] = True
+                    cum += float(wi[j])
+                    if cum > p:
+                        break
+                sel[b, h, i, i] = True
+    return sel
+
+
+def block_sparse_attention(q, k, v, sel, sm_scale: float, n_rep: int, block: int = 128,
+                           heads: Optional[list] = None, query_blocks: Optional[list] = None):
+    """Step 5: causal attention of each query block against the selected key blocks of its
+    kv-head (``sel`` [B, Hkv, nb, nb]); P is rounded to v's dtype before PV as in the
+    two-phase kernel. Returns q's dtype; heads / query blocks not listed are zero."""
+    B, Hq, N, D = q.shape
+    nb = -(-N // block)
+    dt = _dtype_name(v)
+    rdt = {"fp32": None, "fp16": torch.float16, "bf16": torch.bfloat16}[dt]
+    out = torch.zeros((B, Hq, N, D), dtype=torch.float32)
+    qf, kf, vf = q.float(), k.float(), v.float()
+    heads = list(range(Hq)) if heads is None else list(heads)
+    qbs = list(range(nb)) if query_blocks is None else list(query_blocks)
+    for b in range(B):
+        for h in heads:
+            hk = h // n_rep
+            for i in qbs:
+                m0, m1 = i * block, min(N, (i + 1) * block)
+                blocks = [j for j in range(i + 1) if bool(sel[b, hk, i, j])]
+                cols = torch.cat([torch.arange(j * block, min(N, (j + 1) * block)) for j in blocks])
+                sc = (qf[b, h, m0:m1] @ kf[b, hk, cols].T) * sm_scale
+                rows = torch.arange(m0, m1)
+                sc = torch.where(cols[None, :] <= rows[:, None], sc, torch.tensor(float("-inf")))
+                mx = sc.max(1, keepdim=True).values
+                pr = torch.exp(sc - mx)
+                l = pr.sum(1, keepdim=True)
+                pr = pr if rdt is None else pr.to(rdt).float()
+                out[b, h, m0:m1] = (pr @ vf[b, hk, cols]) / l
+    return out.to(q.dtype)
 
 
 # ---------------------------------------------------------------------------
