@@ -94,13 +94,16 @@ __global__ void __launch_bounds__(DPX_B) dpxa_compact_kernel(const T* __restrict
 }
 
 // ------------------------------------------------------------------ 2-3. scoring
-// One CTA of 128 threads (4 warps) per (query block i, batch * q-head): the query block's
-// anchors stay in shared memory as A fragments in registers (warp w owns row tiles w and w+4),
-// the anchors of key blocks 0..i stream through two shared-memory buffers (cp.async, the next
-// block loading while this one is scored). Per tile each thread folds its scores into a
-// running (max, sum of exp(S - max)); the CTA reduces them and writes tile (i, j).
+// One CTA of 8 warps per (query block i, batch * q-head). The query block's anchors sit in
+// shared memory; warp w scores key blocks w, w+8, ... <= i on its own: it streams the block's
+// anchors through a two-slot ring of 16-row chunks (cp.async, the next chunk loading while
+// this one is multiplied), computes S for every 16-row tile of query anchors against the
+// chunk (mma.sync m16n8k16, fp32), folds the scores into a running (max, sum exp(S - max))
+// and writes tile (i, j) after a warp reduction: no CTA-wide barrier per tile.
+constexpr int DPX_KC = 16;  // key anchors per chunk
+constexpr int DPX_SW = 8;   // warps per scoring CTA
 template <typename T, int D>
-__global__ void __launch_bounds__(128) dpxa_score_kernel(const T* __restrict__ cq, const int32_t* __restrict__ qpos,
+__global__ void __launch_bounds__(DPX_SW * 32) dpxa_score_kernel(const T* __restrict__ cq, const int32_t* __restrict__ qpos,
                                                          const int32_t* __restrict__ qcnt, const T* __restrict__ ck,
                                                          const int32_t* __restrict__ kpos,
                                                          const int32_t* __restrict__ kcnt, float* __restrict__ tmax,
@@ -108,96 +111,111 @@ __global__ void __launch_bounds__(128) dpxa_score_kernel(const T* __restrict__ c
                                                          int nb) {
   constexpr int ROWB = D * 2, SEGS = D / 8;
   extern __shared__ __align__(128) uint8_t dsm[];
-  uint8_t* Qs = dsm;                               // [128][D] swizzled 16-byte segments
-  uint8_t* Ks = dsm + DPX_B * ROWB;                // [2][128][D]
-  int32_t* qp = reinterpret_cast<int32_t*>(Ks + 2 * DPX_B * ROWB);  // [128]
-  int32_t* kp = qp + DPX_B;                        // [2][128]
-  float* red = reinterpret_cast<float*>(kp + 2 * DPX_B);             // [4][2]
+  uint8_t* Qs = dsm;                                             // [128][D] swizzled 16-byte segments
+  int32_t* qp = reinterpret_cast<int32_t*>(Qs + DPX_B * ROWB);   // [128]
+  uint8_t* Kw = reinterpret_cast<uint8_t*>(qp + DPX_B);          // [warps][2 slots][DPX_KC][D]
   const int i = blockIdx.x, bq = blockIdx.y;
   const int b = bq / Hq, h = bq - b * Hq, hk = h / G;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t qslot = static_cast<int64_t>(bq) * nb + i;
   const int64_t kbase = (static_cast<int64_t>(b) * (Hq / G) + hk) * nb;
   const int nq = qcnt[qslot];
-  // anchors of the query block (rows >= nq zero-filled) and of key block 0
-  auto load_rows = [&](uint8_t* dstb, const T* src, int n) {
-    for (int e = tid; e < DPX_B * SEGS; e += 128) {
-      const int r = e / SEGS, sg = e - (e / SEGS) * SEGS;
-      dpx_cp16(smem_u32(dstb + r * ROWB + ((sg ^ (r & 7)) << 4)), src + static_cast<int64_t>(r < n ? r : 0) * D + sg * 8,
-               r < n);
-    }
-  };
-  load_rows(Qs, cq + qslot * DPX_B * D, nq);
-  qp[tid] = qpos[qslot * DPX_B + tid];
-  int nk = kcnt[kbase];
-  load_rows(Ks, ck + kbase * DPX_B * D, nk);
-  kp[tid] = kpos[kbase * DPX_B + tid];
+  const int mtiles = (nq + 15) / 16;
+  for (int e = tid; e < mtiles * 16 * SEGS; e += DPX_SW * 32) {
+    const int r = e / SEGS, sg = e - (e / SEGS) * SEGS;
+    dpx_cp16(smem_u32(Qs + r * ROWB + ((sg ^ (r & 7)) << 4)),
+             cq + (qslot * DPX_B + (r < nq ? r : 0)) * D + sg * 8, r < nq);
+  }
   asm volatile("cp.async.commit_group;" ::: "memory");
+  if (tid < DPX_B) qp[tid] = qpos[qslot * DPX_B + tid];
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-  // A fragments of this warp's two row tiles for every k-step
-  const int mtiles = (nq + 15) / 16;
-  uint32_t af[2][D / 16][4];
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int mt = warp + 4 * u;
-#pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      const int r = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-      const int sg = kk * 2 + (lane >> 4);
-      if (mt < mtiles) dpx_ldsm_x4(af[u][kk], smem_u32(Qs + r * ROWB + ((sg ^ (r & 7)) << 4)));
-    }
-  }
+  uint8_t* kring = Kw + warp * 2 * DPX_KC * ROWB;
   const int g = lane >> 2, c2 = (lane & 3) * 2;
-  for (int j = 0; j <= i; ++j) {
-    const int buf = j & 1;
-    int nk_next = 0;
-    if (j < i) {  // next key block's anchors into the other buffer
-      nk_next = kcnt[kbase + j + 1];
-      load_rows(Ks + (buf ^ 1) * DPX_B * ROWB, ck + (kbase + j + 1) * DPX_B * D, nk_next);
-      kp[(buf ^ 1) * DPX_B + tid] = kpos[(kbase + j + 1) * DPX_B + tid];
-      asm volatile("cp.async.commit_group;" ::: "memory");
+  // the warp's chunk `c` of key block j into ring slot `slot` (rows >= n zero)
+  auto load_chunk = [&](int j, int c, int n, int slot) {
+    const T* src = ck + ((kbase + j) * DPX_B + c * DPX_KC) * D;
+    uint8_t* dst = kring + slot * DPX_KC * ROWB;
+#pragma unroll 4
+    for (int e = lane; e < DPX_KC * SEGS; e += 32) {
+      const int r = e / SEGS, sg = e - (e / SEGS) * SEGS;
+      const bool ok = c * DPX_KC + r < n;
+      dpx_cp16(smem_u32(dst + r * ROWB + ((sg ^ (r & 7)) << 4)), src + static_cast<int64_t>(ok ? r : 0) * D + sg * 8, ok);
     }
-    const uint8_t* Kb = Ks + buf * DPX_B * ROWB;
-    const int32_t* kpb = kp + buf * DPX_B;
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  for (int j = warp; j <= i; j += DPX_SW) {
+    const int nk = kcnt[kbase + j];
+    const int nch = (nk + DPX_KC - 1) / DPX_KC;
+    const int32_t* kpj = kpos + (kbase + j) * DPX_B;
     float m = -INFINITY, sacc = 0.f;
-    const int ntiles = (nk + 7) / 8;
-    for (int nt = 0; nt < ntiles; ++nt) {
-      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if (nch > 0) load_chunk(j, 0, nk, 0);
+    for (int c = 0; c < nch; ++c) {
+      if (c + 1 < nch) {
+        load_chunk(j, c + 1, nk, (c + 1) & 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+      }
+      __syncwarp();
+      const uint8_t* Kb = kring + (c & 1) * DPX_KC * ROWB;
+      const int nt_n = min(DPX_KC, nk - c * DPX_KC);  // valid key rows of the chunk
+      const bool diag = j == i;
+      for (int mt = 0; mt < mtiles; ++mt) {
+        // S of this 16-row query tile against the chunk's four 8-key tiles: four independent
+        // mma chains in flight
+        float acc[DPX_KC / 8][4];
 #pragma unroll
-      for (int kp2 = 0; kp2 < D / 32; ++kp2) {
-        const int r = nt * 8 + (lane & 7);
-        const int sg = 4 * kp2 + (lane >> 3);
-        uint32_t bb[4];
-        dpx_ldsm_x4(bb, smem_u32(Kb + r * ROWB + ((sg ^ (r & 7)) << 4)));
+        for (int nt = 0; nt < DPX_KC / 8; ++nt)
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          if (warp + 4 * u < mtiles) {
-            dpx_mma<T>(acc[u], af[u][2 * kp2], bb[0], bb[1]);
-            dpx_mma<T>(acc[u], af[u][2 * kp2 + 1], bb[2], bb[3]);
+          for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+#pragma unroll
+        for (int kp2 = 0; kp2 < D / 32; ++kp2) {
+          uint32_t a0[4], a1[4];
+          {
+            const int r = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+            const int sg0 = (2 * kp2) * 2 + (lane >> 4), sg1 = (2 * kp2 + 1) * 2 + (lane >> 4);
+            dpx_ldsm_x4(a0, smem_u32(Qs + r * ROWB + ((sg0 ^ (r & 7)) << 4)));
+            dpx_ldsm_x4(a1, smem_u32(Qs + r * ROWB + ((sg1 ^ (r & 7)) << 4)));
+          }
+#pragma unroll
+          for (int nt = 0; nt < DPX_KC / 8; ++nt) {
+            const int r = nt * 8 + (lane & 7);
+            const int sg = 4 * kp2 + (lane >> 3);
+            uint32_t bb[4];
+            dpx_ldsm_x4(bb, smem_u32(Kb + r * ROWB + ((sg ^ (r & 7)) << 4)));
+            dpx_mma<T>(acc[nt], a0, bb[0], bb[1]);
+            dpx_mma<T>(acc[nt], a1, bb[2], bb[3]);
           }
         }
-      }
+        // fold the tile's scores into (m, sum exp(S - m)): one rescale per 8-key tile; masks
+        // only where the tile crosses the anchor counts or the diagonal
+        const bool full_rows = mt * 16 + 16 <= nq;
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int mt = warp + 4 * u;
-        if (mt >= mtiles) continue;
+        for (int nt = 0; nt < DPX_KC / 8; ++nt) {
+          float x[4];
+          const bool full = full_rows && nt * 8 + 8 <= nt_n && !diag;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int row = mt * 16 + g + (e >> 1) * 8, col = nt * 8 + c2 + (e & 1);
-          const bool ok = row < nq && col < nk && (j < i || kpb[col] <= qp[row]);
-          if (!ok) continue;
-          const float x = acc[u][e] * sm_scale;
-          if (x > m) {
-            sacc = sacc * __expf(m - x) + 1.f;
-            m = x;
-          } else {
-            sacc += __expf(x - m);
+          for (int e = 0; e < 4; ++e) {
+            x[e] = acc[nt][e] * sm_scale;
+            if (!full) {
+              const int row = mt * 16 + g + (e >> 1) * 8, col = nt * 8 + c2 + (e & 1);
+              bool ok = row < nq && col < nt_n;
+              if (ok && diag) ok = kpj[c * DPX_KC + col] <= qp[row];
+              if (!ok) x[e] = -INFINITY;
+            }
           }
+          const float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+          if (mx > m) {
+            sacc *= __expf(m - mx);
+            m = mx;
+          }
+          if (m != -INFINITY)
+            sacc += (__expf(x[0] - m) + __expf(x[1] - m)) + (__expf(x[2] - m) + __expf(x[3] - m));
         }
       }
+      __syncwarp();  // every lane is done with this slot before it is refilled
     }
-    // (max, sum) over the CTA
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
       const float m2 = __shfl_xor_sync(0xFFFFFFFFu, m, o), s2 = __shfl_xor_sync(0xFFFFFFFFu, sacc, o);
@@ -206,24 +224,9 @@ __global__ void __launch_bounds__(128) dpxa_score_kernel(const T* __restrict__ c
       m = mm;
     }
     if (lane == 0) {
-      red[warp * 2] = m;
-      red[warp * 2 + 1] = sacc;
+      tmax[qslot * nb + j] = m;
+      tsum[qslot * nb + j] = sacc;
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-    if (tid == 0) {
-      float M = red[0], S = red[1];
-      for (int w = 1; w < 4; ++w) {
-        const float m2 = red[w * 2], s2 = red[w * 2 + 1];
-        const float mm = fmaxf(M, m2);
-        S = (mm == -INFINITY) ? 0.f : S * __expf(M - mm) + s2 * __expf(m2 - mm);
-        M = mm;
-      }
-      tmax[qslot * nb + j] = M;
-      tsum[qslot * nb + j] = S;
-    }
-    nk = nk_next;
-    __syncthreads();
   }
 }
 
@@ -346,11 +349,11 @@ template <typename T, int D>
 static cudaError_t launch_score_t(const void* cq, const int32_t* qpos, const int32_t* qcnt, const void* ck,
                                   const int32_t* kpos, const int32_t* kcnt, float* tmax, float* tsum, float sm_scale,
                                   int B, int Hq, int G, int nb, cudaStream_t st) {
-  const int smem = 3 * DPX_B * D * 2 + 3 * DPX_B * 4 + 64;
+  const int smem = DPX_B * D * 2 + DPX_B * 4 + DPX_SW * 2 * DPX_KC * D * 2;
   auto kfn = dpxa_score_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  kfn<<<dim3(static_cast<unsigned>(nb), static_cast<unsigned>(B * Hq)), 128, smem, st>>>(
+  kfn<<<dim3(static_cast<unsigned>(nb), static_cast<unsigned>(B * Hq)), DPX_SW * 32, smem, st>>>(
       static_cast<const T*>(cq), qpos, qcnt, static_cast<const T*>(ck), kpos, kcnt, tmax, tsum, sm_scale, Hq, G, nb);
   return cudaGetLastError();
 }
