@@ -638,7 +638,7 @@ struct PackHdr {
   int err;  // first word: the error word dab_workspace_error reads
   unsigned ticket, done, epoch;
 };
-enum : int { ERR_PACK_LOOKBACK = 0x201 };
+enum : int { ERR_PACK_LOOKBACK = 0x401 };  // a predecessor tile never published its count
 
 __device__ __forceinline__ uint64_t pk_ld(const uint64_t* p) {
   uint64_t v;
