@@ -309,7 +309,12 @@ struct TileSeqT {
       }
       state = 2;
       return false;
+    } else {
+      return next_hybrid(p, U, t);
     }
+  }
+
+  __device__ __forceinline__ bool next_hybrid(const TcParams& p, const Unit& U, TileInfo& t) {
     while (state == 0) {
       if (cur >= pmax) { state = 1; cur = dlo; break; }
       const int j = cur++;
@@ -884,10 +889,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         // from that chunk. P of keys 0..63 (chunks 0 and 1) is released to the MMA warp (p_lo)
         // only after chunks 2 and 3 have passed the same check, so released P is final.
         // (KEYED: per-key weights are fine too)
-        const bool fast = BF16 && (KEYED || !perkey) && !any_mask;
+        // a tile masked only by a per-row key limit (the causal diagonal, the end of the keys, the
+        // packed tail) also takes the fast path: its masked S entries are overwritten with -inf in
+        // TMEM first, so the unmodified streaming code gives them probability 0
+        const bool lim_mask = any_mask && p.variant != TC_PURE;
+        const bool fast = BF16 && (KEYED || !perkey) && (!any_mask || lim_mask);
         if (!warp_wait(s_full + x, s_par, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
         s_par ^= 1;
         tc_fence_after();
+        if (fast && lim_mask) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            if (!__any_sync(0xFFFFFFFFu, lim < c * 32 + 32)) continue;  // no masked column in chunk c
+            uint32_t sc[32];
+            tmem_ld32(tS + c * 32, sc);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) sc[e] = (c * 32 + e < lim) ? sc[e] : NEG_INF;
+            tmem_st32(tS + c * 32, sc);
+          }
+          tmem_st_wait();
+        }
         int stop = 0;  // first chunk the fast path did not finish
         bool lo_sent = false;  // p_lo arrived (P of keys 0..63 final)
         if (fast) {
