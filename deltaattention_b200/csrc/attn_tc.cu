@@ -44,7 +44,9 @@ template <int D> struct TcCfg {
   static constexpr int OFF_AUXC = OFF_V + NV * KVBYTES;
   static constexpr int OFF_AUXT = OFF_AUXC + NV * TC_BN * 4;
   static constexpr int OFF_ONES = OFF_AUXT + NV * TC_BN * 4;  // 128 unit weights (dense blocks, KEYED)
-  static constexpr int OFF_BAR = OFF_ONES + TC_BN * 4;
+  static constexpr int OFF_EPI = OFF_ONES + TC_BN * 4;  // per softmax warp: 32 rows x 80 B of output staging
+  static constexpr int EPI_PITCH = 80;                  // 64 B of a 32-column chunk + 16 B (no bank conflicts)
+  static constexpr int OFF_BAR = OFF_EPI + 8 * 32 * EPI_PITCH;
   static constexpr int NBAR = 2 + 2 * NK + 2 * NV + 2 * 6 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 64 + 1024;  // + alignment slack
@@ -1049,7 +1051,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
       if (!warp_wait(o_full + x, o_par, ab, ERR_TIMEOUT_EPILOGUE)) break;
       o_par ^= 1;
       tc_fence_after();
-      if (o_has) {
+      if (o_has && p.out_vec_ok) {
+        // each 32-column chunk goes through the warp's staging rows, so a 16-byte store
+        // instruction covers 8 rows x 64 B (8 lines) instead of 32 rows x 16 B (32 lines)
+        uint8_t* stg = smem + C::OFF_EPI + (warp - 4) * 32 * C::EPI_PITCH;
+        const int rr = lane >> 2, seg = lane & 3;  // the row / 16-byte piece this lane stores
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t ob[32];
+          tmem_ld32(tO + c * 32, ob);
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            uint4 w;
+            w.x = pack2(__uint_as_float(ob[j]) * inv, __uint_as_float(ob[j + 1]) * inv, BF16);
+            w.y = pack2(__uint_as_float(ob[j + 2]) * inv, __uint_as_float(ob[j + 3]) * inv, BF16);
+            w.z = pack2(__uint_as_float(ob[j + 4]) * inv, __uint_as_float(ob[j + 5]) * inv, BF16);
+            w.w = pack2(__uint_as_float(ob[j + 6]) * inv, __uint_as_float(ob[j + 7]) * inv, BF16);
+            *reinterpret_cast<uint4*>(stg + lane * C::EPI_PITCH + j * 2) = w;
+          }
+          __syncwarp();
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int lr = q4 * 8 + rr;  // lane (row) of the warp whose piece this is
+            const uint4 w = *reinterpret_cast<const uint4*>(stg + lr * C::EPI_PITCH + seg * 16);
+            if (row - lane + lr < p.seq_q)
+              *reinterpret_cast<uint4*>(orow + static_cast<int64_t>(lr - lane) * p.os_m + c * 32 + seg * 8) = w;
+          }
+          __syncwarp();
+        }
+      } else if (o_has) {
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t ob[32];
