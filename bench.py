@@ -642,21 +642,26 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm), "source": src}
 
 
+SUSTAINED_S = 4.0  # length of the back-to-back GEMM loop behind the sustained bf16 figure
+
+
 def pick_peak(clocks, timed_s):
-    """The roofline denominator for the attention launch: the burst bf16 figure when the timed
-    region ran at (>= 95% of) the maximum SM clock, or was too short to sample and under a second
-    (the burst figure is measured at that clock), else the sustained power-capped figure."""
+    """The roofline denominator for the attention launch: the burst bf16 figure unless the timed
+    region was at least as long as the loop the sustained figure was measured over and ran below
+    95% of the maximum SM clock; then the sustained power-capped figure. (The sustained figure's
+    GEMM loop settles at a lower clock than a shorter region reaches, so against a short region
+    it would overstate the fraction.)"""
     burst, sustained, src = peaks()
     sm, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
     if sm and mx:
-        at_max = sm >= 0.95 * mx
+        below_max = sm < 0.95 * mx
         why = f"median SM clock {sm:.0f} of max {mx:.0f} MHz over the timed region ({timed_s * 1e3:.0f} ms)"
     else:
-        at_max = timed_s < 1.0
+        below_max = False
         why = f"no clock samples; timed region {timed_s * 1e3:.0f} ms"
-    if at_max:
-        return burst, f"{src} bf16 burst ({why}); sustained {sustained}", sustained
-    return sustained, f"{src} bf16 sustained ({why}); burst {burst}", burst
+    if below_max and timed_s >= SUSTAINED_S:
+        return sustained, f"{src} bf16 sustained ({why}); burst {burst}", burst
+    return burst, f"{src} bf16 burst ({why}); sustained {sustained}", sustained
 
 
 def dist_setup():
