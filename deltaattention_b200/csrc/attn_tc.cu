@@ -780,6 +780,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         // 32-column chunk, built before S is read
         uint32_t vm[4] = {~0u, ~0u, ~0u, ~0u};
         if (p.variant == TC_PURE) {
+          const int nval = packed_len(p) - n0;  // keys of this block below the packed length
 #pragma unroll 1
           for (int w = 0; w < 4; ++w) {
             uint32_t bits = 0;
@@ -787,7 +788,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             for (int e = 0; e < 32; ++e) {
               const int j = w * 32 + e;
               const float cj = cint ? static_cast<float>(static_cast<int32_t>(cnt[j])) : __uint_as_float(cnt[j]);
-              const bool v = (n0 + j < packed_len(p)) && cj > 0.f && tsv[j] <= row;
+              const bool v = (j < nval) && cj > 0.f && tsv[j] <= row;
               bits |= (v ? 1u : 0u) << e;
             }
             if (w == 0) vm[0] = bits; else if (w == 1) vm[1] = bits; else if (w == 2) vm[2] = bits; else vm[3] = bits;
