@@ -779,8 +779,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         // pure-phase-1 validity (count > 0, index < num_packed, timestamp <= row): 32 bits per
         // 32-column chunk, built before S is read
         uint32_t vm[4] = {~0u, ~0u, ~0u, ~0u};
+        int lim = TC_BN;
+        bool pure_prefix = false;  // pure phase 1 with a per-row prefix mask (below)
         if (p.variant == TC_PURE) {
           const int nval = packed_len(p) - n0;  // keys of this block below the packed length
+          // Packed keys keep sequence order, so their timestamps ascend. When they do in this
+          // block and every count below the packed length is positive, a row's valid keys are
+          // the prefix with timestamp <= row: a per-row limit, which the streaming path handles.
+          {
+            const int j0 = 4 * lane;
+            const int4 tv = *reinterpret_cast<const int4*>(tsv + j0);
+            const uint4 cv = *reinterpret_cast<const uint4*>(cnt + j0);
+            const int tn = __shfl_down_sync(0xFFFFFFFFu, tv.x, 1);  // the next lane's first key
+            const int tt[4] = {tv.x, tv.y, tv.z, tv.w};
+            const uint32_t cc[4] = {cv.x, cv.y, cv.z, cv.w};
+            bool okp = true;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int j = j0 + e;
+              const float cj = cint ? static_cast<float>(static_cast<int32_t>(cc[e])) : __uint_as_float(cc[e]);
+              const int tnext = e < 3 ? tt[e + 1] : tn;
+              if (j < nval && !(cj > 0.f)) okp = false;
+              if (j + 1 < nval && j + 1 < TC_BN && tnext < tt[e]) okp = false;
+            }
+            pure_prefix = __all_sync(0xFFFFFFFFu, okp);
+          }
+          if (pure_prefix) {
+            // keys with timestamp <= row among the first nval (a search over the sorted prefix)
+            const int nv = max(0, min(nval, TC_BN));
+            int pos = 0;
+#pragma unroll
+            for (int step = TC_BN; step > 0; step >>= 1)
+              if (pos + step <= nv && tsv[pos + step - 1] <= row) pos += step;
+            lim = pos;
+          }
+        }
+        if (p.variant == TC_PURE && !pure_prefix) {
+          const int nval = packed_len(p) - n0;
 #pragma unroll 1
           for (int w = 0; w < 4; ++w) {
             uint32_t bits = 0;
@@ -794,7 +829,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
             if (w == 0) vm[0] = bits; else if (w == 1) vm[1] = bits; else if (w == 2) vm[2] = bits; else vm[3] = bits;
           }
         }
-        int lim = TC_BN;
         if (p.variant != TC_PURE) {
           if (t.packed) {
             lim = packed_len(p) - n0;
@@ -804,7 +838,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
           }
         }
         // S chunk c (columns 32c..32c+31) with masked columns set to -inf
-        const bool any_mask = __any_sync(0xFFFFFFFFu, (p.variant == TC_PURE) || lim < TC_BN);
+        const bool any_mask = __any_sync(0xFFFFFFFFu, (p.variant == TC_PURE && !pure_prefix) || lim < TC_BN);
         auto load_chunk = [&](int c, uint32_t* sc) {
           tmem_ld32(tS + c * 32, sc);
           if (any_mask) {
@@ -895,7 +929,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         // a tile masked only by a per-row key limit (the causal diagonal, the end of the keys, the
         // packed tail) also takes the fast path: its masked S entries are overwritten with -inf in
         // TMEM first, so the unmodified streaming code gives them probability 0
-        const bool lim_mask = any_mask && p.variant != TC_PURE;
+        const bool lim_mask = any_mask && (p.variant != TC_PURE || pure_prefix);
         const bool fast = BF16 && (KEYED || !perkey) && (!any_mask || lim_mask);
         if (!warp_wait(s_full + x, s_par, ab, ERR_TIMEOUT_SOFTMAX)) { ok = false; break; }
         s_par ^= 1;

@@ -407,6 +407,33 @@ def test_tcgen05_vs_simt_and_oracle(variant, dt, D):
     _check_ws_clean()
 
 
+@pytest.mark.parametrize("disorder", ["sorted", "permuted", "zero_count"])
+def test_pure_phase1_prefix_and_general_masks(disorder):
+    """Pure phase 1 (bf16): a packed block whose timestamps ascend and whose counts are positive
+    takes a per-row prefix mask on the streaming path; a block with keys out of timestamp order
+    (the packed rows permuted inside their 128-key block, K / V / timestamps / counts together)
+    or a zero count below the packed length takes the general per-key mask. Each against the
+    oracle on the same packed tensors, which does not depend on the key order."""
+    dt, H, N, D = torch.bfloat16, 2, 1500, 128
+    q, k, v = I.attn_inputs(1, H, N, D, dt, 61)
+    keep = O.periodic_keep_mask(1, H, N, 0.25)
+    _, kp, vp, ts, counts = O.pack_from_keep(k, v, keep)
+    counts = counts.float()
+    if disorder == "permuted":
+        g = torch.Generator().manual_seed(5)
+        M = kp.shape[2]
+        perm = torch.cat([b0 + torch.randperm(min(128, M - b0), generator=g) for b0 in range(0, M, 128)])
+        kp, vp, ts, counts = kp[:, :, perm], vp[:, :, perm], ts[:, :, perm], counts[:, :, perm]
+    elif disorder == "zero_count":
+        counts[:, :, 5] = 0.0
+        counts[:, :, 200] = 0.0
+    ref = O.hybrid_attention(q, k, v, kp, vp, ts, counts, D ** -0.5, 128, "pure_phase1")
+    c = lambda t: t.cuda().contiguous()  # noqa: E731
+    out = _launch_variant("pure_phase1", c(q), c(k), c(v), c(kp), c(vp), c(ts), c(counts), 128)
+    _cmp(out, ref, dt, f"pure/{disorder}")
+    _check_ws_clean()
+
+
 @pytest.mark.parametrize("variant", ["hybrid", "sanity", "pure_phase1"])
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
 def test_tcgen05_score_jumps(variant, dt):
