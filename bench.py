@@ -9,7 +9,8 @@ On N GPUs (torchrun, one rank per GPU) the one sequence is partitioned by kv-hea
 query heads over the whole sequence, with no collective on the data path (strong scaling:
 the job's work is fixed). ``--shard seq`` instead gives every rank a sequence of its own
 (weak scaling). Per-GPU inputs larger than the 126 MB L2 need no flush between steps;
-smaller ones (4 and 8 GPUs) get a 256 MiB L2 flush between steps, outside the timed events.
+smaller ones (4 and 8 GPUs) get an L2 flush between steps (256 MiB written, then 256 MiB read,
+so no dirty flush lines are left for the step to write back), outside the timed events.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--shard heads|seq]
 
@@ -50,8 +51,8 @@ def workload_config(n_gpus, shard="heads", flushed=False):
     return {"workload": "cfg2: RoPE(q,k) + periodic r=4 packing + two-phase delta attention, one layer",
             "B": CFG["B"], "Hq": CFG["Hq"], "Hkv": CFG["Hkv"], "N": CFG["N"], "d": CFG["D"],
             "r": CFG["r"], "dense_window": CFG["W"], "global_batch": gb, "parallelism": par,
-            "l2": ("per-GPU inputs smaller than 1.5x L2: 256 MiB L2 flush between timed steps (outside the "
-                   "per-step events)") if flushed else "per-GPU inputs larger than L2; no flush"}
+            "l2": ("per-GPU inputs smaller than 1.5x L2: L2 flushed between timed steps, 256 MiB written then "
+                   "256 MiB read (outside the per-step events)") if flushed else "per-GPU inputs larger than L2; no flush"}
 
 
 def peaks():
@@ -71,6 +72,22 @@ def hbm_peak():
         return 6650.0, "fallback"
 
 
+class L2Flush:
+    """Evicts L2 between timed launches: writes a 256 MiB buffer (twice the 126 MB L2), then
+    reads another 256 MiB buffer, so L2 ends up holding clean lines of the read buffer. After a
+    write alone L2 would be full of the flush's dirty lines, and the timed kernel would pay for
+    writing them back to HBM as its own reads evict them (~126 MB of extra traffic)."""
+
+    def __init__(self, dev):
+        self.w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        self.r = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+        self.out = torch.empty((), dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.w.fill_(1)
+        torch.sum(self.r, dim=0, out=self.out)
+
+
 def hbm_kernels(dev, seed):
     """HBM-bound kernels of the path, each launch timed alone with L2 flushed before it.
 
@@ -82,13 +99,13 @@ def hbm_kernels(dev, seed):
     from deltaattention_b200 import ops, synth
     from deltaattention_b200.launch import fused_hybrid_decode_kernel, fused_hybrid_decode_update_kernel
     peak, _ = hbm_peak()
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     stream = torch.cuda.current_stream(dev)
 
     def timed(fn, reps=10):
         ts = []
         for _ in range(reps + 2):
-            flush.fill_(1)
+            flush()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             fn()
@@ -816,7 +833,7 @@ def _timed_steps(step, steps, stream, flush=None):
         return t0.elapsed_time(t1)
     evs = []
     for _ in range(steps):
-        flush.fill_(1)
+        flush()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         step(True)
@@ -851,7 +868,7 @@ def run_ours(args, world, rank, local):
         tokens = B * N * world
     my_hq, my_hkv = q.shape[1], k.shape[1]
     in_bytes = (q.numel() + k.numel() + v.numel()) * 2
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if in_bytes < 1.5 * L2_BYTES else None
+    flush = L2Flush(dev) if in_bytes < 1.5 * L2_BYTES else None
     period = r
     stream = torch.cuda.current_stream(dev)
     attn_events = []
