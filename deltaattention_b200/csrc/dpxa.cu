@@ -98,8 +98,10 @@ __global__ void __launch_bounds__(DPX_B) dpxa_compact_kernel(const T* __restrict
 // shared memory; warp w scores key blocks w, w+8, ... <= i on its own: it streams the block's
 // anchors through a two-slot ring of 16-row chunks (cp.async, the next chunk loading while
 // this one is multiplied), computes S for every 16-row tile of query anchors against the
-// chunk (mma.sync m16n8k16, fp32), folds the scores into a running (max, sum exp(S - max))
-// and writes tile (i, j) after a warp reduction: no CTA-wide barrier per tile.
+// chunk (mma.sync m16n8k16, fp32; the chunk's key fragments held in registers and two query
+// tiles multiplied per pass, four accumulator chains in flight), folds the scores into a
+// running (max, sum exp(S - max)) and writes tile (i, j) after a warp reduction: no CTA-wide
+// barrier per tile.
 constexpr int DPX_KC = 16;  // key anchors per chunk
 constexpr int DPX_SW = 8;   // warps per scoring CTA
 template <typename T, int D>
@@ -161,57 +163,73 @@ __global__ void __launch_bounds__(DPX_SW * 32) dpxa_score_kernel(const T* __rest
       const uint8_t* Kb = kring + (c & 1) * DPX_KC * ROWB;
       const int nt_n = min(DPX_KC, nk - c * DPX_KC);  // valid key rows of the chunk
       const bool diag = j == i;
-      for (int mt = 0; mt < mtiles; ++mt) {
-        // S of this 16-row query tile against the chunk's four 8-key tiles: four independent
-        // mma chains in flight
-        float acc[DPX_KC / 8][4];
+      // the chunk's B fragments (16 keys x D) in registers once, reused by every query tile
+      uint32_t bf[D / 32][DPX_KC / 8][4];
 #pragma unroll
-        for (int nt = 0; nt < DPX_KC / 8; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-#pragma unroll
-        for (int kp2 = 0; kp2 < D / 32; ++kp2) {
-          uint32_t a0[4], a1[4];
-          {
-            const int r = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-            const int sg0 = (2 * kp2) * 2 + (lane >> 4), sg1 = (2 * kp2 + 1) * 2 + (lane >> 4);
-            dpx_ldsm_x4(a0, smem_u32(Qs + r * ROWB + ((sg0 ^ (r & 7)) << 4)));
-            dpx_ldsm_x4(a1, smem_u32(Qs + r * ROWB + ((sg1 ^ (r & 7)) << 4)));
-          }
-#pragma unroll
-          for (int nt = 0; nt < DPX_KC / 8; ++nt) {
-            const int r = nt * 8 + (lane & 7);
-            const int sg = 4 * kp2 + (lane >> 3);
-            uint32_t bb[4];
-            dpx_ldsm_x4(bb, smem_u32(Kb + r * ROWB + ((sg ^ (r & 7)) << 4)));
-            dpx_mma<T>(acc[nt], a0, bb[0], bb[1]);
-            dpx_mma<T>(acc[nt], a1, bb[2], bb[3]);
-          }
-        }
-        // fold the tile's scores into (m, sum exp(S - m)): one rescale per 8-key tile; masks
-        // only where the tile crosses the anchor counts or the diagonal
-        const bool full_rows = mt * 16 + 16 <= nq;
+      for (int kp2 = 0; kp2 < D / 32; ++kp2)
 #pragma unroll
         for (int nt = 0; nt < DPX_KC / 8; ++nt) {
-          float x[4];
-          const bool full = full_rows && nt * 8 + 8 <= nt_n && !diag;
+          const int r = nt * 8 + (lane & 7);
+          const int sg = 4 * kp2 + (lane >> 3);
+          dpx_ldsm_x4(bf[kp2][nt], smem_u32(Kb + r * ROWB + ((sg ^ (r & 7)) << 4)));
+        }
+      for (int mt0 = 0; mt0 < mtiles; mt0 += 2) {
+        // S of two 16-row query tiles against the chunk's two 8-key tiles: four independent
+        // mma chains in flight (the second tile only when it exists; warp-uniform)
+        const bool two = mt0 + 1 < mtiles;
+        float acc[2][DPX_KC / 8][4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            x[e] = acc[nt][e] * sm_scale;
-            if (!full) {
-              const int row = mt * 16 + g + (e >> 1) * 8, col = nt * 8 + c2 + (e & 1);
-              bool ok = row < nq && col < nt_n;
-              if (ok && diag) ok = kpj[c * DPX_KC + col] <= qp[row];
-              if (!ok) x[e] = -INFINITY;
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int nt = 0; nt < DPX_KC / 8; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[t][nt][e] = 0.f;
+#pragma unroll
+        for (int kp2 = 0; kp2 < D / 32; ++kp2) {
+          const int sg0 = (2 * kp2) * 2 + (lane >> 4), sg1 = (2 * kp2 + 1) * 2 + (lane >> 4);
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (t == 1 && !two) continue;
+            uint32_t a0[4], a1[4];
+            const int r = (mt0 + t) * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+            dpx_ldsm_x4(a0, smem_u32(Qs + r * ROWB + ((sg0 ^ (r & 7)) << 4)));
+            dpx_ldsm_x4(a1, smem_u32(Qs + r * ROWB + ((sg1 ^ (r & 7)) << 4)));
+#pragma unroll
+            for (int nt = 0; nt < DPX_KC / 8; ++nt) {
+              dpx_mma<T>(acc[t][nt], a0, bf[kp2][nt][0], bf[kp2][nt][1]);
+              dpx_mma<T>(acc[t][nt], a1, bf[kp2][nt][2], bf[kp2][nt][3]);
             }
           }
-          const float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-          if (mx > m) {
-            sacc *= __expf(m - mx);
-            m = mx;
+        }
+        // fold the tiles' scores into (m, sum exp(S - m)): one rescale per 8-key tile; masks
+        // only where a tile crosses the anchor counts or the diagonal
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (t == 1 && !two) continue;
+          const int mt = mt0 + t;
+          const bool full_rows = mt * 16 + 16 <= nq;
+#pragma unroll
+          for (int nt = 0; nt < DPX_KC / 8; ++nt) {
+            float x[4];
+            const bool full = full_rows && nt * 8 + 8 <= nt_n && !diag;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              x[e] = acc[t][nt][e] * sm_scale;
+              if (!full) {
+                const int row = mt * 16 + g + (e >> 1) * 8, col = nt * 8 + c2 + (e & 1);
+                bool ok = row < nq && col < nt_n;
+                if (ok && diag) ok = kpj[c * DPX_KC + col] <= qp[row];
+                if (!ok) x[e] = -INFINITY;
+              }
+            }
+            const float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+            if (mx > m) {
+              sacc *= __expf(m - mx);
+              m = mx;
+            }
+            if (m != -INFINITY)
+              sacc += (__expf(x[0] - m) + __expf(x[1] - m)) + (__expf(x[2] - m) + __expf(x[3] - m));
           }
-          if (m != -INFINITY)
-            sacc += (__expf(x[0] - m) + __expf(x[1] - m)) + (__expf(x[2] - m) + __expf(x[3] - m));
         }
       }
       __syncwarp();  // every lane is done with this slot before it is refilled
