@@ -134,6 +134,7 @@ __global__ void __launch_bounds__(DPX_SW * 32) dpxa_score_kernel(const T* __rest
   __syncthreads();
   uint8_t* kring = Kw + warp * 2 * DPX_KC * ROWB;
   const int g = lane >> 2, c2 = (lane & 3) * 2;
+  const float sl2 = sm_scale * 1.4426950408889634f;  // scores in log2 units
   // the warp's chunk `c` of key block j into ring slot `slot` (rows >= n zero)
   auto load_chunk = [&](int j, int c, int n, int slot) {
     const T* src = ck + ((kbase + j) * DPX_B + c * DPX_KC) * D;
@@ -201,8 +202,9 @@ __global__ void __launch_bounds__(DPX_SW * 32) dpxa_score_kernel(const T* __rest
             }
           }
         }
-        // fold the tiles' scores into (m, sum exp(S - m)): one rescale per 8-key tile; masks
-        // only where a tile crosses the anchor counts or the diagonal
+        // fold the tiles' scores into (m, sum 2^(S' - m)), S' = S * scale * log2(e): the maximum
+        // is taken on the raw accumulators and scaled once, each probability is one FMA and one
+        // ex2; masks only where a tile crosses the anchor counts or the diagonal
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (t == 1 && !two) continue;
@@ -211,24 +213,26 @@ __global__ void __launch_bounds__(DPX_SW * 32) dpxa_score_kernel(const T* __rest
 #pragma unroll
           for (int nt = 0; nt < DPX_KC / 8; ++nt) {
             float x[4];
-            const bool full = full_rows && nt * 8 + 8 <= nt_n && !diag;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              x[e] = acc[t][nt][e] * sm_scale;
-              if (!full) {
+            for (int e = 0; e < 4; ++e) x[e] = acc[t][nt][e];
+            const bool full = full_rows && nt * 8 + 8 <= nt_n && !diag;
+            if (!full) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
                 const int row = mt * 16 + g + (e >> 1) * 8, col = nt * 8 + c2 + (e & 1);
                 bool ok = row < nq && col < nt_n;
                 if (ok && diag) ok = kpj[c * DPX_KC + col] <= qp[row];
                 if (!ok) x[e] = -INFINITY;
               }
             }
-            const float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+            const float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])) * sl2;
             if (mx > m) {
-              sacc *= __expf(m - mx);
+              sacc *= ex2(m - mx);
               m = mx;
             }
             if (m != -INFINITY)
-              sacc += (__expf(x[0] - m) + __expf(x[1] - m)) + (__expf(x[2] - m) + __expf(x[3] - m));
+              sacc += (ex2(fmaf(x[0], sl2, -m)) + ex2(fmaf(x[1], sl2, -m))) +
+                      (ex2(fmaf(x[2], sl2, -m)) + ex2(fmaf(x[3], sl2, -m)));
           }
         }
       }
@@ -238,11 +242,11 @@ __global__ void __launch_bounds__(DPX_SW * 32) dpxa_score_kernel(const T* __rest
     for (int o = 16; o; o >>= 1) {
       const float m2 = __shfl_xor_sync(0xFFFFFFFFu, m, o), s2 = __shfl_xor_sync(0xFFFFFFFFu, sacc, o);
       const float mm = fmaxf(m, m2);
-      sacc = (mm == -INFINITY) ? 0.f : sacc * __expf(m - mm) + s2 * __expf(m2 - mm);
+      sacc = (mm == -INFINITY) ? 0.f : sacc * ex2(m - mm) + s2 * ex2(m2 - mm);
       m = mm;
     }
     if (lane == 0) {
-      tmax[qslot * nb + j] = m;
+      tmax[qslot * nb + j] = m * 0.6931471805599453f;  // back to natural-log units
       tsum[qslot * nb + j] = sacc;
     }
   }
