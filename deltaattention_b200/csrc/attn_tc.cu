@@ -781,11 +781,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_tc_kernel(const __grid_con
         uint32_t vm[4] = {~0u, ~0u, ~0u, ~0u};
         int lim = TC_BN;
         bool pure_prefix = false;  // pure phase 1 with a per-row prefix mask (below)
-        if (p.variant == TC_PURE) {
+        if (!KEYED && p.variant == TC_PURE) {
           const int nval = packed_len(p) - n0;  // keys of this block below the packed length
           // Packed keys keep sequence order, so their timestamps ascend. When they do in this
           // block and every count below the packed length is positive, a row's valid keys are
           // the prefix with timestamp <= row: a per-row limit, which the streaming path handles.
+          // (Not compiled into the KEYED kernels: the extra code slowed their streaming path;
+          // pure phase 1 on device-packed histories keeps the general mask.)
           {
             const int j0 = 4 * lane;
             const int4 tv = *reinterpret_cast<const int4*>(tsv + j0);
