@@ -1085,6 +1085,8 @@ def main():
                     help="time the hot-path step only (no comparator, e2e or CPU legs); for profiling")
     ap.add_argument("--only-hbm", action="store_true",
                     help="run the HBM-bound kernel measurements alone and print them; for profiling")
+    ap.add_argument("--only-dpxa", action="store_true",
+                    help="run the DPXA selection + block-sparse attention measurement alone (honours --n)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.n:
@@ -1095,6 +1097,9 @@ def main():
         run_reference(args, world, rank)
         return
     world, rank, local = dist_setup()
+    if args.only_dpxa:
+        print(json.dumps(dpxa_bench(torch.device("cuda", local), 7000 + rank)), flush=True)
+        return
     if args.only_hbm:
         dev = torch.device("cuda", local)
         print(json.dumps({**hbm_kernels(dev, 2000 + rank), "decode_step": decode_step(dev, 4000 + rank),
